@@ -1,0 +1,222 @@
+/*
+ * qxcuda.h — C ABI of libqxcuda, the B200 (sm_100a) implementation of qx's
+ * grouped-query-attention hot path: RoPE, bounded KV-cache append, split-KV
+ * flash decode with a log-sum-exp combine, causal prefill, and the partial
+ * (m, l, O) exchange format for a KV cache split across GPUs.
+ *
+ * Plain C types only: device pointers are `void*`, sizes are integers,
+ * errors are status codes plus a per-context message. A Rust `qx-cuda`
+ * crate binds these symbols one-to-one.
+ *
+ * Reference interfaces replaced (paths within blasrodri/qx):
+ *   crates/qx-runtime/src/lib.rs:350-432     KvCache (new/len/is_empty/reset/append)
+ *   crates/qx-runtime/src/lib.rs:434-442     apply_granite_rope
+ *   crates/qx-runtime/src/lib.rs:444-452     granite_attention_decode
+ *   crates/qx-runtime-v2/src/lib.rs:6566-6636 ExecutionPlan KV byte plan
+ *   crates/qx-runtime-v2/src/lib.rs:6837-6860 GpuRuntimeBuffers::kv_key_buffer/kv_value_buffer
+ *   crates/qx-runtime-v2/src/lib.rs:6863-6968 encode_attention_layer[_with_plan] (RoPE/KV + attention stage)
+ *   crates/qx-runtime-v2/src/lib.rs:1793-1821 PreparedAttentionStack::encode (24-layer stack)
+ *   crates/qx-runtime-v2/src/lib.rs:3265-3310 checkpoint_kv / rollback_kv / commit_kv
+ *   crates/qx-runtime-v2/src/lib.rs:904-1024  Qwen attention stage (qk-norm RoPE, store KV, GQA)
+ *   crates/qx-metal/src/lib.rs:14488         MetalContext::run_qwen_gqa_attention
+ *   crates/qx-metal/src/lib.rs:9404-9440     DecodeGraph::finish (errors surface at wait)
+ *
+ * Threading: one qxc_ctx per host thread (like the reference's DecodeGraph,
+ * which is not Send). Calls that take device pointers are asynchronous on the
+ * context's stream; qxc_sync waits and reports device-side errors. Calls that
+ * take host pointers are synchronous.
+ */
+#ifndef QXCUDA_H
+#define QXCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QXC_ABI_VERSION 1
+
+typedef enum qxc_status {
+  QXC_OK = 0,
+  QXC_ERR_INVALID_ARG = 1,   /* shape, size, dtype or null pointer */
+  QXC_ERR_POSITION = 2,      /* non-sequential or >= capacity (qx-runtime lib.rs:385-398) */
+  QXC_ERR_NONFINITE = 3,     /* non-finite RoPE input/output or softmax (the reference panics) */
+  QXC_ERR_CUDA = 4,
+  QXC_ERR_NCCL = 5,
+  QXC_ERR_TIMEOUT = 6,       /* a bounded device-side wait gave up */
+  QXC_ERR_UNSUPPORTED = 7,
+  QXC_ERR_OUT_OF_MEMORY = 8
+} qxc_status;
+
+typedef enum qxc_model {
+  QXC_MODEL_GRANITE = 0, /* 16 q heads, 8 kv heads, head_dim 64, scale 1/64, pinned RoPE theta 1e4 */
+  QXC_MODEL_QWEN3 = 1    /* 32 q heads, 4 kv heads, head_dim 128, scale 1/sqrt(128), QK-RMSNorm, RoPE theta 1e6 */
+} qxc_model;
+
+typedef enum qxc_dtype { QXC_F32 = 0, QXC_BF16 = 1, QXC_F16 = 2 } qxc_dtype;
+
+/* Decode flags. */
+#define QXC_DECODE_NO_ADVANCE 0x1 /* do not advance the cursor (caller advances after the last layer) */
+#define QXC_DECODE_NATIVE_EXP 0x2 /* hardware exp2 instead of qx's pinned exp_f32 (Granite) */
+#define QXC_DECODE_PINNED_EXP 0x4 /* qx's pinned exp_f32 (default for Granite; Qwen defaults to native) */
+
+typedef struct qxc_ctx qxc_ctx;
+typedef struct qxc_kv qxc_kv;
+
+/* ---- library / context ------------------------------------------------ */
+int qxc_abi_version(void);
+const char* qxc_status_string(qxc_status status);
+/* One context per host thread; `device` is the CUDA ordinal. */
+qxc_status qxc_init(int device, qxc_ctx** out);
+void qxc_destroy(qxc_ctx* ctx);
+/* Use the caller's cudaStream_t (NULL restores the context's own stream). */
+qxc_status qxc_set_stream(qxc_ctx* ctx, void* cuda_stream);
+void* qxc_get_stream(qxc_ctx* ctx);
+/* Wait for all work on the context stream, then report any device-side
+ * error (non-finite values, bounded-wait timeouts) recorded since the last
+ * sync. Mirrors DecodeGraph::finish (qx-metal lib.rs:9404-9440). */
+qxc_status qxc_sync(qxc_ctx* ctx);
+/* Message of the last failing call on this context ("" when none). */
+const char* qxc_last_error(const qxc_ctx* ctx);
+/* Number of kernels this context has launched so far. */
+uint64_t qxc_launch_count(const qxc_ctx* ctx);
+
+/* ---- KV cache arena ---------------------------------------------------- */
+typedef struct qxc_kv_desc {
+  int32_t model;       /* qxc_model */
+  int32_t layers;      /* >= 1 */
+  int32_t sequences;   /* >= 1, independent cursors */
+  int32_t capacity;    /* slots per sequence (Granite: 1..=4096, ExecutionPlan::granite :6589) */
+  int32_t key_dtype;   /* qxc_dtype of stored keys */
+  int32_t value_dtype; /* qxc_dtype of stored values */
+  int32_t first_position; /* absolute position of slot 0 (KV-length shards); 0 otherwise */
+} qxc_kv_desc;
+
+/* Bytes the arena holds for keys and values, without allocating
+ * (ExecutionPlan::kv_key_bytes/kv_value_bytes, qx-runtime-v2 lib.rs:6640-6656). */
+qxc_status qxc_kv_bytes(const qxc_kv_desc* desc, size_t* key_bytes, size_t* value_bytes);
+/* One device allocation; layout per (sequence, layer):
+ * keys [capacity][kv_heads][head_dim], values likewise (position-major, the
+ * reference's layout). Cursors start at 0. */
+qxc_status qxc_kv_create(qxc_ctx* ctx, const qxc_kv_desc* desc, qxc_kv** out);
+void qxc_kv_destroy(qxc_kv* kv);
+/* KvCache::len / is_empty / reset (qx-runtime lib.rs:370-380). seq < 0 in reset: all. */
+qxc_status qxc_kv_len(const qxc_kv* kv, int32_t seq, int32_t* length);
+qxc_status qxc_kv_reset(qxc_kv* kv, int32_t seq);
+/* Set a cursor after loading a prefix with qxc_kv_write (0 <= length <= capacity). */
+qxc_status qxc_kv_set_len(qxc_kv* kv, int32_t seq, int32_t length);
+/* Speculative cursor (qx-runtime-v2 lib.rs:3265-3310): no KV copies. */
+qxc_status qxc_kv_checkpoint(const qxc_kv* kv, int32_t seq, int32_t* sequence_len);
+qxc_status qxc_kv_rollback(qxc_kv* kv, int32_t seq, int32_t sequence_len);
+qxc_status qxc_kv_commit(qxc_kv* kv, int32_t seq, int32_t sequence_len, int32_t accepted_prefix);
+/* Device views of one (sequence, layer) cache (kv_key_buffer / kv_value_buffer). */
+qxc_status qxc_kv_key_buffer(qxc_kv* kv, int32_t seq, int32_t layer, void** device_ptr, size_t* bytes);
+qxc_status qxc_kv_value_buffer(qxc_kv* kv, int32_t seq, int32_t layer, void** device_ptr, size_t* bytes);
+/* Synchronous host copies of slots [begin, begin+count) of one (sequence,
+ * layer); either host pointer may be NULL. */
+qxc_status qxc_kv_read(qxc_kv* kv, int32_t seq, int32_t layer, int32_t begin, int32_t count,
+                       void* host_keys, void* host_values);
+qxc_status qxc_kv_write(qxc_kv* kv, int32_t seq, int32_t layer, int32_t begin, int32_t count,
+                        const void* host_keys, const void* host_values);
+
+/* ---- decode ------------------------------------------------------------ */
+/* One token step for `seq_count` sequences over layers
+ * [layer_begin, layer_begin + layer_count). Per (sequence, layer): RoPE on
+ * q and k at `position` (Qwen: per-head RMSNorm first), append k/v into slot
+ * `position`, attend over slots [0, position]. Tensors are packed
+ * [seq_count][layer_count][heads * head_dim]:
+ *   q, out: query heads; k, v: kv heads.
+ * positions[i] must equal sequence seq_ids[i]'s length (KvCache::append
+ * :382-405), else QXC_ERR_POSITION and nothing is launched. Unless
+ * QXC_DECODE_NO_ADVANCE, each cursor advances by one. */
+typedef struct qxc_decode_args {
+  int32_t layer_begin;
+  int32_t layer_count;
+  int32_t seq_count;
+  const int32_t* seq_ids;   /* host [seq_count]; NULL = 0..seq_count-1 */
+  const int32_t* positions; /* host [seq_count] */
+  const void* q;            /* device, q_dtype */
+  const void* k;            /* device, in_dtype */
+  const void* v;            /* device, in_dtype */
+  void* out;                /* device, out_dtype */
+  float* q_rot_out;         /* optional device f32 rotated query (V2 writes it back), NULL to skip */
+  const float* q_norm;      /* Qwen: device [128] RMSNorm weight for q, NULL = 1.0 */
+  const float* k_norm;      /* Qwen: device [128] RMSNorm weight for k, NULL = 1.0 */
+  int32_t q_dtype;          /* F32 or BF16 (Qwen: BF16 or F16, the KV type) */
+  int32_t in_dtype;         /* dtype of k and v inputs */
+  int32_t out_dtype;        /* F32, BF16 or F16 */
+  int32_t flags;            /* QXC_DECODE_* */
+  int32_t split;            /* cache positions per CTA split, multiple of 64; 0 = automatic */
+} qxc_decode_args;
+qxc_status qxc_decode(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* args);
+/* Same with q, k, v, out (and q_rot_out) in HOST memory: copies in, decodes,
+ * copies out, waits. */
+qxc_status qxc_decode_host(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* args);
+
+/* granite_attention_decode (qx-runtime lib.rs:444-452): host arrays
+ * q[1024], k[512], v[512] -> out[1024] on sequence 0, layer 0 of a Granite
+ * arena. Synchronous; QXC_ERR_POSITION when position != length. */
+qxc_status qxc_granite_attention_decode(qxc_ctx* ctx, qxc_kv* kv, const float* q, const float* k,
+                                        const float* v, int32_t position, float* out);
+/* apply_granite_rope (qx-runtime lib.rs:434-442) in place on host arrays
+ * q[1024], k[512], computed on the device with qx's pinned sin/cos. */
+qxc_status qxc_apply_granite_rope(qxc_ctx* ctx, float* q, float* k, int32_t position);
+
+/* ---- causal prefill ------------------------------------------------------ */
+/* Prompt prefill of `length` tokens into an EMPTY (sequence, layer) of a
+ * Granite arena (cursor must be 0): RoPE on q and k at positions
+ * 0..length-1, all rows written to the cache, causal attention with fp32
+ * accumulation on tcgen05 tensor cores. q:[L][16][64], k,v:[L][8][64]
+ * (BF16), out:[L][16][64] (F32 or BF16). The cursor of `seq` becomes
+ * `length` (unless QXC_DECODE_NO_ADVANCE). Requires bf16 KV. */
+typedef struct qxc_prefill_args {
+  int32_t seq;
+  int32_t layer;
+  int32_t length;
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int32_t in_dtype;  /* BF16 */
+  int32_t out_dtype; /* F32 or BF16 */
+  int32_t flags;
+} qxc_prefill_args;
+qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* args);
+
+/* ---- KV-length split across GPUs --------------------------------------- */
+/* Partial attention of one (sequence, layer) over this arena's slots
+ * [first_position, first_position + length): per query head the triple
+ * (m, l, O[head_dim]) with O unnormalised relative to m, written as f32
+ * [q_heads][head_dim + 2] = {O..., m, l}. When `append` is non-zero this
+ * shard owns the new token: RoPE at absolute `position`, append into slot
+ * position - first_position, and include it. q/k/v as in qxc_decode for
+ * one sequence and one layer. */
+typedef struct qxc_partial_args {
+  int32_t seq;
+  int32_t layer;
+  int32_t position; /* absolute position of the new token (RoPE angle) */
+  int32_t append;   /* 1 on the shard that owns `position` */
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* q_norm;
+  const float* k_norm;
+  float* partials;  /* device [q_heads][head_dim + 2] */
+  int32_t q_dtype;
+  int32_t in_dtype;
+  int32_t flags;
+  int32_t split;
+} qxc_partial_args;
+qxc_status qxc_decode_partials(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args* args);
+/* Log-sum-exp merge of n_parts partial sets [n_parts][q_heads][head_dim+2]
+ * (device) into out [q_heads][head_dim] (device, out_dtype):
+ * M = max m_i, O = sum e^(m_i-M) O_i / sum e^(m_i-M) l_i. */
+qxc_status qxc_lse_merge(qxc_ctx* ctx, int32_t model, int32_t n_parts, const float* partials, void* out,
+                         int32_t out_dtype);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QXCUDA_H */

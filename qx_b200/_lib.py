@@ -1,0 +1,112 @@
+"""ctypes binding of libqxcuda.so (the C ABI declared in include/qxcuda.h).
+
+The library is required: importing this module on a machine where it is
+missing raises immediately, so no call can silently fall back to a CPU path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libqxcuda.so")
+
+# qxc_status
+OK, ERR_INVALID_ARG, ERR_POSITION, ERR_NONFINITE, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_UNSUPPORTED, \
+    ERR_OUT_OF_MEMORY = range(9)
+# qxc_model / qxc_dtype
+MODEL_GRANITE, MODEL_QWEN3 = 0, 1
+F32, BF16, F16 = 0, 1, 2
+DECODE_NO_ADVANCE, DECODE_NATIVE_EXP, DECODE_PINNED_EXP = 0x1, 0x2, 0x4
+
+
+class KvDesc(C.Structure):
+    _fields_ = [("model", C.c_int32), ("layers", C.c_int32), ("sequences", C.c_int32), ("capacity", C.c_int32),
+                ("key_dtype", C.c_int32), ("value_dtype", C.c_int32), ("first_position", C.c_int32)]
+
+
+class DecodeArgs(C.Structure):
+    _fields_ = [("layer_begin", C.c_int32), ("layer_count", C.c_int32), ("seq_count", C.c_int32),
+                ("seq_ids", C.POINTER(C.c_int32)), ("positions", C.POINTER(C.c_int32)),
+                ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("out", C.c_void_p),
+                ("q_rot_out", C.c_void_p), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p),
+                ("q_dtype", C.c_int32), ("in_dtype", C.c_int32), ("out_dtype", C.c_int32),
+                ("flags", C.c_int32), ("split", C.c_int32)]
+
+
+class PrefillArgs(C.Structure):
+    _fields_ = [("seq", C.c_int32), ("layer", C.c_int32), ("length", C.c_int32), ("q", C.c_void_p),
+                ("k", C.c_void_p), ("v", C.c_void_p), ("out", C.c_void_p), ("in_dtype", C.c_int32),
+                ("out_dtype", C.c_int32), ("flags", C.c_int32)]
+
+
+class PartialArgs(C.Structure):
+    _fields_ = [("seq", C.c_int32), ("layer", C.c_int32), ("position", C.c_int32), ("append", C.c_int32),
+                ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("q_norm", C.c_void_p),
+                ("k_norm", C.c_void_p), ("partials", C.c_void_p), ("q_dtype", C.c_int32),
+                ("in_dtype", C.c_int32), ("flags", C.c_int32), ("split", C.c_int32)]
+
+
+_lib = None
+
+
+def load() -> C.CDLL:
+    """Load libqxcuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m qx_b200.build` "
+                           "(qx_b200 has no CPU fallback)")
+    lib = C.CDLL(LIB_PATH)
+    vp, i32, pp = C.c_void_p, C.c_int32, C.POINTER(C.c_void_p)
+    sig = {
+        "qxc_abi_version": (C.c_int, []),
+        "qxc_status_string": (C.c_char_p, [C.c_int]),
+        "qxc_init": (C.c_int, [C.c_int, pp]),
+        "qxc_destroy": (None, [vp]),
+        "qxc_set_stream": (C.c_int, [vp, vp]),
+        "qxc_get_stream": (vp, [vp]),
+        "qxc_sync": (C.c_int, [vp]),
+        "qxc_last_error": (C.c_char_p, [vp]),
+        "qxc_launch_count": (C.c_uint64, [vp]),
+        "qxc_kv_bytes": (C.c_int, [C.POINTER(KvDesc), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
+        "qxc_kv_create": (C.c_int, [vp, C.POINTER(KvDesc), pp]),
+        "qxc_kv_destroy": (None, [vp]),
+        "qxc_kv_len": (C.c_int, [vp, i32, C.POINTER(i32)]),
+        "qxc_kv_reset": (C.c_int, [vp, i32]),
+        "qxc_kv_set_len": (C.c_int, [vp, i32, i32]),
+        "qxc_kv_checkpoint": (C.c_int, [vp, i32, C.POINTER(i32)]),
+        "qxc_kv_rollback": (C.c_int, [vp, i32, i32]),
+        "qxc_kv_commit": (C.c_int, [vp, i32, i32, i32]),
+        "qxc_kv_key_buffer": (C.c_int, [vp, i32, i32, pp, C.POINTER(C.c_size_t)]),
+        "qxc_kv_value_buffer": (C.c_int, [vp, i32, i32, pp, C.POINTER(C.c_size_t)]),
+        "qxc_kv_read": (C.c_int, [vp, i32, i32, i32, i32, vp, vp]),
+        "qxc_kv_write": (C.c_int, [vp, i32, i32, i32, i32, vp, vp]),
+        "qxc_decode": (C.c_int, [vp, vp, C.POINTER(DecodeArgs)]),
+        "qxc_decode_host": (C.c_int, [vp, vp, C.POINTER(DecodeArgs)]),
+        "qxc_granite_attention_decode": (C.c_int, [vp, vp, vp, vp, vp, i32, vp]),
+        "qxc_apply_granite_rope": (C.c_int, [vp, vp, vp, i32]),
+        "qxc_prefill": (C.c_int, [vp, vp, C.POINTER(PrefillArgs)]),
+        "qxc_decode_partials": (C.c_int, [vp, vp, C.POINTER(PartialArgs)]),
+        "qxc_lse_merge": (C.c_int, [vp, i32, i32, vp, vp, i32]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def header_symbols(header: str | None = None) -> list[str]:
+    """Every function name declared in include/*.h (for the export check)."""
+    import re
+    inc = os.path.join(os.path.dirname(PKG), "include")
+    names = []
+    for f in sorted(os.listdir(inc)) if header is None else [header]:
+        if f.endswith(".h"):
+            text = open(os.path.join(inc, f)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names += re.findall(r"\b(qxc_\w+)\s*\(", text)
+    return sorted(set(names))

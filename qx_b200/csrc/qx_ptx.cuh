@@ -1,0 +1,112 @@
+// qx_ptx.cuh — hand-written PTX for sm_100a: mbarriers, TMA bulk copies,
+// and bounded waits.
+//
+// Every wait on an mbarrier is bounded: after kMaxWaitNs it gives up,
+// records QX_ERR_BIT_TIMEOUT in the context's error word and returns
+// false, so a kernel never spins forever. No copy issued here uses cluster
+// multicast.
+#pragma once
+#include <stdint.h>
+
+namespace qx {
+
+// Error-word bits (qxc_sync maps them to status codes).
+constexpr unsigned QX_ERR_BIT_NONFINITE = 0x1u;
+constexpr unsigned QX_ERR_BIT_TIMEOUT = 0x2u;
+
+// Record a device-side error. The word lives in mapped pinned host memory;
+// a plain volatile store (no read-modify-write) is enough because the host
+// only needs "some error happened, of this kind".
+__device__ __forceinline__ void flag_error(unsigned* err, unsigned bit) {
+  if (err) *reinterpret_cast<volatile unsigned*>(err) = bit;
+}
+
+// Bound on any device-side wait, in nanoseconds of %globaltimer: far beyond
+// a legitimate copy latency (microseconds), short enough that a stuck wait
+// returns an error to the host instead of holding the GPU.
+constexpr unsigned long long kMaxWaitNs = 1000000000ull;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Make mbarrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`. Returns false (and flags the
+// error word) if the phase never completed within the poll budget.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = global_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - start > kMaxWaitNs) break;
+  }
+  flag_error(err, QX_ERR_BIT_TIMEOUT);
+  return false;
+}
+
+// TMA bulk copy global -> this CTA's shared memory, completing on `bar`.
+// dst and src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Same with an L2 eviction-priority hint (evict_first for streamed KV).
+__device__ __forceinline__ void bulk_copy_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                   uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+      "%4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+}  // namespace qx

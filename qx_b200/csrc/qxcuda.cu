@@ -1,0 +1,853 @@
+// qxcuda.cu — host side of libqxcuda: contexts, KV arenas, argument
+// validation with the reference's error behaviour, and kernel dispatch.
+//
+// Error behaviour mirrors crates/qx-runtime/src/lib.rs:382-405
+// (KvCache::append: "KV position {p} does not follow cache length {len}",
+// "KV position {p} exceeds context {max}") and
+// crates/qx-runtime-v2/src/lib.rs:6587-6589 ("context {c} must be in
+// 1..=4096"). Nothing is launched when validation fails, so a rejected call
+// leaves the cache untouched, as the reference's Err return does.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/qxcuda.h"
+#include "decode.cuh"
+#include "prefill.cuh"
+
+using namespace qx;
+
+struct qxc_ctx {
+  int device = 0;
+  int sm_count = 148;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  unsigned* err_host = nullptr;  // mapped pinned error word
+  unsigned* err_dev = nullptr;
+  // scratch (grown on demand)
+  float* partials = nullptr;
+  size_t partials_cap = 0;  // floats
+  int* tickets = nullptr;
+  size_t tickets_cap = 0;  // ints
+  // per-call sequence tables: device ring + pinned host ring
+  static constexpr int kRing = 8;
+  SeqInfo* seq_dev[kRing] = {};
+  SeqInfo* seq_host[kRing] = {};
+  cudaEvent_t seq_ev[kRing] = {};
+  size_t seq_cap[kRing] = {};
+  int seq_next = 0;
+  // device staging for host-pointer entry points
+  char* stage_dev = nullptr;
+  size_t stage_cap = 0;
+  char* stage_host = nullptr;
+  size_t stage_host_cap = 0;
+  unsigned long long launches = 0;
+};
+
+struct qxc_kv {
+  qxc_ctx* ctx = nullptr;
+  qxc_kv_desc desc{};
+  int hq = 0, hkv = 0, d = 0;
+  size_t kes = 0, ves = 0;
+  char* base = nullptr;
+  char* k_region = nullptr;
+  char* v_region = nullptr;
+  size_t k_unit = 0, v_unit = 0;  // bytes per (sequence, layer)
+  std::vector<int> len;
+  float2* rope_table = nullptr;  // Qwen (cos, sin) per absolute position
+};
+
+namespace {
+
+qxc_status fail(qxc_ctx* ctx, qxc_status st, const char* fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    ctx->err = buf;
+  }
+  return st;
+}
+
+#define QXC_CUDA(ctx, call)                                                                          \
+  do {                                                                                               \
+    cudaError_t e_ = (call);                                                                         \
+    if (e_ != cudaSuccess)                                                                           \
+      return fail((ctx), e_ == cudaErrorMemoryAllocation ? QXC_ERR_OUT_OF_MEMORY : QXC_ERR_CUDA,     \
+                  "%s: %s", #call, cudaGetErrorString(e_));                                          \
+  } while (0)
+
+size_t dtype_size(int dt) { return dt == QXC_F32 ? 4 : 2; }
+bool valid_dtype(int dt) { return dt == QXC_F32 || dt == QXC_BF16 || dt == QXC_F16; }
+
+void model_shape(int model, int* hq, int* hkv, int* d) {
+  if (model == QXC_MODEL_QWEN3) {
+    *hq = 32, *hkv = 4, *d = 128;
+  } else {
+    *hq = 16, *hkv = 8, *d = 64;
+  }
+}
+
+qxc_status check_desc(qxc_ctx* ctx, const qxc_kv_desc* d) {
+  if (!d) return fail(ctx, QXC_ERR_INVALID_ARG, "null KV descriptor");
+  if (d->model != QXC_MODEL_GRANITE && d->model != QXC_MODEL_QWEN3)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "unknown model %d", d->model);
+  if (d->layers < 1 || d->sequences < 1)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "layers and sequences must be >= 1");
+  if (!valid_dtype(d->key_dtype) || !valid_dtype(d->value_dtype))
+    return fail(ctx, QXC_ERR_INVALID_ARG, "unknown KV dtype");
+  if (d->first_position < 0) return fail(ctx, QXC_ERR_INVALID_ARG, "first_position must be >= 0");
+  if (d->model == QXC_MODEL_GRANITE) {
+    // ExecutionPlan::granite_with_kv_element_bytes (qx-runtime-v2 lib.rs:6587-6589)
+    if (d->capacity == 0 || d->capacity < 0 || d->first_position + d->capacity > 4096)
+      return fail(ctx, QXC_ERR_INVALID_ARG, "context %d must be in 1..=4096", d->first_position + d->capacity);
+  } else {
+    // Qwen3-30B-A3B max_position_embeddings 40960 (qx-model lib.rs:308); the
+    // decode kernel supports 16-bit KV only.
+    if (d->capacity < 1 || d->first_position + d->capacity > 40960)
+      return fail(ctx, QXC_ERR_INVALID_ARG, "context %d must be in 1..=40960", d->first_position + d->capacity);
+    if (d->key_dtype == QXC_F32 || d->value_dtype != d->key_dtype)
+      return fail(ctx, QXC_ERR_UNSUPPORTED, "Qwen KV must be bf16 or f16 for both keys and values");
+  }
+  if (d->model == QXC_MODEL_GRANITE && d->key_dtype != d->value_dtype) {
+    const bool ok = (d->key_dtype == QXC_F32 && d->value_dtype == QXC_F16) ||
+                    (d->key_dtype == QXC_F16 && d->value_dtype == QXC_F32);
+    if (!ok) return fail(ctx, QXC_ERR_UNSUPPORTED, "mixed KV precision must be f32/f16");
+  }
+  if (d->model == QXC_MODEL_GRANITE && d->key_dtype == QXC_F32 && d->value_dtype == QXC_BF16)
+    return fail(ctx, QXC_ERR_UNSUPPORTED, "unsupported KV precision");
+  return QXC_OK;
+}
+
+template <typename T>
+qxc_status grow(qxc_ctx* ctx, T** ptr, size_t* cap, size_t need, bool zero) {
+  if (need <= *cap) return QXC_OK;
+  size_t n = std::max(need, *cap * 2);
+  if (*ptr) {
+    QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    *cap = 0;
+  }
+  QXC_CUDA(ctx, cudaMalloc(reinterpret_cast<void**>(ptr), n * sizeof(T)));
+  if (zero) QXC_CUDA(ctx, cudaMemsetAsync(*ptr, 0, n * sizeof(T), ctx->stream));
+  *cap = n;
+  return QXC_OK;
+}
+
+// Positions per split: multiple of 64, chosen so the grid covers the GPU
+// several times over (split-KV exists to fill 148 SMs at batch 1).
+int auto_chunk(const qxc_ctx* ctx, long long total_slots, int max_attend) {
+  const long long target = (long long)ctx->sm_count * 8;
+  long long c = (total_slots + target - 1) / target;
+  c = std::max<long long>(c, 256);
+  c = ((c + 63) / 64) * 64;
+  c = std::min<long long>(c, std::max(64, ((max_attend + 63) / 64) * 64));
+  return (int)std::max<long long>(c, 64);
+}
+
+using KernelFn = void (*)(DecodeParams);
+
+template <class M, typename KT, typename VT>
+qxc_status launch_typed(qxc_ctx* ctx, const DecodeParams& p, int items) {
+  using C = DecodeCfg<M, KT, VT>;
+  static unsigned long long configured = 0;  // one bit per device ordinal
+  const unsigned long long bit = 1ull << (ctx->device & 63);
+  if (!(configured & bit)) {
+    QXC_CUDA(ctx, cudaFuncSetAttribute(qx_decode_kernel<M, KT, VT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM));
+    configured |= bit;
+  }
+  qx_decode_kernel<M, KT, VT><<<items, C::NT, C::SMEM, ctx->stream>>>(p);
+  QXC_CUDA(ctx, cudaGetLastError());
+  ctx->launches++;
+  return QXC_OK;
+}
+
+qxc_status launch_decode(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams& p, int items) {
+  const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
+  if (kv->desc.model == QXC_MODEL_QWEN3) {
+    if (kd == QXC_BF16) return launch_typed<Qwen3, __nv_bfloat16, __nv_bfloat16>(ctx, p, items);
+    return launch_typed<Qwen3, __half, __half>(ctx, p, items);
+  }
+  if (kd == QXC_F32 && vd == QXC_F32) return launch_typed<Granite, float, float>(ctx, p, items);
+  if (kd == QXC_F32 && vd == QXC_F16) return launch_typed<Granite, float, __half>(ctx, p, items);
+  if (kd == QXC_F16 && vd == QXC_F32) return launch_typed<Granite, __half, float>(ctx, p, items);
+  if (kd == QXC_F16 && vd == QXC_F16) return launch_typed<Granite, __half, __half>(ctx, p, items);
+  return launch_typed<Granite, __nv_bfloat16, __nv_bfloat16>(ctx, p, items);
+}
+
+// Upload a sequence table through the pinned ring (host slot reuse waits on
+// the event of the copy that last read it).
+qxc_status upload_seq_table(qxc_ctx* ctx, const std::vector<SeqInfo>& tab, const SeqInfo** dev) {
+  const int i = ctx->seq_next;
+  ctx->seq_next = (i + 1) % qxc_ctx::kRing;
+  const size_t need = tab.size();
+  if (ctx->seq_ev[i]) QXC_CUDA(ctx, cudaEventSynchronize(ctx->seq_ev[i]));
+  if (need > ctx->seq_cap[i]) {
+    if (ctx->seq_dev[i]) {
+      QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+      cudaFree(ctx->seq_dev[i]);
+      cudaFreeHost(ctx->seq_host[i]);
+    }
+    size_t n = std::max<size_t>(need, 256);
+    QXC_CUDA(ctx, cudaMalloc(&ctx->seq_dev[i], n * sizeof(SeqInfo)));
+    QXC_CUDA(ctx, cudaMallocHost(&ctx->seq_host[i], n * sizeof(SeqInfo)));
+    ctx->seq_cap[i] = n;
+  }
+  if (!ctx->seq_ev[i]) QXC_CUDA(ctx, cudaEventCreateWithFlags(&ctx->seq_ev[i], cudaEventDisableTiming));
+  memcpy(ctx->seq_host[i], tab.data(), need * sizeof(SeqInfo));
+  QXC_CUDA(ctx, cudaMemcpyAsync(ctx->seq_dev[i], ctx->seq_host[i], need * sizeof(SeqInfo), cudaMemcpyHostToDevice,
+                                ctx->stream));
+  QXC_CUDA(ctx, cudaEventRecord(ctx->seq_ev[i], ctx->stream));
+  *dev = ctx->seq_dev[i];
+  return QXC_OK;
+}
+
+struct CallPlan {
+  std::vector<SeqInfo> tab;
+  int items = 0;
+  int chunk = 0;
+};
+
+// Build the work decomposition of one call. `attend[i]`, `new_slot[i]`,
+// `rope_pos[i]` per sequence entry.
+qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* seq_ids, const int* attend,
+                     const int* new_slot, const int* rope_pos, int layer_count, int split, CallPlan* out) {
+  long long total_slots = 0;
+  int max_attend = 0;
+  for (int i = 0; i < seq_count; ++i) {
+    total_slots += (long long)attend[i] * layer_count * kv->hkv;
+    max_attend = std::max(max_attend, attend[i]);
+  }
+  int chunk = split;
+  if (chunk == 0) chunk = auto_chunk(ctx, total_slots, max_attend);
+  if (chunk <= 0 || chunk % 64 != 0) return fail(ctx, QXC_ERR_INVALID_ARG, "split %d must be a positive multiple of 64", split);
+  out->chunk = chunk;
+  out->tab.resize(seq_count);
+  long long items = 0;
+  for (int i = 0; i < seq_count; ++i) {
+    SeqInfo& s = out->tab[i];
+    s.seq_id = seq_ids ? seq_ids[i] : i;
+    s.attend = attend[i];
+    s.new_slot = new_slot[i];
+    s.rope_pos = rope_pos[i];
+    s.item_begin = (int)items;
+    s.pad[0] = s.pad[1] = s.pad[2] = 0;
+    const long long nsplit = (attend[i] + chunk - 1) / chunk;
+    items += nsplit * layer_count * kv->hkv;
+  }
+  if (items > 0x7fffffffLL) return fail(ctx, QXC_ERR_INVALID_ARG, "too much work in one call");
+  out->items = (int)items;
+  return QXC_OK;
+}
+
+qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer_begin, int layer_count,
+                       DecodeParams* p) {
+  memset(p, 0, sizeof(*p));
+  p->k_region = kv->k_region;
+  p->v_region = kv->v_region;
+  p->k_unit_bytes = (long long)kv->k_unit;
+  p->v_unit_bytes = (long long)kv->v_unit;
+  p->layers = kv->desc.layers;
+  p->layer_begin = layer_begin;
+  p->layer_count = layer_count;
+  p->n_seq = (int)plan.tab.size();
+  p->chunk = plan.chunk;
+  p->rope_table = kv->rope_table;
+  p->err = ctx->err_dev;
+  if (plan.tab.size() == 1) {
+    p->seq_table = nullptr;
+    p->single = plan.tab[0];
+  } else {
+    qxc_status st = upload_seq_table(ctx, plan.tab, &p->seq_table);
+    if (st != QXC_OK) return st;
+  }
+  const int G = kv->hq / kv->hkv;
+  qxc_status st = grow(ctx, &ctx->partials, &ctx->partials_cap, (size_t)plan.items * G * (kv->d + 2), false);
+  if (st != QXC_OK) return st;
+  st = grow(ctx, &ctx->tickets, &ctx->tickets_cap, (size_t)plan.tab.size() * layer_count * kv->hkv, true);
+  if (st != QXC_OK) return st;
+  p->partials = ctx->partials;
+  p->tickets = ctx->tickets;
+  return QXC_OK;
+}
+
+bool default_pinned(const qxc_kv* kv, int flags) {
+  if (flags & QXC_DECODE_NATIVE_EXP) return false;
+  if (flags & QXC_DECODE_PINNED_EXP) return true;
+  return kv->desc.model == QXC_MODEL_GRANITE;
+}
+
+qxc_status check_seq(qxc_ctx* ctx, const qxc_kv* kv, int seq) {
+  if (seq < 0 || seq >= kv->desc.sequences)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "sequence %d is outside the arena (%d sequences)", seq, kv->desc.sequences);
+  return QXC_OK;
+}
+
+}  // namespace
+
+// ============================================================================
+extern "C" {
+
+int qxc_abi_version(void) { return QXC_ABI_VERSION; }
+
+const char* qxc_status_string(qxc_status s) {
+  switch (s) {
+    case QXC_OK: return "ok";
+    case QXC_ERR_INVALID_ARG: return "invalid argument";
+    case QXC_ERR_POSITION: return "KV position error";
+    case QXC_ERR_NONFINITE: return "non-finite value";
+    case QXC_ERR_CUDA: return "CUDA error";
+    case QXC_ERR_NCCL: return "NCCL error";
+    case QXC_ERR_TIMEOUT: return "device wait timed out";
+    case QXC_ERR_UNSUPPORTED: return "unsupported";
+    case QXC_ERR_OUT_OF_MEMORY: return "out of device memory";
+  }
+  return "unknown status";
+}
+
+qxc_status qxc_init(int device, qxc_ctx** out) {
+  if (!out) return QXC_ERR_INVALID_ARG;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return QXC_ERR_CUDA;
+  qxc_ctx* ctx = new (std::nothrow) qxc_ctx();
+  if (!ctx) return QXC_ERR_OUT_OF_MEMORY;
+  ctx->device = device;
+  if (cudaSetDevice(device) != cudaSuccess) {
+    delete ctx;
+    return QXC_ERR_CUDA;
+  }
+  cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void**>(&ctx->err_host), sizeof(unsigned), cudaHostAllocMapped) != cudaSuccess ||
+      cudaHostGetDevicePointer(reinterpret_cast<void**>(&ctx->err_dev), ctx->err_host, 0) != cudaSuccess) {
+    qxc_destroy(ctx);
+    return QXC_ERR_CUDA;
+  }
+  *ctx->err_host = 0;
+  ctx->stream = ctx->own_stream;
+  *out = ctx;
+  return QXC_OK;
+}
+
+void qxc_destroy(qxc_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  cudaFree(ctx->partials);
+  cudaFree(ctx->tickets);
+  for (int i = 0; i < qxc_ctx::kRing; ++i) {
+    cudaFree(ctx->seq_dev[i]);
+    if (ctx->seq_host[i]) cudaFreeHost(ctx->seq_host[i]);
+    if (ctx->seq_ev[i]) cudaEventDestroy(ctx->seq_ev[i]);
+  }
+  cudaFree(ctx->stage_dev);
+  if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
+  if (ctx->err_host) cudaFreeHost(ctx->err_host);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  delete ctx;
+}
+
+qxc_status qxc_set_stream(qxc_ctx* ctx, void* stream) {
+  if (!ctx) return QXC_ERR_INVALID_ARG;
+  ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+  return QXC_OK;
+}
+
+void* qxc_get_stream(qxc_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+qxc_status qxc_sync(qxc_ctx* ctx) {
+  if (!ctx) return QXC_ERR_INVALID_ARG;
+  QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(ctx->err_host);
+  if (e) {
+    *reinterpret_cast<volatile unsigned*>(ctx->err_host) = 0;
+    // a kernel that stopped early may have left split tickets raised
+    if (ctx->tickets) {
+      cudaMemsetAsync(ctx->tickets, 0, ctx->tickets_cap * sizeof(int), ctx->stream);
+      cudaStreamSynchronize(ctx->stream);
+    }
+    if (e & QX_ERR_BIT_TIMEOUT) return fail(ctx, QXC_ERR_TIMEOUT, "a bounded device-side wait gave up");
+    return fail(ctx, QXC_ERR_NONFINITE, "non-finite value in RoPE or attention (the reference panics here)");
+  }
+  return QXC_OK;
+}
+
+const char* qxc_last_error(const qxc_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+uint64_t qxc_launch_count(const qxc_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+// ---- KV arena ---------------------------------------------------------------
+qxc_status qxc_kv_bytes(const qxc_kv_desc* d, size_t* key_bytes, size_t* value_bytes) {
+  qxc_status st = check_desc(nullptr, d);
+  if (st != QXC_OK) return st;
+  int hq, hkv, hd;
+  model_shape(d->model, &hq, &hkv, &hd);
+  const size_t per = (size_t)d->capacity * hkv * hd * (size_t)d->layers * d->sequences;
+  if (key_bytes) *key_bytes = per * dtype_size(d->key_dtype);
+  if (value_bytes) *value_bytes = per * dtype_size(d->value_dtype);
+  return QXC_OK;
+}
+
+qxc_status qxc_kv_create(qxc_ctx* ctx, const qxc_kv_desc* desc, qxc_kv** out) {
+  if (!ctx || !out) return QXC_ERR_INVALID_ARG;
+  *out = nullptr;
+  qxc_status st = check_desc(ctx, desc);
+  if (st != QXC_OK) return st;
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  qxc_kv* kv = new (std::nothrow) qxc_kv();
+  if (!kv) return fail(ctx, QXC_ERR_OUT_OF_MEMORY, "host allocation failed");
+  kv->ctx = ctx;
+  kv->desc = *desc;
+  model_shape(desc->model, &kv->hq, &kv->hkv, &kv->d);
+  kv->kes = dtype_size(desc->key_dtype);
+  kv->ves = dtype_size(desc->value_dtype);
+  kv->k_unit = (size_t)desc->capacity * kv->hkv * kv->d * kv->kes;
+  kv->v_unit = (size_t)desc->capacity * kv->hkv * kv->d * kv->ves;
+  const size_t units = (size_t)desc->layers * desc->sequences;
+  const size_t kbytes = kv->k_unit * units, vbytes = kv->v_unit * units;
+  const size_t koff_v = ((kbytes + 255) / 256) * 256;
+  cudaError_t e = cudaMalloc(&kv->base, koff_v + vbytes);
+  if (e != cudaSuccess) {
+    delete kv;
+    return fail(ctx, e == cudaErrorMemoryAllocation ? QXC_ERR_OUT_OF_MEMORY : QXC_ERR_CUDA,
+                "KV arena of %zu bytes: %s", koff_v + vbytes, cudaGetErrorString(e));
+  }
+  // Zero-initialised like KvCache::new (qx-runtime lib.rs:359-368).
+  cudaMemsetAsync(kv->base, 0, koff_v + vbytes, ctx->stream);
+  kv->k_region = kv->base;
+  kv->v_region = kv->base + koff_v;
+  kv->len.assign(desc->sequences, 0);
+  if (desc->model == QXC_MODEL_QWEN3) {
+    // cos/sin of position * 1e6^(-i/64) with the platform's single-precision
+    // powf/sinf/cosf, as tools/qx-qwen-parity/src/main.rs:1193-1195 evaluates
+    // them; computed once here so the device never evaluates transcendental
+    // RoPE and every position's table is identical to the host's.
+    const int n = desc->first_position + desc->capacity;
+    std::vector<float2> tab((size_t)n * 64);
+    float inv[64];
+    for (int i = 0; i < 64; ++i) inv[i] = powf(1000000.0f, -(float)i / 64.0f);
+    for (int pos = 0; pos < n; ++pos)
+      for (int i = 0; i < 64; ++i) {
+        volatile float angle = (float)pos * inv[i];
+        tab[(size_t)pos * 64 + i] = make_float2(cosf(angle), sinf(angle));
+      }
+    e = cudaMalloc(&kv->rope_table, tab.size() * sizeof(float2));
+    if (e == cudaSuccess)
+      e = cudaMemcpy(kv->rope_table, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(kv->base);
+      cudaFree(kv->rope_table);
+      delete kv;
+      return fail(ctx, QXC_ERR_CUDA, "RoPE table: %s", cudaGetErrorString(e));
+    }
+  }
+  QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  *out = kv;
+  return QXC_OK;
+}
+
+void qxc_kv_destroy(qxc_kv* kv) {
+  if (!kv) return;
+  cudaSetDevice(kv->ctx->device);
+  cudaStreamSynchronize(kv->ctx->stream);
+  cudaFree(kv->base);
+  cudaFree(kv->rope_table);
+  delete kv;
+}
+
+qxc_status qxc_kv_len(const qxc_kv* kv, int32_t seq, int32_t* length) {
+  if (!kv || !length) return QXC_ERR_INVALID_ARG;
+  if (seq < 0 || seq >= kv->desc.sequences) return QXC_ERR_INVALID_ARG;
+  *length = kv->len[seq];
+  return QXC_OK;
+}
+
+qxc_status qxc_kv_reset(qxc_kv* kv, int32_t seq) {
+  if (!kv) return QXC_ERR_INVALID_ARG;
+  if (seq < 0) {
+    std::fill(kv->len.begin(), kv->len.end(), 0);
+    return QXC_OK;
+  }
+  if (seq >= kv->desc.sequences) return fail(kv->ctx, QXC_ERR_INVALID_ARG, "sequence %d out of range", seq);
+  kv->len[seq] = 0;
+  return QXC_OK;
+}
+
+qxc_status qxc_kv_set_len(qxc_kv* kv, int32_t seq, int32_t length) {
+  if (!kv) return QXC_ERR_INVALID_ARG;
+  qxc_status st = check_seq(kv->ctx, kv, seq);
+  if (st != QXC_OK) return st;
+  if (length < 0 || length > kv->desc.capacity)
+    return fail(kv->ctx, QXC_ERR_POSITION, "KV length %d is outside capacity %d", length, kv->desc.capacity);
+  kv->len[seq] = length;
+  return QXC_OK;
+}
+
+qxc_status qxc_kv_checkpoint(const qxc_kv* kv, int32_t seq, int32_t* sequence_len) {
+  return qxc_kv_len(kv, seq, sequence_len);
+}
+
+// rollback_kv (qx-runtime-v2 lib.rs:3273-3286)
+qxc_status qxc_kv_rollback(qxc_kv* kv, int32_t seq, int32_t sequence_len) {
+  if (!kv) return QXC_ERR_INVALID_ARG;
+  qxc_status st = check_seq(kv->ctx, kv, seq);
+  if (st != QXC_OK) return st;
+  if (sequence_len < 0 || sequence_len > kv->len[seq] || sequence_len > kv->desc.capacity)
+    return fail(kv->ctx, QXC_ERR_POSITION, "KV rollback checkpoint %d is outside current position %d / context %d",
+                sequence_len, kv->len[seq], kv->desc.capacity);
+  kv->len[seq] = sequence_len;
+  return QXC_OK;
+}
+
+// commit_kv (qx-runtime-v2 lib.rs:3291-3310)
+qxc_status qxc_kv_commit(qxc_kv* kv, int32_t seq, int32_t sequence_len, int32_t accepted_prefix) {
+  if (!kv) return QXC_ERR_INVALID_ARG;
+  qxc_status st = check_seq(kv->ctx, kv, seq);
+  if (st != QXC_OK) return st;
+  if (sequence_len < 0 || accepted_prefix < 0 || (long long)sequence_len + accepted_prefix > 0x7fffffffLL)
+    return fail(kv->ctx, QXC_ERR_POSITION, "KV commit position overflow");
+  const int end = sequence_len + accepted_prefix;
+  const int position = kv->len[seq];
+  if (sequence_len > position || end > position || end > kv->desc.capacity)
+    return fail(kv->ctx, QXC_ERR_POSITION, "KV commit [%d, %d) is outside current speculative range ending at %d",
+                sequence_len, end, position);
+  kv->len[seq] = end;
+  return QXC_OK;
+}
+
+static qxc_status kv_view(qxc_kv* kv, int32_t seq, int32_t layer, bool key, void** ptr, size_t* bytes) {
+  if (!kv || !ptr) return QXC_ERR_INVALID_ARG;
+  if (seq < 0 || seq >= kv->desc.sequences) return fail(kv->ctx, QXC_ERR_INVALID_ARG, "sequence %d out of range", seq);
+  if (layer < 0 || layer >= kv->desc.layers)
+    return fail(kv->ctx, QXC_ERR_INVALID_ARG, "KV layer %d is outside the plan", layer);
+  const size_t unit = (size_t)seq * kv->desc.layers + layer;
+  *ptr = key ? kv->k_region + unit * kv->k_unit : kv->v_region + unit * kv->v_unit;
+  if (bytes) *bytes = key ? kv->k_unit : kv->v_unit;
+  return QXC_OK;
+}
+
+qxc_status qxc_kv_key_buffer(qxc_kv* kv, int32_t seq, int32_t layer, void** p, size_t* bytes) {
+  return kv_view(kv, seq, layer, true, p, bytes);
+}
+qxc_status qxc_kv_value_buffer(qxc_kv* kv, int32_t seq, int32_t layer, void** p, size_t* bytes) {
+  return kv_view(kv, seq, layer, false, p, bytes);
+}
+
+static qxc_status kv_copy(qxc_kv* kv, int32_t seq, int32_t layer, int32_t begin, int32_t count, void* hk,
+                          void* hv, bool to_host) {
+  if (!kv) return QXC_ERR_INVALID_ARG;
+  qxc_ctx* ctx = kv->ctx;
+  void *kp, *vp;
+  qxc_status st = kv_view(kv, seq, layer, true, &kp, nullptr);
+  if (st != QXC_OK) return st;
+  kv_view(kv, seq, layer, false, &vp, nullptr);
+  if (begin < 0 || count < 0 || (long long)begin + count > kv->desc.capacity)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "slots [%d, %d) outside capacity %d", begin, begin + count, kv->desc.capacity);
+  const size_t row = (size_t)kv->hkv * kv->d;
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  char* kdev = static_cast<char*>(kp) + (size_t)begin * row * kv->kes;
+  char* vdev = static_cast<char*>(vp) + (size_t)begin * row * kv->ves;
+  if (hk) {
+    if (to_host) QXC_CUDA(ctx, cudaMemcpy(hk, kdev, (size_t)count * row * kv->kes, cudaMemcpyDeviceToHost));
+    else QXC_CUDA(ctx, cudaMemcpy(kdev, hk, (size_t)count * row * kv->kes, cudaMemcpyHostToDevice));
+  }
+  if (hv) {
+    if (to_host) QXC_CUDA(ctx, cudaMemcpy(hv, vdev, (size_t)count * row * kv->ves, cudaMemcpyDeviceToHost));
+    else QXC_CUDA(ctx, cudaMemcpy(vdev, hv, (size_t)count * row * kv->ves, cudaMemcpyHostToDevice));
+  }
+  return QXC_OK;
+}
+
+qxc_status qxc_kv_read(qxc_kv* kv, int32_t seq, int32_t layer, int32_t begin, int32_t count, void* hk, void* hv) {
+  return kv_copy(kv, seq, layer, begin, count, hk, hv, true);
+}
+qxc_status qxc_kv_write(qxc_kv* kv, int32_t seq, int32_t layer, int32_t begin, int32_t count, const void* hk,
+                        const void* hv) {
+  return kv_copy(kv, seq, layer, begin, count, const_cast<void*>(hk), const_cast<void*>(hv), false);
+}
+
+// ---- decode -------------------------------------------------------------------
+qxc_status qxc_decode(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* a) {
+  if (!ctx || !kv || !a) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (kv->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "KV arena belongs to another context");
+  if (a->seq_count < 1 || !a->positions) return fail(ctx, QXC_ERR_INVALID_ARG, "seq_count >= 1 and positions required");
+  if (a->layer_count < 1 || a->layer_begin < 0 || a->layer_begin + a->layer_count > kv->desc.layers)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "layers [%d, %d) outside the arena's %d layers", a->layer_begin,
+                a->layer_begin + a->layer_count, kv->desc.layers);
+  if (!a->q || !a->k || !a->v || !a->out) return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
+  if (!valid_dtype(a->q_dtype) || !valid_dtype(a->in_dtype) || !valid_dtype(a->out_dtype))
+    return fail(ctx, QXC_ERR_INVALID_ARG, "unknown tensor dtype");
+  if (kv->desc.model == QXC_MODEL_QWEN3 && (a->q_dtype != kv->desc.key_dtype || a->in_dtype != kv->desc.key_dtype))
+    return fail(ctx, QXC_ERR_INVALID_ARG, "Qwen q/k/v must use the KV cache's 16-bit type");
+  if (kv->desc.first_position != 0)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "a KV-length shard decodes through qxc_decode_partials");
+  std::vector<int> attend(a->seq_count), new_slot(a->seq_count), rope(a->seq_count);
+  std::vector<char> seen(kv->desc.sequences, 0);
+  for (int i = 0; i < a->seq_count; ++i) {
+    const int seq = a->seq_ids ? a->seq_ids[i] : i;
+    qxc_status st = check_seq(ctx, kv, seq);
+    if (st != QXC_OK) return st;
+    if (seen[seq]) return fail(ctx, QXC_ERR_INVALID_ARG, "sequence %d appears twice in one call", seq);
+    seen[seq] = 1;
+    const int position = a->positions[i];
+    // KvCache::append (qx-runtime lib.rs:385-398)
+    if (position != kv->len[seq])
+      return fail(ctx, QXC_ERR_POSITION, "KV position %d does not follow cache length %d", position, kv->len[seq]);
+    if (position >= kv->desc.capacity)
+      return fail(ctx, QXC_ERR_POSITION, "KV position %d exceeds context %d", position, kv->desc.capacity);
+    attend[i] = position + 1;
+    new_slot[i] = position;
+    rope[i] = position;
+  }
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  CallPlan plan;
+  qxc_status st = plan_call(ctx, kv, a->seq_count, a->seq_ids, attend.data(), new_slot.data(), rope.data(),
+                            a->layer_count, a->split, &plan);
+  if (st != QXC_OK) return st;
+  DecodeParams p;
+  st = fill_params(ctx, kv, plan, a->layer_begin, a->layer_count, &p);
+  if (st != QXC_OK) return st;
+  p.q = a->q;
+  p.k = a->k;
+  p.v = a->v;
+  p.out = a->out;
+  p.q_rot_out = a->q_rot_out;
+  p.q_norm = a->q_norm;
+  p.k_norm = a->k_norm;
+  p.q_dtype = a->q_dtype;
+  p.in_dtype = a->in_dtype;
+  p.out_dtype = a->out_dtype;
+  p.pinned_exp = default_pinned(kv, a->flags) ? 1 : 0;
+  p.emit_partials = 0;
+  st = launch_decode(ctx, kv, p, plan.items);
+  if (st != QXC_OK) return st;
+  if (!(a->flags & QXC_DECODE_NO_ADVANCE))
+    for (int i = 0; i < a->seq_count; ++i) kv->len[a->seq_ids ? a->seq_ids[i] : i] += 1;
+  return QXC_OK;
+}
+
+static qxc_status stage_reserve(qxc_ctx* ctx, size_t bytes) {
+  if (bytes > ctx->stage_cap) {
+    QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    cudaFree(ctx->stage_dev);
+    ctx->stage_dev = nullptr;
+    ctx->stage_cap = 0;
+    QXC_CUDA(ctx, cudaMalloc(&ctx->stage_dev, bytes));
+    ctx->stage_cap = bytes;
+  }
+  if (bytes > ctx->stage_host_cap) {
+    if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
+    ctx->stage_host = nullptr;
+    ctx->stage_host_cap = 0;
+    QXC_CUDA(ctx, cudaMallocHost(&ctx->stage_host, bytes));
+    ctx->stage_host_cap = bytes;
+  }
+  return QXC_OK;
+}
+
+qxc_status qxc_decode_host(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* a) {
+  if (!ctx || !kv || !a) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (!a->q || !a->k || !a->v || !a->out) return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
+  const size_t units = (size_t)std::max(a->seq_count, 0) * std::max(a->layer_count, 0);
+  const size_t qb = units * kv->hq * kv->d * dtype_size(a->q_dtype);
+  const size_t kb = units * kv->hkv * kv->d * dtype_size(a->in_dtype);
+  const size_t ob = units * kv->hq * kv->d * dtype_size(a->out_dtype);
+  const size_t rb = a->q_rot_out ? units * kv->hq * kv->d * 4 : 0;
+  auto al = [](size_t x) { return ((x + 255) / 256) * 256; };
+  const size_t off_k = al(qb), off_v = off_k + al(kb), off_o = off_v + al(kb), off_r = off_o + al(ob);
+  const size_t total = off_r + al(rb);
+  qxc_status st = stage_reserve(ctx, total);
+  if (st != QXC_OK) return st;
+  // one pinned staging buffer -> one host-to-device copy for q, k and v
+  memcpy(ctx->stage_host, a->q, qb);
+  memcpy(ctx->stage_host + off_k, a->k, kb);
+  memcpy(ctx->stage_host + off_v, a->v, kb);
+  QXC_CUDA(ctx, cudaMemcpyAsync(ctx->stage_dev, ctx->stage_host, off_o, cudaMemcpyHostToDevice, ctx->stream));
+  qxc_decode_args d = *a;
+  d.q = ctx->stage_dev;
+  d.k = ctx->stage_dev + off_k;
+  d.v = ctx->stage_dev + off_v;
+  d.out = ctx->stage_dev + off_o;
+  d.q_rot_out = a->q_rot_out ? reinterpret_cast<float*>(ctx->stage_dev + off_r) : nullptr;
+  st = qxc_decode(ctx, kv, &d);
+  if (st != QXC_OK) return st;
+  QXC_CUDA(ctx, cudaMemcpyAsync(ctx->stage_host + off_o, ctx->stage_dev + off_o, total - off_o,
+                                cudaMemcpyDeviceToHost, ctx->stream));
+  st = qxc_sync(ctx);
+  if (st != QXC_OK) return st;
+  memcpy(a->out, ctx->stage_host + off_o, ob);
+  if (a->q_rot_out) memcpy(a->q_rot_out, ctx->stage_host + off_r, rb);
+  return QXC_OK;
+}
+
+qxc_status qxc_granite_attention_decode(qxc_ctx* ctx, qxc_kv* kv, const float* q, const float* k, const float* v,
+                                        int32_t position, float* out) {
+  if (!kv) return fail(ctx, QXC_ERR_INVALID_ARG, "null KV cache");
+  if (kv->desc.model != QXC_MODEL_GRANITE) return fail(ctx, QXC_ERR_INVALID_ARG, "not a Granite KV arena");
+  qxc_decode_args a;
+  memset(&a, 0, sizeof(a));
+  const int32_t pos = position;
+  a.layer_begin = 0;
+  a.layer_count = 1;
+  a.seq_count = 1;
+  a.positions = &pos;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.out = out;
+  a.q_dtype = a.in_dtype = a.out_dtype = QXC_F32;
+  return qxc_decode_host(ctx, kv, &a);
+}
+
+qxc_status qxc_apply_granite_rope(qxc_ctx* ctx, float* q, float* k, int32_t position) {
+  if (!ctx || !q || !k) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (position < 0) return fail(ctx, QXC_ERR_INVALID_ARG, "negative position");
+  qxc_status st = stage_reserve(ctx, 1536 * sizeof(float));
+  if (st != QXC_OK) return st;
+  float* h = reinterpret_cast<float*>(ctx->stage_host);
+  memcpy(h, q, 1024 * sizeof(float));
+  memcpy(h + 1024, k, 512 * sizeof(float));
+  float* dq = reinterpret_cast<float*>(ctx->stage_dev);
+  QXC_CUDA(ctx, cudaMemcpyAsync(dq, h, 1536 * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+  qx_granite_rope_kernel<<<6, 128, 0, ctx->stream>>>(dq, dq + 1024, position, ctx->err_dev);
+  QXC_CUDA(ctx, cudaGetLastError());
+  ctx->launches++;
+  QXC_CUDA(ctx, cudaMemcpyAsync(h, dq, 1536 * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+  st = qxc_sync(ctx);
+  if (st != QXC_OK) return st;
+  memcpy(q, h, 1024 * sizeof(float));
+  memcpy(k, h + 1024, 512 * sizeof(float));
+  return QXC_OK;
+}
+
+// ---- KV-length split ---------------------------------------------------------
+qxc_status qxc_decode_partials(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args* a) {
+  if (!ctx || !kv || !a) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (kv->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "KV arena belongs to another context");
+  qxc_status st = check_seq(ctx, kv, a->seq);
+  if (st != QXC_OK) return st;
+  if (a->layer < 0 || a->layer >= kv->desc.layers) return fail(ctx, QXC_ERR_INVALID_ARG, "layer %d out of range", a->layer);
+  if (!a->q || !a->partials || (a->append && (!a->k || !a->v)))
+    return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
+  if (kv->desc.model == QXC_MODEL_QWEN3 && (a->q_dtype != kv->desc.key_dtype || (a->append && a->in_dtype != kv->desc.key_dtype)))
+    return fail(ctx, QXC_ERR_INVALID_ARG, "Qwen q/k/v must use the KV cache's 16-bit type");
+  const int first = kv->desc.first_position;
+  const int len = kv->len[a->seq];
+  int attend, new_slot;
+  if (a->append) {
+    const int local = a->position - first;
+    if (local != len)
+      return fail(ctx, QXC_ERR_POSITION, "KV position %d does not follow cache length %d", a->position, first + len);
+    if (local >= kv->desc.capacity)
+      return fail(ctx, QXC_ERR_POSITION, "KV position %d exceeds context %d", a->position, first + kv->desc.capacity);
+    attend = local + 1;
+    new_slot = local;
+  } else {
+    if (len < 1) return fail(ctx, QXC_ERR_INVALID_ARG, "a shard without the new token needs cached rows");
+    if (a->position < first + len)
+      return fail(ctx, QXC_ERR_POSITION, "position %d precedes this shard's slots", a->position);
+    attend = len;
+    new_slot = -1;
+  }
+  if (kv->desc.model == QXC_MODEL_GRANITE && a->position >= 4096)
+    return fail(ctx, QXC_ERR_POSITION, "KV position %d exceeds context 4096", a->position);
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  CallPlan plan;
+  const int seq = a->seq, rope = a->position;
+  st = plan_call(ctx, kv, 1, &seq, &attend, &new_slot, &rope, 1, a->split, &plan);
+  if (st != QXC_OK) return st;
+  DecodeParams p;
+  st = fill_params(ctx, kv, plan, a->layer, 1, &p);
+  if (st != QXC_OK) return st;
+  p.q = a->q;
+  p.k = a->k ? a->k : a->q;
+  p.v = a->v ? a->v : a->q;
+  p.out = a->partials;
+  p.q_norm = a->q_norm;
+  p.k_norm = a->k_norm;
+  p.q_dtype = a->q_dtype;
+  p.in_dtype = a->in_dtype;
+  p.out_dtype = QXC_F32;
+  p.pinned_exp = default_pinned(kv, a->flags) ? 1 : 0;
+  p.emit_partials = 1;
+  st = launch_decode(ctx, kv, p, plan.items);
+  if (st != QXC_OK) return st;
+  if (a->append) kv->len[a->seq] += 1;
+  return QXC_OK;
+}
+
+qxc_status qxc_lse_merge(qxc_ctx* ctx, int32_t model, int32_t n_parts, const float* partials, void* out,
+                         int32_t out_dtype) {
+  if (!ctx || !partials || !out || n_parts < 1) return fail(ctx, QXC_ERR_INVALID_ARG, "invalid merge arguments");
+  if (!valid_dtype(out_dtype)) return fail(ctx, QXC_ERR_INVALID_ARG, "unknown dtype");
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  const int pinned = model == QXC_MODEL_GRANITE ? 1 : 0;
+  if (model == QXC_MODEL_QWEN3)
+    qx_lse_merge_kernel<32, 128><<<32, 128, 0, ctx->stream>>>(partials, n_parts, out, out_dtype, pinned, ctx->err_dev);
+  else if (model == QXC_MODEL_GRANITE)
+    qx_lse_merge_kernel<16, 64><<<16, 64, 0, ctx->stream>>>(partials, n_parts, out, out_dtype, pinned, ctx->err_dev);
+  else
+    return fail(ctx, QXC_ERR_INVALID_ARG, "unknown model %d", model);
+  QXC_CUDA(ctx, cudaGetLastError());
+  ctx->launches++;
+  return QXC_OK;
+}
+
+// ---- prefill -------------------------------------------------------------------
+qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
+  if (!ctx || !kv || !a) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (kv->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "KV arena belongs to another context");
+  if (kv->desc.model != QXC_MODEL_GRANITE) return fail(ctx, QXC_ERR_UNSUPPORTED, "prefill supports Granite only");
+  if (kv->desc.key_dtype != QXC_BF16 || kv->desc.value_dtype != QXC_BF16)
+    return fail(ctx, QXC_ERR_UNSUPPORTED, "prefill requires a bf16 KV arena");
+  if (a->in_dtype != QXC_BF16) return fail(ctx, QXC_ERR_UNSUPPORTED, "prefill inputs must be bf16");
+  if (a->out_dtype != QXC_F32 && a->out_dtype != QXC_BF16)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "prefill output must be f32 or bf16");
+  qxc_status st = check_seq(ctx, kv, a->seq);
+  if (st != QXC_OK) return st;
+  if (a->layer < 0 || a->layer >= kv->desc.layers) return fail(ctx, QXC_ERR_INVALID_ARG, "layer %d out of range", a->layer);
+  if (!a->q || !a->k || !a->v || !a->out) return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
+  if (kv->len[a->seq] != 0)
+    return fail(ctx, QXC_ERR_POSITION, "KV position 0 does not follow cache length %d", kv->len[a->seq]);
+  if (a->length < 1 || a->length > kv->desc.capacity)
+    return fail(ctx, QXC_ERR_POSITION, "KV position %d exceeds context %d", a->length - 1, kv->desc.capacity);
+  if (kv->desc.first_position != 0) return fail(ctx, QXC_ERR_INVALID_ARG, "prefill needs an unsharded arena");
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  void *kc, *vc;
+  kv_view(kv, a->seq, a->layer, true, &kc, nullptr);
+  kv_view(kv, a->seq, a->layer, false, &vc, nullptr);
+  PrefillParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = static_cast<const __nv_bfloat16*>(a->q);
+  p.k = static_cast<const __nv_bfloat16*>(a->k);
+  p.v = static_cast<const __nv_bfloat16*>(a->v);
+  p.k_cache = static_cast<__nv_bfloat16*>(kc);
+  p.v_cache = static_cast<__nv_bfloat16*>(vc);
+  p.out = a->out;
+  p.out_dtype = a->out_dtype;
+  p.length = a->length;
+  p.pinned_exp = (a->flags & QXC_DECODE_NATIVE_EXP) ? 0 : 1;
+  p.err = ctx->err_dev;
+  int launches = 0;
+  cudaError_t e = launch_prefill(p, ctx->stream, &launches);
+  if (e != cudaSuccess) return fail(ctx, QXC_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e));
+  ctx->launches += launches;
+  if (!(a->flags & QXC_DECODE_NO_ADVANCE)) kv->len[a->seq] = a->length;
+  return QXC_OK;
+}
+
+}  // extern "C"

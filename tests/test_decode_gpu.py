@@ -1,0 +1,364 @@
+"""GPU parity of the split-KV decode against the CPU oracle.
+
+Gates: KV-cache rows and cursors bit-exact; outputs
+within normwise relative error 1e-5 for fp32 KV and 2e-2 for 16-bit KV,
+normwise = max|gpu - oracle| / max|oracle|.
+"""
+import numpy as np
+import pytest
+
+from helpers import as_kv, granite_inputs, normwise
+from qx_b200 import BF16, F16, F32, MODEL_GRANITE, MODEL_QWEN3, KvArena, KvCache, QxError
+from qx_b200 import _lib
+from qx_b200 import granite_attention_decode as gpu_decode
+from qx_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+TOL = {F32: 1e-5, BF16: 2e-2, F16: 2e-2}
+
+
+def oracle_cache(oracle, capacity, kd, vd, kc, vc):
+    c = oracle.KvCache(capacity, kd, vd)
+    n = kc.shape[0]
+    c.keys[:n] = as_kv(kc, kd)
+    c.values[:n] = as_kv(vc, vd)
+    c.length.value = n
+    return c
+
+
+def gpu_arena(ctx, capacity, kd, vd, kc, vc, layers=1, sequences=1):
+    a = KvArena(ctx, MODEL_GRANITE, layers, sequences, capacity, kd, vd)
+    n = kc.shape[0]
+    if n:
+        for s in range(sequences):
+            for l in range(layers):
+                a.write(s, l, 0, as_kv(kc, kd), as_kv(vc, vd))
+            a.set_len(s, n)
+    return a
+
+
+def test_config0_granite_single_layer(gpu_ctx, oracle):
+    """one Granite layer, fp32, cache of 511 + new token at 511."""
+    q, k, v, kc, vc = granite_inputs(syn.seed_for(0), 511, 512)
+    oc = oracle_cache(oracle, 512, F32, F32, kc, vc)
+    st, ref = oracle.granite_attention_decode(q, k, v, 511, oc)
+    assert st == 0
+    arena = gpu_arena(gpu_ctx, 512, F32, F32, kc, vc)
+    out = arena.decode_host(q[None], k[None], v[None], [511])[0]
+    assert normwise(out, ref) <= 1e-5
+    assert arena.len(0) == 512
+    gk, gv = arena.read(0, 0, 0, 512)
+    assert np.array_equal(gk.view(np.uint32), oc.keys.view(np.uint32))
+    assert np.array_equal(gv.view(np.uint32), oc.values.view(np.uint32))
+
+
+@pytest.mark.parametrize("length", [1, 2, 31, 32, 33, 63, 64, 65, 127, 128, 129, 511, 512, 513, 1000, 4096])
+@pytest.mark.parametrize("split", [0, 64])
+def test_edge_lengths_fp32(gpu_ctx, oracle, length, split):
+    cap = max(length, 64)
+    q, k, v, kc, vc = granite_inputs(0x1000 + length, length - 1, cap)
+    oc = oracle_cache(oracle, cap, F32, F32, kc, vc)
+    st, ref = oracle.granite_attention_decode(q, k, v, length - 1, oc)
+    assert st == 0
+    arena = gpu_arena(gpu_ctx, cap, F32, F32, kc, vc)
+    out = arena.decode_host(q[None], k[None], v[None], [length - 1], split=split)[0]
+    assert normwise(out, ref) <= 1e-5, (length, split)
+    gk, gv = arena.read(0, 0, length - 1, 1)
+    assert np.array_equal(gk.reshape(-1).view(np.uint32), oc.keys[length - 1].reshape(-1).view(np.uint32))
+    assert np.array_equal(gv.reshape(-1).view(np.uint32), oc.values[length - 1].reshape(-1).view(np.uint32))
+
+
+@pytest.mark.parametrize("kd,vd", [(F32, F16), (F16, F32), (F16, F16), (BF16, BF16)])
+def test_kv_precisions(gpu_ctx, oracle, kd, vd):
+    L = 777
+    q, k, v, kc, vc = granite_inputs(0x2000 + kd * 4 + vd, L - 1, 1024)
+    oc = oracle_cache(oracle, 1024, kd, vd, kc, vc)
+    st, ref = oracle.granite_attention_decode(q, k, v, L - 1, oc)
+    assert st == 0
+    arena = gpu_arena(gpu_ctx, 1024, kd, vd, kc, vc)
+    out = arena.decode_host(q[None], k[None], v[None], [L - 1], split=128)[0]
+    assert normwise(out, ref) <= max(TOL[kd], TOL[vd])
+    gk, gv = arena.read(0, 0, 0, L)
+    assert np.array_equal(gk, oc.keys[:L]) and np.array_equal(gv, oc.values[:L])
+
+
+def test_sequential_steps_keep_cache_bit_exact(gpu_ctx, oracle):
+    """Eight consecutive appends through the V1 mirror (KvCache / granite_attention_decode)."""
+    cache = KvCache(64, gpu_ctx)
+    oc = oracle.KvCache(64)
+    for step in range(8):
+        q = syn.normal(900 + step, (1024,))
+        k = syn.normal(1900 + step, (512,))
+        v = syn.normal(2900 + step, (512,))
+        out = gpu_decode(q, k, v, step, cache)
+        st, ref = oracle.granite_attention_decode(q, k, v, step, oc)
+        assert st == 0 and normwise(out, ref) <= 1e-5
+        assert len(cache) == step + 1
+    gk, gv = cache.arena.read(0, 0, 0, 8)
+    assert np.array_equal(gk, oc.keys[:8]) and np.array_equal(gv, oc.values[:8])
+    kt, vt = cache.token(3)
+    assert np.array_equal(kt, oc.keys[3].reshape(-1))
+
+
+def test_grouped_query_attention_uses_the_matching_kv_head(gpu_ctx):
+    # qx-runtime lib.rs:2873-2893 on the GPU path
+    cache = KvCache(4, gpu_ctx)
+    q = np.zeros(1024, np.float32)
+    k = np.zeros(512, np.float32)
+    v = np.zeros(512, np.float32)
+    for h in range(8):
+        v[h * 64:(h + 1) * 64] = h + 1
+    out = gpu_decode(q, k, v, 0, cache)
+    assert len(cache) == 1
+    for qh in range(16):
+        assert np.all(out[qh * 64:(qh + 1) * 64] == qh // 2 + 1)
+
+
+def test_kv_cache_rejects_non_sequential_positions(gpu_ctx):
+    # qx-runtime lib.rs:2895-2902: Err, cache untouched
+    cache = KvCache(2, gpu_ctx)
+    z = np.zeros(1024, np.float32)
+    with pytest.raises(QxError) as e:
+        gpu_decode(z, z[:512], z[:512], 1, cache)
+    assert e.value.status == _lib.ERR_POSITION
+    assert str(e.value) == "KV position 1 does not follow cache length 0"
+    assert len(cache) == 0
+
+
+def test_kv_cache_rejects_position_beyond_capacity(gpu_ctx):
+    cache = KvCache(1, gpu_ctx)
+    z = np.zeros(1024, np.float32)
+    gpu_decode(z, z[:512], z[:512], 0, cache)
+    with pytest.raises(QxError) as e:
+        gpu_decode(z, z[:512], z[:512], 1, cache)
+    assert str(e.value) == "KV position 1 exceeds context 1"
+
+
+def test_nonfinite_input_is_reported_at_sync(gpu_ctx):
+    cache = KvCache(4, gpu_ctx)
+    q = np.zeros(1024, np.float32)
+    q[5] = np.inf
+    z = np.zeros(512, np.float32)
+    with pytest.raises(QxError) as e:
+        gpu_decode(q, z, z, 0, cache)
+    assert e.value.status == _lib.ERR_NONFINITE
+    # the context stays usable after the reported error
+    cache.reset()
+    out = gpu_decode(np.zeros(1024, np.float32), z, z, 0, cache)
+    assert np.all(out == 0)
+
+
+def test_apply_granite_rope_bit_exact(gpu_ctx, oracle):
+    from qx_b200 import apply_granite_rope
+    for position in (0, 1, 511, 4095):
+        q = syn.normal(position + 7, (1024,))
+        k = syn.normal(position + 8, (512,))
+        rq, rk = q.copy(), k.copy()
+        assert oracle.lib().qxo_rotate_heads(oracle._fp(rq), 16, position) == 0
+        assert oracle.lib().qxo_rotate_heads(oracle._fp(rk), 8, position) == 0
+        apply_granite_rope(q, k, position, gpu_ctx)
+        assert np.array_equal(q.view(np.uint32), rq.view(np.uint32))
+        assert np.array_equal(k.view(np.uint32), rk.view(np.uint32))
+
+
+def test_stack_24_layers_one_launch(gpu_ctx, oracle):
+    """BASELINE config 1 shape (24 independent layers), small context, 3 steps."""
+    import torch
+    L0, steps, cap = 300, 3, 512
+    layers = 24
+    arena = KvArena(gpu_ctx, MODEL_GRANITE, layers, 1, cap, F32, F32)
+    ocs = []
+    for l in range(layers):
+        _, _, _, kc, vc = granite_inputs(syn.seed_for(1, l), L0, cap)
+        arena.write(0, l, 0, kc, vc)
+        ocs.append(oracle_cache(oracle, cap, F32, F32, kc, vc))
+    arena.set_len(0, L0)
+    for step in range(steps):
+        pos = L0 + step
+        qs = [syn.normal(syn.seed_for(1, l) + 7 * pos, (1024,)) for l in range(layers)]
+        ks = [syn.normal(syn.seed_for(1, l) + 7 * pos + 1, (512,)) for l in range(layers)]
+        vs = [syn.normal(syn.seed_for(1, l) + 7 * pos + 2, (512,)) for l in range(layers)]
+        q = torch.from_numpy(np.stack(qs)).cuda()
+        k = torch.from_numpy(np.stack(ks)).cuda()
+        v = torch.from_numpy(np.stack(vs)).cuda()
+        out = torch.zeros(layers, 1024, device="cuda")
+        before = gpu_ctx.launch_count
+        arena.decode(q, k, v, out, [pos], 0, layers)
+        gpu_ctx.sync()
+        assert gpu_ctx.launch_count - before == 1
+        worst, refs = oracle.granite_decode_many(qs, ks, vs, [pos] * layers, ocs, threads=4)
+        assert worst == 0
+        got = out.cpu().numpy()
+        for l in range(layers):
+            assert normwise(got[l], refs[l]) <= 1e-5, (step, l)
+    assert arena.len(0) == L0 + steps
+    for l in (0, 11, 23):
+        gk, gv = arena.read(0, l, 0, L0 + steps)
+        assert np.array_equal(gk, ocs[l].keys[:L0 + steps]) and np.array_equal(gv, ocs[l].values[:L0 + steps])
+
+
+def test_multi_sequence_ragged_bf16(gpu_ctx, oracle):
+    """BASELINE config 4 shape: independent sequences of different lengths, bf16 KV."""
+    import torch
+    n_seq, layers, cap = 9, 3, 600
+    lengths = [1, 2, 63, 64, 65, 200, 333, 512, 599]
+    arena = KvArena(gpu_ctx, MODEL_GRANITE, layers, n_seq, cap, BF16, BF16)
+    ocs, qs, ks, vs = [], [], [], []
+    for s, L in enumerate(lengths):
+        for l in range(layers):
+            q, k, v, kc, vc = granite_inputs(0x4000 + 31 * s + l, L - 1, cap)
+            arena.write(s, l, 0, as_kv(kc, BF16), as_kv(vc, BF16))
+            ocs.append(oracle_cache(oracle, cap, BF16, BF16, kc, vc))
+            qs.append(q), ks.append(k), vs.append(v)
+        arena.set_len(s, L - 1)
+    order = list(range(n_seq))[::-1]  # seq_ids in a non-trivial order
+    pack = lambda xs: torch.from_numpy(np.stack([xs[s * layers + l] for s in order for l in range(layers)])).cuda()
+    out = torch.zeros(n_seq * layers, 1024, device="cuda")
+    arena.decode(pack(qs), pack(ks), pack(vs), out, [lengths[s] - 1 for s in order], 0, layers, seq_ids=order,
+                 split=64)
+    gpu_ctx.sync()
+    worst, refs = oracle.granite_decode_many(qs, ks, vs, [lengths[u // layers] - 1 for u in range(n_seq * layers)],
+                                             ocs, threads=4)
+    assert worst == 0
+    got = out.cpu().numpy()
+    for i, s in enumerate(order):
+        for l in range(layers):
+            assert normwise(got[i * layers + l], refs[s * layers + l]) <= 2e-2
+            assert normwise(got[i * layers + l], refs[s * layers + l]) <= 5e-3
+    for s in (0, 8):
+        gk, gv = arena.read(s, 1, 0, lengths[s])
+        assert np.array_equal(gk, ocs[s * layers + 1].keys[:lengths[s]])
+        assert arena.len(s) == lengths[s]
+
+
+def test_speculative_cursor(gpu_ctx):
+    """checkpoint / rollback / commit (qx-runtime-v2 lib.rs:3265-3310): cursor only, no copies."""
+    arena = KvArena(gpu_ctx, MODEL_GRANITE, 1, 1, 16, F32, F32)
+    z = np.zeros((1, 1024), np.float32)
+    zk = np.zeros((1, 512), np.float32)
+    for p in range(3):
+        arena.decode_host(z, zk, zk, [p])
+    cp = arena.checkpoint(0)
+    assert cp == 3
+    for p in range(3, 6):
+        arena.decode_host(z, zk, zk, [p])
+    arena.rollback(0, cp)
+    assert arena.len(0) == 3
+    with pytest.raises(QxError):
+        arena.rollback(0, 4)
+    for p in range(3, 6):
+        arena.decode_host(z, zk, zk, [p])
+    arena.rollback(0, cp)
+    with pytest.raises(QxError):
+        arena.commit(0, cp, 1)  # beyond the current speculative range (position 3)
+    for p in range(3, 5):
+        arena.decode_host(z, zk, zk, [p])
+    arena.commit(0, cp, 1)
+    assert arena.len(0) == 4
+
+
+# ---- Qwen3 ------------------------------------------------------------------------
+def qwen_case(seed, prefix, cap, dtype=BF16):
+    conv = syn.to_bf16_bits if dtype == BF16 else syn.to_f16_bits
+    q = conv(syn.normal(seed, (32, 128)))
+    k = conv(syn.normal(seed + 1, (4, 128)))
+    v = conv(syn.normal(seed + 2, (4, 128)))
+    kc = np.zeros((cap, 4, 128), np.uint16)
+    vc = np.zeros((cap, 4, 128), np.uint16)
+    kc[:prefix] = conv(syn.normal(seed + 3, (prefix, 4, 128)))
+    vc[:prefix] = conv(syn.normal(seed + 4, (prefix, 4, 128)))
+    return q, k, v, kc, vc
+
+
+@pytest.mark.parametrize("prefix,dtype", [(0, BF16), (5, BF16), (700, BF16), (4095, BF16), (1000, F16)])
+def test_qwen_decode(gpu_ctx, oracle, prefix, dtype):
+    import torch
+    cap = prefix + 8
+    q, k, v, kc, vc = qwen_case(0x3000 + prefix, prefix, cap, dtype)
+    qn = (1.0 + 0.1 * syn.normal(77, (128,))).astype(np.float32)
+    kn = (1.0 + 0.1 * syn.normal(78, (128,))).astype(np.float32)
+    okc, ovc = kc.copy(), vc.copy()
+    qr, kr, ref, _ = oracle.qwen_decode(q, k, v, qn, kn, okc, ovc, prefix, dtype, threads=4)
+    arena = KvArena(gpu_ctx, MODEL_QWEN3, 1, 1, cap, dtype, dtype)
+    if prefix:
+        arena.write(0, 0, 0, kc[:prefix], vc[:prefix])
+        arena.set_len(0, prefix)
+    tq = torch.from_numpy(q.view(np.int16).reshape(1, -1)).cuda()
+    tk = torch.from_numpy(k.view(np.int16).reshape(1, -1)).cuda()
+    tv = torch.from_numpy(v.view(np.int16).reshape(1, -1)).cuda()
+    out = torch.zeros(1, 4096, device="cuda")
+    qrot = torch.zeros(1, 4096, device="cuda")
+    arena.decode(tq, tk, tv, out, [prefix], q_rot_out=qrot, q_norm=torch.from_numpy(qn).cuda(),
+                 k_norm=torch.from_numpy(kn).cuda(), split=64 if prefix > 100 else 0)
+    gpu_ctx.sync()
+    got = out.cpu().numpy()[0]
+    assert normwise(got, ref) <= 2e-2
+    assert normwise(got, ref) <= 2e-3  # observed margin: q/k/v identical, only summation order differs
+    gk, gv = arena.read(0, 0, prefix, 1)
+    assert np.array_equal(gk.reshape(-1), kr), "rotated key row must be bit-exact"
+    assert np.array_equal(gv.reshape(-1), v.reshape(-1))
+    conv = syn.to_bf16_bits if dtype == BF16 else syn.to_f16_bits
+    assert np.array_equal(conv(qrot.cpu().numpy()[0]), qr), "rotated query must match the reference rounding"
+
+
+def test_qwen_config3_full_length(gpu_ctx, oracle):
+    """BASELINE config 3 at full size: KV length 32768 (32767 cached + new token)."""
+    import torch
+    prefix, cap = 32767, 32768
+    q, k, v, kc, vc = qwen_case(syn.seed_for(3), prefix, cap)
+    ones = np.ones(128, np.float32)
+    okc, ovc = kc.copy(), vc.copy()
+    qr, kr, ref, _ = oracle.qwen_decode(q, k, v, ones, ones, okc, ovc, prefix, BF16, threads=8)
+    arena = KvArena(gpu_ctx, MODEL_QWEN3, 1, 1, cap, BF16, BF16)
+    arena.write(0, 0, 0, kc[:prefix], vc[:prefix])
+    arena.set_len(0, prefix)
+    dev = lambda a: torch.from_numpy(a.view(np.int16).reshape(1, -1)).cuda()
+    out = torch.zeros(1, 4096, device="cuda")
+    arena.decode(dev(q), dev(k), dev(v), out, [prefix])
+    gpu_ctx.sync()
+    assert normwise(out.cpu().numpy()[0], ref) <= 2e-2
+    gk, _ = arena.read(0, 0, prefix, 1)
+    assert np.array_equal(gk.reshape(-1), kr)
+
+
+# ---- KV-length split partials + LSE merge ---------------------------------------------
+@pytest.mark.parametrize("model", [MODEL_GRANITE, MODEL_QWEN3])
+@pytest.mark.parametrize("shards", [2, 3])
+def test_partials_merge_equals_whole(gpu_ctx, model, shards):
+    import torch
+    if model == MODEL_GRANITE:
+        L, dt, hq, d = 1500, F32, 16, 64
+        q, k, v, kc, vc = granite_inputs(0x5000, L - 1, L)
+        kc_s, vc_s = kc, vc
+        dev = lambda a: torch.from_numpy(a.reshape(1, -1)).cuda()
+        tol = 1e-5
+    else:
+        L, dt, hq, d = 3000, BF16, 32, 128
+        q, k, v, kc, vc = qwen_case(0x6000, L - 1, L)
+        kc_s, vc_s = kc[:L - 1], vc[:L - 1]
+        dev = lambda a: torch.from_numpy(a.view(np.int16).reshape(1, -1)).cuda()
+        tol = 2e-3
+    whole = KvArena(gpu_ctx, model, 1, 1, L, dt, dt)
+    whole.write(0, 0, 0, kc_s, vc_s)
+    whole.set_len(0, L - 1)
+    out = torch.zeros(1, hq * d, device="cuda")
+    whole.decode(dev(q), dev(k), dev(v), out, [L - 1])
+    bounds = [round(i * L / shards) for i in range(shards + 1)]
+    parts = torch.zeros(shards, hq, d + 2, device="cuda")
+    arenas = []
+    for i in range(shards):
+        b, e = bounds[i], bounds[i + 1]
+        a = KvArena(gpu_ctx, model, 1, 1, e - b, dt, dt, first_position=b)
+        n_cached = min(e, L - 1) - b
+        a.write(0, 0, 0, kc_s[b:b + n_cached], vc_s[b:b + n_cached])
+        a.set_len(0, n_cached)
+        a.decode_partials(dev(q), dev(k), dev(v), parts[i], L - 1, append=(i == shards - 1), split=128)
+        arenas.append(a)
+    merged = torch.zeros(hq * d, device="cuda")
+    gpu_ctx.lse_merge(model, shards, parts, merged)
+    gpu_ctx.sync()
+    assert normwise(merged.cpu().numpy(), out.cpu().numpy()[0]) <= tol
+    gk, _ = arenas[-1].read(0, 0, arenas[-1].len(0) - 1, 1)
+    wk, _ = whole.read(0, 0, L - 1, 1)
+    assert np.array_equal(gk, wk)

@@ -1,0 +1,166 @@
+"""CPU tests of the oracle against the reference's own known answers
+(crates/qx-consensus-math/src/lib.rs:213-330, crates/qx-runtime/src/lib.rs:2873-2902)."""
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+KATS = json.load(open(os.path.join(HERE, "golden", "consensus_math_kats.json")))
+
+
+def bits(f: float) -> int:
+    return struct.unpack("<I", struct.pack("<f", f))[0]
+
+
+def test_inverse_frequency_table(oracle):
+    lib = oracle.lib()
+    assert [lib.qxo_granite_inverse_frequency_bits(i) for i in range(32)] == KATS["granite_inverse_frequency_bits"]
+
+
+def test_exp_golden_bits(oracle):
+    got = [bits(oracle.exp_f32(x)) for x in KATS["exp"]["inputs"]]
+    assert got == KATS["exp"]["bits"]
+
+
+def test_rsqrt_golden_bits(oracle):
+    got = [bits(oracle.rsqrt_f32(x)) for x in KATS["rsqrt"]["inputs"]]
+    assert got == KATS["rsqrt"]["bits"]
+
+
+def test_rope_sin_cos_golden_bits(oracle):
+    for case in KATS["granite_rope_sin_cos"]:
+        s, c = oracle.granite_rope_sin_cos(case["position"], case["pair"])
+        assert (bits(s), bits(c)) == (case["sine_bits"], case["cosine_bits"])
+
+
+def test_error_bounds(oracle):
+    lib = oracle.lib()
+    b = KATS["error_bounds"]
+    assert lib.qxo_exp_worst_relative_error() <= b["exp_worst_relative"]
+    assert lib.qxo_rsqrt_worst_relative_error() <= b["rsqrt_worst_relative"]
+    assert lib.qxo_rope_worst_absolute_error() <= b["rope_worst_absolute"]
+
+
+def test_special_values(oracle):
+    # special_values_are_rejected_or_clamped (qx-consensus-math lib.rs:256-264)
+    assert oracle.exp_f32(-100.0) == 0.0
+    assert oracle.exp_f32(100.0) == np.finfo(np.float32).max
+    assert oracle.exp_f32(float("nan")) is None
+    assert oracle.rsqrt_f32(0.0) is None
+    assert oracle.rsqrt_f32(-1.0) is None
+    assert oracle.granite_rope_sin_cos(5000, 0) is None  # angle > 4096
+
+
+def test_reduce_simd32_order(oracle):
+    lanes = np.array([1e8] + [1.0] * 31, np.float32)
+    # the tree order (16,8,4,2,1) differs from a sequential sum here
+    t = lanes.astype(np.float32).copy()
+    for off in (16, 8, 4, 2, 1):
+        t[:off] = t[:off] + t[off:2 * off]
+    assert oracle.reduce_simd32(lanes) == t[0]
+
+
+def test_grouped_query_attention_uses_the_matching_kv_head(oracle):
+    cache = oracle.KvCache(4)
+    q = np.zeros(1024, np.float32)
+    k = np.zeros(512, np.float32)
+    v = np.zeros(512, np.float32)
+    for h in range(8):
+        v[h * 64:(h + 1) * 64] = h + 1
+    st, out = oracle.granite_attention_decode(q, k, v, 0, cache)
+    assert st == oracle.OK and len(cache) == 1
+    for qh in range(16):
+        assert np.all(out[qh * 64:(qh + 1) * 64] == qh // 2 + 1)
+
+
+def test_kv_cache_rejects_non_sequential_positions(oracle):
+    cache = oracle.KvCache(2)
+    z = np.zeros(1024, np.float32)
+    st, _ = oracle.granite_attention_decode(z, z[:512], z[:512], 1, cache)
+    assert st == oracle.ERR_POSITION and len(cache) == 0
+
+
+def test_kv_cache_rejects_full_cache(oracle):
+    cache = oracle.KvCache(1)
+    z = np.zeros(1024, np.float32)
+    assert oracle.granite_attention_decode(z, z[:512], z[:512], 0, cache)[0] == oracle.OK
+    assert oracle.granite_attention_decode(z, z[:512], z[:512], 1, cache)[0] == oracle.ERR_POSITION
+
+
+def test_hierarchical_matches_plain_closely(oracle):
+    from helpers import granite_inputs, normwise
+    q, k, v, kc, vc = granite_inputs(0x51580000, 300, 512)
+    outs = []
+    for hier in (False, True):
+        c = oracle.KvCache(512)
+        c.keys[:300], c.values[:300] = kc, vc
+        c.length.value = 300
+        st, o = oracle.granite_attention_decode(q, k, v, 300, c, hierarchical=hier)
+        assert st == 0
+        outs.append(o)
+    assert normwise(outs[1], outs[0]) < 1e-5
+
+
+def test_hierarchical_rejects_beyond_512(oracle):
+    q, k, v = (np.zeros(n, np.float32) for n in (1024, 512, 512))
+    c = oracle.KvCache(600)
+    c.length.value = 512
+    st, _ = oracle.granite_attention_decode(q, k, v, 512, c, hierarchical=True)
+    assert st == oracle.ERR_INVALID_ARG  # the reference slices partials[..17] and panics
+
+
+def test_prefill_equals_iterated_decode(oracle):
+    from qx_b200 import synthetic as syn
+    L = 70
+    q = syn.to_bf16_bits(syn.normal(1, (L, 16, 64), 0.5))
+    k = syn.to_bf16_bits(syn.normal(2, (L, 8, 64), 0.5))
+    v = syn.to_bf16_bits(syn.normal(3, (L, 8, 64), 0.5))
+    st, kc, vc, out = oracle.granite_prefill(q, k, v, oracle.BF16, oracle.BF16, threads=4)
+    assert st == 0
+    cache = oracle.KvCache(L, oracle.BF16, oracle.BF16)
+    for p in range(L):
+        st, o = oracle.granite_attention_decode(syn.bf16_bits_to_f32(q[p]), syn.bf16_bits_to_f32(k[p]),
+                                                syn.bf16_bits_to_f32(v[p]), p, cache)
+        assert st == 0
+        assert np.array_equal(o, out[p].reshape(-1))
+    assert np.array_equal(cache.keys, kc) and np.array_equal(cache.values, vc)
+
+
+def test_qwen_oracle_f16_matches_written_reference_shape(oracle):
+    from qx_b200 import synthetic as syn
+    q = syn.to_f16_bits(syn.normal(5, (32, 128)))
+    k = syn.to_f16_bits(syn.normal(6, (4, 128)))
+    ones = np.ones(128, np.float32)
+    qo, ko = oracle.qwen_qk_norm_rope(q, k, ones, ones, 37, oracle.F16)
+    # RMS-normalised rows have unit RMS before rotation; rotation keeps the norm
+    qf = qo.view(np.float16).astype(np.float32).reshape(32, 128)
+    assert np.allclose(np.sqrt((qf ** 2).mean(axis=1)), 1.0, atol=3e-3)
+    kc = syn.to_f16_bits(syn.normal(7, (64, 4, 128)))
+    vc = syn.to_f16_bits(syn.normal(8, (64, 4, 128)))
+    out, _ = oracle.qwen_gqa_attention(qo, kc, vc, 64, oracle.F16)
+    assert np.all(np.isfinite(out))
+
+
+@pytest.mark.parametrize("threads", [1, 3])
+def test_decode_many_threads_identical(oracle, threads):
+    from helpers import granite_inputs
+    caches, qs, ks, vs = [], [], [], []
+    for u in range(5):
+        q, k, v, kc, vc = granite_inputs(100 + u, 40 + u, 64)
+        c = oracle.KvCache(64)
+        c.keys[:40 + u], c.values[:40 + u] = kc, vc
+        c.length.value = 40 + u
+        caches.append(c)
+        qs.append(q), ks.append(k), vs.append(v)
+    worst, outs = oracle.granite_decode_many(qs, ks, vs, [40 + u for u in range(5)], caches, threads=threads)
+    assert worst == 0
+    for u in range(5):
+        c = oracle.KvCache(64)
+        _, _, _, kc, vc = granite_inputs(100 + u, 40 + u, 64)
+        c.keys[:40 + u], c.values[:40 + u] = kc, vc
+        c.length.value = 40 + u
+        st, o = oracle.granite_attention_decode(qs[u], ks[u], vs[u], 40 + u, c)
+        assert np.array_equal(o, outs[u])
