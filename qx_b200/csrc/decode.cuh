@@ -2,19 +2,21 @@
 //
 // One CTA per work item (sequence, layer, kv head, split of the cache). The
 // CTA
-//   1. issues TMA bulk copies (cp.async.bulk, one per cache row of its kv
-//      head; the cache keeps the reference's position-major layout
-//      [pos][kv_head][head_dim]) into a multi-stage shared-memory ring, with
-//      an mbarrier per stage, before doing anything else;
-//   2. meanwhile applies RoPE to the G query heads that share this kv head
+//   1. dedicates one producer warp to TMA: 3-D tensor-map boxes of 64 cache
+//      rows of its kv head (the cache keeps the reference's position-major
+//      layout [pos][kv_head][head_dim]) into a multi-stage shared-memory
+//      ring guarded by full/empty mbarriers;
+//   2. meanwhile the four consumer warps apply RoPE to the G query heads that share this kv head
 //      (Granite: qx's pinned sin/cos and FMA order, qx-consensus-math
 //      lib.rs:148-207; Qwen: per-head RMSNorm then rotate-half RoPE,
 //      qx-qwen-parity main.rs:1177-1204), and, on the split that owns the
 //      new token, RoPE on k, writing k and v into slot `position` and into
 //      its own last tile (so no CTA ever reads the slot being written);
-//   3. streams tiles of 64 positions: scores for all G heads against each
-//      key row held once in shared memory, a tile-wise online softmax with
-//      warp-shuffle max/sum, and P.V accumulation in registers;
+//   3. each consumer warp owns 16 rows of every stage and keeps its own
+//      online-softmax state (scores for all G query heads against each key
+//      row held once in shared memory, 16-lane shuffle max/sum, P.V in
+//      registers), so the loop has no block-wide barrier; the four warp
+//      states merge once at the end;
 //   4. writes its (m, l, O) partial; the last CTA of the (sequence, layer,
 //      kv head) to finish (atomic ticket, no spinning) merges the partials
 //      with a log-sum-exp combine and writes the output.
@@ -23,6 +25,7 @@
 // (granite_attention_decode_with_profile) for Granite, and
 // tools/qx-qwen-parity/src/main.rs:1170-1258 for Qwen3.
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -54,6 +57,12 @@ struct SeqInfo {
 };
 
 struct DecodeParams {
+  // 3-D tensor maps over the key / value regions of the arena:
+  // dims {head_dim, kv_heads, sequences*layers*capacity}, box
+  // {128 bytes of head_dim, 1, 64 positions}, 128-byte swizzle.
+  CUtensorMap tmk;
+  CUtensorMap tmv;
+  int capacity;  // rows per (sequence, layer) in the tensor maps
   // arena
   char* k_region;
   char* v_region;
@@ -83,26 +92,40 @@ struct DecodeParams {
 
 template <class M, typename KT, typename VT>
 struct DecodeCfg {
-  static constexpr int T = 64, NT = 128;
+  static constexpr int T = 64;             // positions per pipeline stage
+  static constexpr int NWC = 4;            // consumer warps
+  static constexpr int NT = 32 * NWC + 32;  // + one producer warp
+  static constexpr int WT = T / NWC;       // positions per consumer warp per stage
   static constexpr int D = M::D, G = M::G;
+  static constexpr int QPL = G * WT / 32;  // query heads per lane in QK (Granite 1, Qwen 4)
+  static constexpr int DPL = D / 32;       // dims per lane in P.V (Granite 2, Qwen 4)
   static constexpr int KROW = D * (int)sizeof(KT), VROW = D * (int)sizeof(VT);
-  // 16-byte row padding: consecutive rows start 4 banks apart, so the
-  // 8 rows a 128-bit shared load wavefront touches never collide.
-  static constexpr int KSTR = KROW + 16, VSTR = VROW + 16;
-  static constexpr int STAGE_BYTES = T * (KSTR + VSTR);
-  static constexpr int STAGES = STAGE_BYTES <= 20480 ? 4 : 3;
-  static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = OFF_K + STAGES * T * KSTR;
-  static constexpr int OFF_Q = OFF_V + STAGES * T * VSTR;   // float [G][D]
-  static constexpr int OFF_S = OFF_Q + G * D * 4;            // float [T][G]
-  static constexpr int OFF_NEWK = OFF_S + T * G * 4;         // KT [D]
+  // A stage arrives as 128-byte-wide TMA boxes ([64 rows][128 B], 128-byte
+  // swizzle: chunk c of row t sits at chunk c ^ (t & 7)), so 128-bit shared
+  // loads by 8 consecutive rows never hit the same bank twice.
+  static constexpr int KB = KROW / 128, VB = VROW / 128;  // boxes per row
+  static constexpr int BOX = T * 128;
+  static constexpr int STAGE_K = KB * BOX, STAGE_V = VB * BOX;
+  static constexpr int STAGES = (STAGE_K + STAGE_V) <= 16384 ? 4 : 3;
+  static constexpr int OFF_K = 0;                         // 1024-aligned
+  static constexpr int OFF_V = OFF_K + STAGES * STAGE_K;  // 1024-aligned
+  static constexpr int OFF_Q = OFF_V + STAGES * STAGE_V;  // float [G][D]
+  static constexpr int OFF_P = OFF_Q + G * D * 4;         // float [NWC][WT][G]
+  static constexpr int OFF_NEWK = OFF_P + NWC * WT * G * 4;
   static constexpr int OFF_NEWV = OFF_NEWK + ((KROW + 15) / 16) * 16;
-  static constexpr int OFF_STAT = OFF_NEWV + ((VROW + 15) / 16) * 16;  // float m[G], l[G], a[G], inv[G+1]
-  static constexpr int OFF_BAR = ((OFF_STAT + 4 * (4 * G + 1) + 15) / 16) * 16;
-  static constexpr int SMEM = OFF_BAR + 8 * STAGES + 16;
-  static constexpr int HPT = G / 2;   // query heads per thread in QK and PV
-  static constexpr int DPT = D / 64;  // dims per thread in PV
+  static constexpr int OFF_STAT = OFF_NEWV + ((VROW + 15) / 16) * 16;  // float [NWC][G][2], inv[G+1]
+  static constexpr int OFF_BAR = ((OFF_STAT + 4 * (NWC * G * 2 + G + 1) + 15) / 16) * 16;
+  static constexpr int SMEM = OFF_BAR + 16 * STAGES + 16 + 1024;  // + slack to align the base to 1024
+  // after the main loop the stage buffers hold the per-warp merge [NWC][G][D]
+  static_assert(NWC * G * D * 4 <= STAGES * (STAGE_K + STAGE_V), "merge buffer must fit the stages");
 };
+
+// Byte offset of byte `b` of row `t` inside a swizzled [64][128 B] box stack.
+template <int BOX>
+__device__ __forceinline__ int swz(int t, int b) {
+  const int w = b & 127;
+  return (b >> 7) * BOX + t * 128 + ((((w >> 4) ^ (t & 7))) << 4) + (w & 15);
+}
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -114,6 +137,23 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+// Reductions within each 16-lane half of a warp.
+__device__ __forceinline__ float half_max(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float half_sum(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Barrier over the 128 consumer threads only (the producer warp is busy).
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier 0 over the whole CTA, reached from the producer and the consumer
+// branches (PTX counts arrivals, wherever they come from).
+__device__ __forceinline__ void cta_sync() { asm volatile("bar.sync 0;" ::: "memory"); }
 
 // Locate this CTA's sequence entry (binary search over item_begin).
 __device__ __forceinline__ int find_slot(const DecodeParams& p, SeqInfo* info) {
@@ -133,23 +173,23 @@ __device__ __forceinline__ int find_slot(const DecodeParams& p, SeqInfo* info) {
 }
 
 template <class M, typename KT, typename VT>
-__global__ void __launch_bounds__(128) qx_decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ DecodeParams p) {
   using C = DecodeCfg<M, KT, VT>;
-  constexpr int D = M::D, G = M::G, HKV = M::HKV, HQ = M::HQ, T = C::T, NT = C::NT;
-  constexpr int HPT = C::HPT, DPT = C::DPT, STAGES = C::STAGES;
-  extern __shared__ __align__(128) unsigned char sm[];
+  constexpr int D = M::D, G = M::G, HKV = M::HKV, HQ = M::HQ, T = C::T, NWC = C::NWC, WT = C::WT;
+  constexpr int QPL = C::QPL, DPL = C::DPL, STAGES = C::STAGES;
+  extern __shared__ __align__(1024) unsigned char sm_raw[];
+  unsigned char* sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
   unsigned char* ktiles = sm + C::OFF_K;
   unsigned char* vtiles = sm + C::OFF_V;
   float* q_s = reinterpret_cast<float*>(sm + C::OFF_Q);
-  float* S = reinterpret_cast<float*>(sm + C::OFF_S);
+  float* P_s = reinterpret_cast<float*>(sm + C::OFF_P);
   KT* newk = reinterpret_cast<KT*>(sm + C::OFF_NEWK);
   VT* newv = reinterpret_cast<VT*>(sm + C::OFF_NEWV);
-  float* st_m = reinterpret_cast<float*>(sm + C::OFF_STAT);
-  float* st_l = st_m + G;
-  float* st_a = st_l + G;
-  float* st_inv = st_a + G;  // [G + 1]: Qwen inverse RMS of q heads, then k
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
-  int* s_flag = reinterpret_cast<int*>(bars + STAGES);
+  float* stat = reinterpret_cast<float*>(sm + C::OFF_STAT);  // [NWC][G][2]
+  float* st_inv = stat + NWC * G * 2;                         // [G + 1]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  int* s_flag = reinterpret_cast<int*>(empty + STAGES);  // [0] last-CTA flag, [1] abort
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -173,256 +213,311 @@ __global__ void __launch_bounds__(128) qx_decode_kernel(const DecodeParams p) {
   const long long cu = (long long)slot * p.layer_count + lloc;  // packed q/k/v/out index
   const bool last_split = (s == nsplit - 1);
 
-  // ---- barriers, then the first tiles in flight ----------------------------
   if (tid == 0) {
 #pragma unroll
-    for (int i = 0; i < STAGES; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NWC);
+    }
+    s_flag[1] = 0;
     fence_barrier_init();
   }
   __syncthreads();
 
-  auto issue = [&](int tile) {  // warp 0
-    const int st = tile % STAGES;
-    const int t0 = begin + tile * T;
-    const int rows = min(T, end - t0);
-    const int fetch = rows - ((has_new && tile == ntiles - 1) ? 1 : 0);
-    if (lane == 0) mbar_arrive_expect_tx(&bars[st], (uint32_t)fetch * (C::KROW + C::VROW));
-    __syncwarp();
-    unsigned char* kt = ktiles + st * T * C::KSTR;
-    unsigned char* vt = vtiles + st * T * C::VSTR;
-    for (int rr = lane; rr < fetch; rr += 32) {
-      const long long row = (long long)(t0 + rr) * HKV + h;
-      bulk_copy_g2s(kt + rr * C::KSTR, kunit + row * C::KROW, C::KROW, &bars[st]);
-      bulk_copy_g2s(vt + rr * C::VSTR, vunit + row * C::VROW, C::VROW, &bars[st]);
-    }
-  };
-  if (warp == 0) {
-    const int first = min(STAGES, ntiles);
-    for (int i = 0; i < first; ++i) issue(i);
-  }
-
-  // ---- prologue: RoPE (and the new k/v row on the owning split) -------------
-  const long long qbase = (cu * HQ + (long long)h * G) * D;  // first query element of this group
-  const long long kvbase = (cu * HKV + h) * D;
-  bool bad = false;
-  if constexpr (!M::QWEN) {
-    // 32 rotation pairs per head; warps 0-1 take the G=2 query heads, warp 2 k.
-    if (tid < G * 32) {
-      const int g = tid >> 5, pair = tid & 31;
-      float left = load_any(p.q, qbase + g * D + pair, p.q_dtype);
-      float right = load_any(p.q, qbase + g * D + pair + 32, p.q_dtype);
-      float sn, cs, a = 0.f, b = 0.f;
-      bool ok = granite_sin_cos((uint32_t)si.rope_pos, pair, &sn, &cs) && granite_rotate(left, right, sn, cs, &a, &b);
-      bad |= !ok;
-      q_s[g * D + pair] = a;
-      q_s[g * D + pair + 32] = b;
-      if (p.q_rot_out && last_split) {
-        p.q_rot_out[qbase + g * D + pair] = a;
-        p.q_rot_out[qbase + g * D + pair + 32] = b;
+  if (warp == NWC) {
+    // ---- producer warp: TMA boxes into the stage ring -----------------------
+    if (lane == 0) {
+      prefetch_tmap(&p.tmk);
+      prefetch_tmap(&p.tmv);
+      const int z0 = (int)(unit * p.capacity) + begin;
+      for (int tile = 0; tile < ntiles; ++tile) {
+        const int st = tile % STAGES;
+        if (tile >= STAGES && !mbar_wait_bounded(&empty[st], (uint32_t)((tile / STAGES) - 1) & 1u, p.err)) {
+          s_flag[1] = 1;
+          break;
+        }
+        unsigned char* kt = ktiles + st * C::STAGE_K;
+        unsigned char* vt = vtiles + st * C::STAGE_V;
+        mbar_arrive_expect_tx(&full[st], (uint32_t)(C::STAGE_K + C::STAGE_V));
+#pragma unroll
+        for (int b = 0; b < C::KB; ++b)
+          tma_load_3d(kt + b * C::BOX, &p.tmk, b * (128 / (int)sizeof(KT)), h, z0 + tile * T, &full[st]);
+#pragma unroll
+        for (int b = 0; b < C::VB; ++b)
+          tma_load_3d(vt + b * C::BOX, &p.tmv, b * (128 / (int)sizeof(VT)), h, z0 + tile * T, &full[st]);
       }
-    } else if (has_new && tid < G * 32 + 32) {
-      const int pair = tid - G * 32;
-      float left = load_any(p.k, kvbase + pair, p.in_dtype);
-      float right = load_any(p.k, kvbase + pair + 32, p.in_dtype);
-      float sn, cs, a = 0.f, b = 0.f;
-      bool ok = granite_sin_cos((uint32_t)si.rope_pos, pair, &sn, &cs) && granite_rotate(left, right, sn, cs, &a, &b);
-      bad |= !ok;
-      newk[pair] = Elem<KT>::from_f32(a);
-      newk[pair + 32] = Elem<KT>::from_f32(b);
     }
   } else {
-    // Per-head RMSNorm needs the reference's sequential sum of squares
-    // (bit-exact K); one thread per head.
-    if (tid < G || (tid == G && has_new)) {
-      const bool is_q = tid < G;
-      float sum = 0.0f;
-      for (int i = 0; i < D; ++i) {
-        float x = is_q ? load_any(p.q, qbase + tid * D + i, p.q_dtype) : load_any(p.k, kvbase + i, p.in_dtype);
-        sum = __fadd_rn(sum, __fmul_rn(x, x));
-      }
-      st_inv[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 128.0f), 1.0e-6f)));
-    }
-    __syncthreads();
-    const float2* tab = p.rope_table + (long long)si.rope_pos * 64;
-    for (int idx = tid; idx < (G + 1) * 64; idx += NT) {
-      const int g = idx >> 6, i = idx & 63;
-      if (g == G && !has_new) break;
-      const bool is_q = g < G;
-      const float inv = st_inv[g];
-      const float* wn = is_q ? p.q_norm : p.k_norm;
-      float x = is_q ? load_any(p.q, qbase + g * D + i, p.q_dtype) : load_any(p.k, kvbase + i, p.in_dtype);
-      float y = is_q ? load_any(p.q, qbase + g * D + i + 64, p.q_dtype) : load_any(p.k, kvbase + i + 64, p.in_dtype);
-      float left = __fmul_rn(__fmul_rn(x, inv), wn ? wn[i] : 1.0f);
-      float right = __fmul_rn(__fmul_rn(y, inv), wn ? wn[64 + i] : 1.0f);
-      const float2 cssn = tab[i];
-      float a = __fsub_rn(__fmul_rn(left, cssn.x), __fmul_rn(right, cssn.y));
-      float b = __fadd_rn(__fmul_rn(right, cssn.x), __fmul_rn(left, cssn.y));
-      bad |= !(isfinite(a) && isfinite(b));
-      if (is_q) {
-        // the reference rounds the rotated query to its 16-bit type
-        a = Elem<KT>::to_f32(Elem<KT>::from_f32(a));
-        b = Elem<KT>::to_f32(Elem<KT>::from_f32(b));
-        q_s[g * D + i] = a;
-        q_s[g * D + i + 64] = b;
+    // ---- consumers: prologue (RoPE; the new k/v row on the owning split) -----
+    const long long qbase = (cu * HQ + (long long)h * G) * D;  // first query element of this group
+    const long long kvbase = (cu * HKV + h) * D;
+    bool bad = false;
+    if constexpr (!M::QWEN) {
+      // 32 rotation pairs per head: warps 0-1 the G=2 query heads, warp 2 k.
+      if (tid < G * 32) {
+        const int g = tid >> 5, pair = tid & 31;
+        float left = load_any(p.q, qbase + g * D + pair, p.q_dtype);
+        float right = load_any(p.q, qbase + g * D + pair + 32, p.q_dtype);
+        float sn, cs, a = 0.f, b = 0.f;
+        bool ok = granite_sin_cos((uint32_t)si.rope_pos, pair, &sn, &cs) &&
+                  granite_rotate(left, right, sn, cs, &a, &b);
+        bad |= !ok;
+        q_s[g * D + pair] = a;
+        q_s[g * D + pair + 32] = b;
         if (p.q_rot_out && last_split) {
-          p.q_rot_out[qbase + g * D + i] = a;
-          p.q_rot_out[qbase + g * D + i + 64] = b;
+          p.q_rot_out[qbase + g * D + pair] = a;
+          p.q_rot_out[qbase + g * D + pair + 32] = b;
         }
-      } else {
-        newk[i] = Elem<KT>::from_f32(a);
-        newk[i + 64] = Elem<KT>::from_f32(b);
+      } else if (has_new && tid < G * 32 + 32) {
+        const int pair = tid - G * 32;
+        float left = load_any(p.k, kvbase + pair, p.in_dtype);
+        float right = load_any(p.k, kvbase + pair + 32, p.in_dtype);
+        float sn, cs, a = 0.f, b = 0.f;
+        bool ok = granite_sin_cos((uint32_t)si.rope_pos, pair, &sn, &cs) &&
+                  granite_rotate(left, right, sn, cs, &a, &b);
+        bad |= !ok;
+        newk[pair] = Elem<KT>::from_f32(a);
+        newk[pair + 32] = Elem<KT>::from_f32(b);
+      }
+    } else {
+      // Per-head RMSNorm with the reference's sequential sum of squares
+      // (bit-exact K); one thread per head.
+      if (tid < G || (tid == G && has_new)) {
+        const bool is_q = tid < G;
+        float sum = 0.0f;
+        for (int i = 0; i < D; ++i) {
+          float x = is_q ? load_any(p.q, qbase + tid * D + i, p.q_dtype) : load_any(p.k, kvbase + i, p.in_dtype);
+          sum = __fadd_rn(sum, __fmul_rn(x, x));
+        }
+        st_inv[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 128.0f), 1.0e-6f)));
+      }
+      consumers_sync();
+      const float2* tab = p.rope_table + (long long)si.rope_pos * 64;
+      for (int idx = tid; idx < (G + 1) * 64; idx += 32 * NWC) {
+        const int g = idx >> 6, i = idx & 63;
+        if (g == G && !has_new) break;
+        const bool is_q = g < G;
+        const float inv = st_inv[g];
+        const float* wn = is_q ? p.q_norm : p.k_norm;
+        float x = is_q ? load_any(p.q, qbase + g * D + i, p.q_dtype) : load_any(p.k, kvbase + i, p.in_dtype);
+        float y = is_q ? load_any(p.q, qbase + g * D + i + 64, p.q_dtype) : load_any(p.k, kvbase + i + 64, p.in_dtype);
+        float left = __fmul_rn(__fmul_rn(x, inv), wn ? wn[i] : 1.0f);
+        float right = __fmul_rn(__fmul_rn(y, inv), wn ? wn[64 + i] : 1.0f);
+        const float2 cssn = tab[i];
+        float a = __fsub_rn(__fmul_rn(left, cssn.x), __fmul_rn(right, cssn.y));
+        float b = __fadd_rn(__fmul_rn(right, cssn.x), __fmul_rn(left, cssn.y));
+        bad |= !(isfinite(a) && isfinite(b));
+        if (is_q) {
+          // the reference rounds the rotated query to its 16-bit type
+          a = Elem<KT>::to_f32(Elem<KT>::from_f32(a));
+          b = Elem<KT>::to_f32(Elem<KT>::from_f32(b));
+          q_s[g * D + i] = a;
+          q_s[g * D + i + 64] = b;
+          if (p.q_rot_out && last_split) {
+            p.q_rot_out[qbase + g * D + i] = a;
+            p.q_rot_out[qbase + g * D + i + 64] = b;
+          }
+        } else {
+          newk[i] = Elem<KT>::from_f32(a);
+          newk[i + 64] = Elem<KT>::from_f32(b);
+        }
       }
     }
-  }
-  if (has_new) {
-    for (int i = tid; i < D; i += NT) newv[i] = Elem<VT>::from_f32(load_any(p.v, kvbase + i, p.in_dtype));
-  }
-  if (tid < G) {
-    st_m[tid] = -INFINITY;
-    st_l[tid] = 0.0f;
-  }
-  if (bad) flag_error(p.err, QX_ERR_BIT_NONFINITE);
-  __syncthreads();
-  if (has_new) {
-    // Append: slot new_slot of this kv head, same bits the tile will use.
-    char* kdst = const_cast<char*>(kunit) + ((long long)si.new_slot * HKV + h) * C::KROW;
-    char* vdst = const_cast<char*>(vunit) + ((long long)si.new_slot * HKV + h) * C::VROW;
-    for (int i = tid; i < C::KROW / 16; i += NT)
-      reinterpret_cast<uint4*>(kdst)[i] = reinterpret_cast<const uint4*>(newk)[i];
-    for (int i = tid; i < C::VROW / 16; i += NT)
-      reinterpret_cast<uint4*>(vdst)[i] = reinterpret_cast<const uint4*>(newv)[i];
-  }
-
-  // ---- main loop over tiles -------------------------------------------------
-  const int hg = tid >> 6, t_own = tid & 63, dg = tid & 63;
-  float acc[HPT][DPT];
-#pragma unroll
-  for (int j = 0; j < HPT; ++j)
-#pragma unroll
-    for (int e = 0; e < DPT; ++e) acc[j][e] = 0.0f;
-  const bool pinned = p.pinned_exp != 0;
-
-  for (int tile = 0; tile < ntiles; ++tile) {
-    const int st = tile % STAGES;
-    const uint32_t parity = (uint32_t)(tile / STAGES) & 1u;
-    const bool ok = mbar_wait_bounded(&bars[st], parity, p.err);
-    if (__syncthreads_or(!ok)) return;  // bounded wait gave up; error recorded
-    const int t0 = begin + tile * T;
-    const int rows = min(T, end - t0);
-    unsigned char* kt = ktiles + st * T * C::KSTR;
-    unsigned char* vt = vtiles + st * T * C::VSTR;
-    if (has_new && tile == ntiles - 1) {
-      for (int i = tid; i < C::KROW / 16; i += NT)
-        reinterpret_cast<uint4*>(kt + (rows - 1) * C::KSTR)[i] = reinterpret_cast<const uint4*>(newk)[i];
-      for (int i = tid; i < C::VROW / 16; i += NT)
-        reinterpret_cast<uint4*>(vt + (rows - 1) * C::VSTR)[i] = reinterpret_cast<const uint4*>(newv)[i];
-      __syncthreads();
+    if (has_new)
+      for (int i = tid; i < D; i += 32 * NWC) newv[i] = Elem<VT>::from_f32(load_any(p.v, kvbase + i, p.in_dtype));
+    if (bad) flag_error(p.err, QX_ERR_BIT_NONFINITE);
+    consumers_sync();
+    if (has_new) {
+      // Append: slot new_slot of this kv head.
+      char* kdst = const_cast<char*>(kunit) + ((long long)si.new_slot * HKV + h) * C::KROW;
+      char* vdst = const_cast<char*>(vunit) + ((long long)si.new_slot * HKV + h) * C::VROW;
+      for (int i = tid; i < C::KROW / 16; i += 32 * NWC)
+        reinterpret_cast<uint4*>(kdst)[i] = reinterpret_cast<const uint4*>(newk)[i];
+      for (int i = tid; i < C::VROW / 16; i += 32 * NWC)
+        reinterpret_cast<uint4*>(vdst)[i] = reinterpret_cast<const uint4*>(newv)[i];
     }
-    // scores: thread (position t_own, heads hg*HPT .. +HPT)
-    {
-      float sc[HPT];
+
+    // ---- consumers: main loop; warp w owns rows [16w, 16w+16) of each stage --
+    const bool pinned = p.pinned_exp != 0;
+    const int trow = lane & 15;              // QK: row within my 16
+    const int hq0 = (lane >> 4) * QPL;       // QK: first query head of this lane
+    float m_run[G], l_run[G], acc[G][DPL];
 #pragma unroll
-      for (int j = 0; j < HPT; ++j) sc[j] = 0.0f;
-      if (t_own < rows) {
-        const KT* krow = reinterpret_cast<const KT*>(kt + t_own * C::KSTR);
-        constexpr int VEC = Vec16<KT>::N;
-#pragma unroll 2
-        for (int d0 = 0; d0 < D; d0 += VEC) {
-          float kf[VEC];
-          Vec16<KT>::load(krow + d0, kf);
+    for (int g = 0; g < G; ++g) {
+      m_run[g] = -INFINITY;
+      l_run[g] = 0.0f;
 #pragma unroll
-          for (int j = 0; j < HPT; ++j) {
-            const float* qrow = &q_s[(hg * HPT + j) * D + d0];
+      for (int e = 0; e < DPL; ++e) acc[g][e] = 0.0f;
+    }
+    float* Pw = P_s + warp * WT * G;
+    for (int tile = 0; tile < ntiles; ++tile) {
+      const int st = tile % STAGES;
+      if (!mbar_wait_bounded(&full[st], (uint32_t)(tile / STAGES) & 1u, p.err)) {
+        s_flag[1] = 1;
+        break;
+      }
+      unsigned char* kt = ktiles + st * C::STAGE_K;
+      unsigned char* vt = vtiles + st * C::STAGE_V;
+      const int rows = min(T, end - (begin + tile * T));
+      const int r0 = warp * WT;
+      const int mine = max(0, min(WT, rows - r0));
+      if (has_new && tile == ntiles - 1 && rows - 1 >= r0 && rows - 1 < r0 + WT) {
+        // the appended slot comes from registers, not from the copy
+        for (int i = lane; i < C::KROW / 16; i += 32)
+          *reinterpret_cast<uint4*>(kt + swz<C::BOX>(rows - 1, i * 16)) = reinterpret_cast<const uint4*>(newk)[i];
+        for (int i = lane; i < C::VROW / 16; i += 32)
+          *reinterpret_cast<uint4*>(vt + swz<C::BOX>(rows - 1, i * 16)) = reinterpret_cast<const uint4*>(newv)[i];
+        __syncwarp();
+      }
+      if (mine > 0) {
+        // scores: lane (row r0+trow, heads hq0..hq0+QPL-1), 4 partial sums
+        float sc[QPL];
+        if (trow < mine) {
+          float part[QPL][4];
 #pragma unroll
-            for (int v4 = 0; v4 < VEC; v4 += 4) {
-              const float4 qv = *reinterpret_cast<const float4*>(qrow + v4);
-              sc[j] = fmaf(qv.x, kf[v4], sc[j]);
-              sc[j] = fmaf(qv.y, kf[v4 + 1], sc[j]);
-              sc[j] = fmaf(qv.z, kf[v4 + 2], sc[j]);
-              sc[j] = fmaf(qv.w, kf[v4 + 3], sc[j]);
+          for (int j = 0; j < QPL; ++j)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) part[j][u] = 0.0f;
+          constexpr int VEC = Vec16<KT>::N;
+#pragma unroll
+          for (int d0 = 0; d0 < D; d0 += VEC) {
+            float kf[VEC];
+            Vec16<KT>::load(reinterpret_cast<const KT*>(kt + swz<C::BOX>(r0 + trow, d0 * (int)sizeof(KT))), kf);
+#pragma unroll
+            for (int j = 0; j < QPL; ++j) {
+              const float* qrow = &q_s[(hq0 + j) * D + d0];
+#pragma unroll
+              for (int v4 = 0; v4 < VEC; v4 += 4) {
+                const float4 qv = *reinterpret_cast<const float4*>(qrow + v4);
+                part[j][0] = fmaf(qv.x, kf[v4], part[j][0]);
+                part[j][1] = fmaf(qv.y, kf[v4 + 1], part[j][1]);
+                part[j][2] = fmaf(qv.z, kf[v4 + 2], part[j][2]);
+                part[j][3] = fmaf(qv.w, kf[v4 + 3], part[j][3]);
+              }
             }
           }
+#pragma unroll
+          for (int j = 0; j < QPL; ++j) sc[j] = ((part[j][0] + part[j][1]) + (part[j][2] + part[j][3])) * M::SCALE;
+        } else {
+#pragma unroll
+          for (int j = 0; j < QPL; ++j) sc[j] = -INFINITY;
         }
+        // online softmax per head over this warp's rows (16-lane halves)
+        float a_l[QPL], s_l[QPL], m_l[QPL];
 #pragma unroll
-        for (int j = 0; j < HPT; ++j) sc[j] *= M::SCALE;
-      } else {
+        for (int j = 0; j < QPL; ++j) {
+          const int g = hq0 + j;
+          const float mt = half_max(sc[j]);
+          float mold = m_run[0];
 #pragma unroll
-        for (int j = 0; j < HPT; ++j) sc[j] = -INFINITY;
-      }
+          for (int gg = 1; gg < G; ++gg)
+            if (gg == g) mold = m_run[gg];
+          const float mnew = fmaxf(mold, mt);
+          a_l[j] = (mold == -INFINITY) ? 0.0f : softmax_exp(mold - mnew, pinned);
+          const float pw = trow < mine ? softmax_exp(sc[j] - mnew, pinned) : 0.0f;
+          Pw[trow * G + g] = pw;
+          s_l[j] = half_sum(pw);
+          m_l[j] = mnew;
+        }
+        __syncwarp();
+        // every lane needs (alpha, tile sum, new max) of all G heads; head g
+        // lives in slot g % QPL of the lanes of half g / QPL.
 #pragma unroll
-      for (int j = 0; j < HPT; ++j) S[t_own * G + hg * HPT + j] = sc[j];
-    }
-    __syncthreads();
-    // tile-wise online softmax: warp w owns heads w, w+4, ...
-    for (int g = warp; g < G; g += 4) {
-      const float s0 = S[lane * G + g], s1 = S[(lane + 32) * G + g];
-      const float mt = warp_max(fmaxf(s0, s1));
-      const float mold = st_m[g];
-      const float mnew = fmaxf(mold, mt);
-      const float alpha = (mold == -INFINITY) ? 0.0f : softmax_exp(mold - mnew, pinned);
-      const float p0 = lane < rows ? softmax_exp(s0 - mnew, pinned) : 0.0f;
-      const float p1 = lane + 32 < rows ? softmax_exp(s1 - mnew, pinned) : 0.0f;
-      S[lane * G + g] = p0;
-      S[(lane + 32) * G + g] = p1;
-      const float sum = warp_sum(p0 + p1);
-      if (lane == 0) {
-        st_l[g] = fmaf(st_l[g], alpha, sum);
-        st_m[g] = mnew;
-        st_a[g] = alpha;
-      }
-    }
-    __syncthreads();
-    // P.V: thread owns heads hg*HPT.. and dims dg*DPT..
-    {
+        for (int g = 0; g < G; ++g) {
+          const int src = (g / QPL) * 16;
+          const float a = __shfl_sync(0xffffffffu, a_l[g % QPL], src);
+          const float ts = __shfl_sync(0xffffffffu, s_l[g % QPL], src);
+          m_run[g] = __shfl_sync(0xffffffffu, m_l[g % QPL], src);
+          l_run[g] = fmaf(l_run[g], a, ts);
 #pragma unroll
-      for (int j = 0; j < HPT; ++j) {
-        const float a = st_a[hg * HPT + j];
+          for (int e = 0; e < DPL; ++e) acc[g][e] *= a;
+        }
+        // P.V: lane owns dims [lane*DPL, lane*DPL + DPL) of all G heads
+        for (int tt = 0; tt < mine; ++tt) {
+          float vv[DPL];
+          const VT* vrow = reinterpret_cast<const VT*>(vt + swz<C::BOX>(r0 + tt, lane * DPL * (int)sizeof(VT)));
 #pragma unroll
-        for (int e = 0; e < DPT; ++e) acc[j][e] *= a;
-      }
-#pragma unroll 4
-      for (int tt = 0; tt < rows; ++tt) {
-        const VT* vrow = reinterpret_cast<const VT*>(vt + tt * C::VSTR);
-        float vv[DPT];
+          for (int e = 0; e < DPL; ++e) vv[e] = Elem<VT>::to_f32(vrow[e]);
+          const float* prow = &Pw[tt * G];
 #pragma unroll
-        for (int e = 0; e < DPT; ++e) vv[e] = Elem<VT>::to_f32(vrow[dg * DPT + e]);
-        const float* prow = &S[tt * G + hg * HPT];
+          for (int g = 0; g < G; ++g) {
+            const float pw = prow[g];
 #pragma unroll
-        for (int j = 0; j < HPT; ++j) {
-          const float pw = prow[j];
-#pragma unroll
-          for (int e = 0; e < DPT; ++e) acc[j][e] = fmaf(pw, vv[e], acc[j][e]);
+            for (int e = 0; e < DPL; ++e) acc[g][e] = fmaf(pw, vv[e], acc[g][e]);
+          }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
     }
-    __syncthreads();  // stage `st` and S are free again
-    if (warp == 0 && tile + STAGES < ntiles) issue(tile + STAGES);
+    // per-warp state for the merge
+    if (lane == 0) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        stat[(warp * G + g) * 2] = m_run[g];
+        stat[(warp * G + g) * 2 + 1] = l_run[g];
+      }
+    }
+    // stash acc once every warp has left the stage buffers
+    cta_sync();  // (A) all 160 threads
+    if (!s_flag[1]) {
+      float* mbuf = reinterpret_cast<float*>(sm + C::OFF_K);  // [NWC][G][D]
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NWC; ++w) mx = fmaxf(mx, stat[(w * G + g) * 2]);
+        const float sc_w = (m_run[g] == -INFINITY) ? 0.0f : softmax_exp(m_run[g] - mx, pinned);
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) mbuf[(warp * G + g) * D + lane * DPL + e] = acc[g][e] * sc_w;
+      }
+    }
+  }
+  if (warp == NWC) cta_sync();  // (A) for the producer warp
+  cta_sync();                  // (B) merge buffer complete
+  if (s_flag[1]) return;             // a bounded wait gave up; error recorded
+  if (warp == NWC) return;
+
+  // ---- combine the warps: thread -> outputs (g, d) = idx / D, idx % D --------
+  constexpr int OPT = G * D / 128;  // outputs per consumer thread
+  const bool pinned = p.pinned_exp != 0;
+  const float* mbuf = reinterpret_cast<const float*>(sm + C::OFF_K);
+  float O[OPT], Mg[OPT], Lg[OPT];
+#pragma unroll
+  for (int k = 0; k < OPT; ++k) {
+    const int idx = tid + k * 128, g = idx / D, d = idx % D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NWC; ++w) mx = fmaxf(mx, stat[(w * G + g) * 2]);
+    float L = 0.0f, o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NWC; ++w) {
+      const float mw = stat[(w * G + g) * 2];
+      if (mw != -INFINITY) L = fmaf(stat[(w * G + g) * 2 + 1], softmax_exp(mw - mx, pinned), L);
+      o += mbuf[(w * G + g) * D + d];
+    }
+    O[k] = o;
+    Mg[k] = mx;
+    Lg[k] = L;
   }
 
-  // ---- finish: direct output, or partial + last-CTA merge -------------------
   const long long obase = (cu * HQ + (long long)h * G) * D;
   if (nsplit == 1) {
     bool nonfinite = false;
 #pragma unroll
-    for (int j = 0; j < HPT; ++j) {
-      const int g = hg * HPT + j;
-      const float l = st_l[g];
+    for (int k = 0; k < OPT; ++k) {
+      const int idx = tid + k * 128, g = idx / D, d = idx % D;
       if (p.emit_partials) {
         float* part = reinterpret_cast<float*>(p.out) + (cu * HQ + (long long)h * G + g) * (D + 2);
-#pragma unroll
-        for (int e = 0; e < DPT; ++e) part[dg * DPT + e] = acc[j][e];
-        if (dg == 0) {
-          part[D] = st_m[g];
-          part[D + 1] = l;
+        part[d] = O[k];
+        if (d == 0) {
+          part[D] = Mg[k];
+          part[D + 1] = Lg[k];
         }
       } else {
-        const float inv = 1.0f / l;
-#pragma unroll
-        for (int e = 0; e < DPT; ++e) {
-          const float o = acc[j][e] * inv;
-          nonfinite |= !isfinite(o);
-          store_any(p.out, obase + g * D + dg * DPT + e, p.out_dtype, o);
-        }
+        const float o = O[k] / Lg[k];
+        nonfinite |= !isfinite(o);
+        store_any(p.out, obase + idx, p.out_dtype, o);
       }
     }
     if (nonfinite) flag_error(p.err, QX_ERR_BIT_NONFINITE);
@@ -431,54 +526,47 @@ __global__ void __launch_bounds__(128) qx_decode_kernel(const DecodeParams p) {
 
   float* part = p.partials + (long long)blockIdx.x * G * (D + 2);
 #pragma unroll
-  for (int j = 0; j < HPT; ++j)
-#pragma unroll
-    for (int e = 0; e < DPT; ++e) part[(hg * HPT + j) * (D + 2) + dg * DPT + e] = acc[j][e];
-  if (tid < G) {
-    part[tid * (D + 2) + D] = st_m[tid];
-    part[tid * (D + 2) + D + 1] = st_l[tid];
+  for (int k = 0; k < OPT; ++k) {
+    const int idx = tid + k * 128, g = idx / D, d = idx % D;
+    part[g * (D + 2) + d] = O[k];
+    if (d == 0) {
+      part[g * (D + 2) + D] = Mg[k];
+      part[g * (D + 2) + D + 1] = Lg[k];
+    }
   }
   __threadfence();
-  __syncthreads();
+  consumers_sync();
   int* ticket = p.tickets + cu * HKV + h;
   if (tid == 0) s_flag[0] = (atomicAdd(ticket, 1) == nsplit - 1);
-  __syncthreads();
+  consumers_sync();
   if (!s_flag[0]) return;
   __threadfence();
 
   const float* first = p.partials + (long long)(blockIdx.x - s) * G * (D + 2);
   bool nonfinite = false;
 #pragma unroll
-  for (int j = 0; j < HPT; ++j) {
-    const int g = hg * HPT + j;
+  for (int k = 0; k < OPT; ++k) {
+    const int idx = tid + k * 128, g = idx / D, d = idx % D;
     float mx = -INFINITY;
     for (int i = 0; i < nsplit; ++i) mx = fmaxf(mx, __ldcg(first + ((long long)i * G + g) * (D + 2) + D));
-    float L = 0.0f, O[DPT];
-#pragma unroll
-    for (int e = 0; e < DPT; ++e) O[e] = 0.0f;
+    float L = 0.0f, o = 0.0f;
     for (int i = 0; i < nsplit; ++i) {
       const float* pi = first + ((long long)i * G + g) * (D + 2);
       const float w = softmax_exp(__ldcg(pi + D) - mx, pinned);
       L = fmaf(w, __ldcg(pi + D + 1), L);
-#pragma unroll
-      for (int e = 0; e < DPT; ++e) O[e] = fmaf(w, __ldcg(pi + dg * DPT + e), O[e]);
+      o = fmaf(w, __ldcg(pi + d), o);
     }
     if (p.emit_partials) {
       float* dst = reinterpret_cast<float*>(p.out) + (cu * HQ + (long long)h * G + g) * (D + 2);
-#pragma unroll
-      for (int e = 0; e < DPT; ++e) dst[dg * DPT + e] = O[e];
-      if (dg == 0) {
+      dst[d] = o;
+      if (d == 0) {
         dst[D] = mx;
         dst[D + 1] = L;
       }
     } else {
-      const float inv = 1.0f / L;
-#pragma unroll
-      for (int e = 0; e < DPT; ++e) {
-        const float o = O[e] * inv;
-        nonfinite |= !isfinite(o);
-        store_any(p.out, obase + g * D + dg * DPT + e, p.out_dtype, o);
-      }
+      const float v = o / L;
+      nonfinite |= !isfinite(v);
+      store_any(p.out, obase + idx, p.out_dtype, v);
     }
   }
   if (nonfinite) flag_error(p.err, QX_ERR_BIT_NONFINITE);

@@ -103,6 +103,21 @@ __device__ __forceinline__ void bulk_copy_g2s_hint(void* dst, const void* src, u
       : "memory");
 }
 
+// TMA tensor-tile copy (3-D tensor map) global -> this CTA's shared memory.
+// The innermost coordinate x must be a multiple of 16 bytes' worth of
+// elements; callers only pass x = 0 or a multiple of a 128-byte box.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_addr(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

@@ -7,6 +7,8 @@
 // crates/qx-runtime-v2/src/lib.rs:6587-6589 ("context {c} must be in
 // 1..=4096"). Nothing is launched when validation fails, so a rejected call
 // leaves the cache untouched, as the reference's Err return does.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -50,7 +52,12 @@ struct qxc_ctx {
   char* stage_host = nullptr;
   size_t stage_host_cap = 0;
   unsigned long long launches = 0;
+  // Qwen RoPE (cos, sin) for every position 0..kQwenMaxPositions-1, shared
+  // by all Qwen arenas of this context (created with the first one).
+  float2* qwen_rope = nullptr;
 };
+
+constexpr int kQwenMaxPositions = 40960;  // max_position_embeddings, qx-model lib.rs:308
 
 struct qxc_kv {
   qxc_ctx* ctx = nullptr;
@@ -62,7 +69,8 @@ struct qxc_kv {
   char* v_region = nullptr;
   size_t k_unit = 0, v_unit = 0;  // bytes per (sequence, layer)
   std::vector<int> len;
-  float2* rope_table = nullptr;  // Qwen (cos, sin) per absolute position
+  float2* rope_table = nullptr;  // Qwen (cos, sin) per absolute position (owned by ctx)
+  CUtensorMap tmk, tmv;          // tensor maps over the key / value regions
 };
 
 namespace {
@@ -255,6 +263,9 @@ qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* s
 qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer_begin, int layer_count,
                        DecodeParams* p) {
   memset(p, 0, sizeof(*p));
+  p->tmk = kv->tmk;
+  p->tmv = kv->tmv;
+  p->capacity = kv->desc.capacity;
   p->k_region = kv->k_region;
   p->v_region = kv->v_region;
   p->k_unit_bytes = (long long)kv->k_unit;
@@ -292,6 +303,57 @@ bool default_pinned(const qxc_kv* kv, int flags) {
 qxc_status check_seq(qxc_ctx* ctx, const qxc_kv* kv, int seq) {
   if (seq < 0 || seq >= kv->desc.sequences)
     return fail(ctx, QXC_ERR_INVALID_ARG, "sequence %d is outside the arena (%d sequences)", seq, kv->desc.sequences);
+  return QXC_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 3-D map over one region: {head_dim, kv_heads, rows}, box {128 B of
+// head_dim, 1 head, 64 rows}, 128-byte swizzle. Rows past the region read
+// as zero.
+qxc_status encode_kv_map(qxc_ctx* ctx, CUtensorMap* map, void* base, int dtype, int hkv, int d, size_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(ctx, QXC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const size_t es = dtype_size(dtype);
+  const CUtensorMapDataType t = dtype == QXC_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                : dtype == QXC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)hkv, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)(d * es), (cuuint64_t)(hkv * d * es)};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / es), 1, 64};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, t, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, QXC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return QXC_OK;
+}
+
+qxc_status ensure_qwen_rope(qxc_ctx* ctx) {
+  if (ctx->qwen_rope) return QXC_OK;
+  // cos/sin of position * 1e6^(-i/64) with the platform's single-precision
+  // powf/sinf/cosf, as tools/qx-qwen-parity/src/main.rs:1193-1195 evaluates
+  // them; computed once on the host so the device never evaluates
+  // transcendental RoPE and every position's values equal the host's.
+  std::vector<float2> tab((size_t)kQwenMaxPositions * 64);
+  float inv[64];
+  for (int i = 0; i < 64; ++i) inv[i] = powf(1000000.0f, -(float)i / 64.0f);
+  for (int pos = 0; pos < kQwenMaxPositions; ++pos)
+    for (int i = 0; i < 64; ++i) {
+      volatile float angle = (float)pos * inv[i];
+      tab[(size_t)pos * 64 + i] = make_float2(cosf(angle), sinf(angle));
+    }
+  QXC_CUDA(ctx, cudaMalloc(&ctx->qwen_rope, tab.size() * sizeof(float2)));
+  QXC_CUDA(ctx, cudaMemcpy(ctx->qwen_rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
   return QXC_OK;
 }
 
@@ -354,6 +416,7 @@ void qxc_destroy(qxc_ctx* ctx) {
     if (ctx->seq_ev[i]) cudaEventDestroy(ctx->seq_ev[i]);
   }
   cudaFree(ctx->stage_dev);
+  cudaFree(ctx->qwen_rope);
   if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -430,30 +493,16 @@ qxc_status qxc_kv_create(qxc_ctx* ctx, const qxc_kv_desc* desc, qxc_kv** out) {
   kv->k_region = kv->base;
   kv->v_region = kv->base + koff_v;
   kv->len.assign(desc->sequences, 0);
-  if (desc->model == QXC_MODEL_QWEN3) {
-    // cos/sin of position * 1e6^(-i/64) with the platform's single-precision
-    // powf/sinf/cosf, as tools/qx-qwen-parity/src/main.rs:1193-1195 evaluates
-    // them; computed once here so the device never evaluates transcendental
-    // RoPE and every position's table is identical to the host's.
-    const int n = desc->first_position + desc->capacity;
-    std::vector<float2> tab((size_t)n * 64);
-    float inv[64];
-    for (int i = 0; i < 64; ++i) inv[i] = powf(1000000.0f, -(float)i / 64.0f);
-    for (int pos = 0; pos < n; ++pos)
-      for (int i = 0; i < 64; ++i) {
-        volatile float angle = (float)pos * inv[i];
-        tab[(size_t)pos * 64 + i] = make_float2(cosf(angle), sinf(angle));
-      }
-    e = cudaMalloc(&kv->rope_table, tab.size() * sizeof(float2));
-    if (e == cudaSuccess)
-      e = cudaMemcpy(kv->rope_table, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
-      cudaFree(kv->base);
-      cudaFree(kv->rope_table);
-      delete kv;
-      return fail(ctx, QXC_ERR_CUDA, "RoPE table: %s", cudaGetErrorString(e));
-    }
+  qxc_status mst = encode_kv_map(ctx, &kv->tmk, kv->k_region, desc->key_dtype, kv->hkv, kv->d, units * desc->capacity);
+  if (mst == QXC_OK)
+    mst = encode_kv_map(ctx, &kv->tmv, kv->v_region, desc->value_dtype, kv->hkv, kv->d, units * desc->capacity);
+  if (mst == QXC_OK && desc->model == QXC_MODEL_QWEN3) mst = ensure_qwen_rope(ctx);
+  if (mst != QXC_OK) {
+    cudaFree(kv->base);
+    delete kv;
+    return mst;
   }
+  kv->rope_table = ctx->qwen_rope;
   QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
   *out = kv;
   return QXC_OK;
@@ -464,7 +513,6 @@ void qxc_kv_destroy(qxc_kv* kv) {
   cudaSetDevice(kv->ctx->device);
   cudaStreamSynchronize(kv->ctx->stream);
   cudaFree(kv->base);
-  cudaFree(kv->rope_table);
   delete kv;
 }
 
@@ -765,6 +813,8 @@ qxc_status qxc_decode_partials(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args*
   }
   if (kv->desc.model == QXC_MODEL_GRANITE && a->position >= 4096)
     return fail(ctx, QXC_ERR_POSITION, "KV position %d exceeds context 4096", a->position);
+  if (kv->desc.model == QXC_MODEL_QWEN3 && a->position >= kQwenMaxPositions)
+    return fail(ctx, QXC_ERR_POSITION, "KV position %d exceeds context %d", a->position, kQwenMaxPositions);
   QXC_CUDA(ctx, cudaSetDevice(ctx->device));
   CallPlan plan;
   const int seq = a->seq, rope = a->position;

@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import ctypes as C
 import enum
+import weakref
 from dataclasses import dataclass
 
 import numpy as np
@@ -64,9 +65,12 @@ class Context:
             raise QxError(st, f"qxc_init({device}) failed: {self.lib.qxc_status_string(st).decode()}")
         self.handle = h
         self.device = device
+        self._arenas = weakref.WeakSet()  # destroyed before the context
 
     def close(self):
         if self.handle:
+            for a in list(self._arenas):
+                a.close()
             self.lib.qxc_destroy(self.handle)
             self.handle = None
 
@@ -131,13 +135,15 @@ class KvArena:
         h = C.c_void_p()
         ctx.check(self.lib.qxc_kv_create(ctx.handle, C.byref(self.desc), C.byref(h)))
         self.handle = h
+        ctx._arenas.add(self)
         self.model, self.layers, self.sequences, self.capacity = model, layers, sequences, capacity
         self.key_dtype, self.value_dtype, self.first_position = key_dtype, value_dtype, first_position
         self.hq, self.hkv, self.d = model_shape(model)
 
     def close(self):
         if getattr(self, "handle", None):
-            self.lib.qxc_kv_destroy(self.handle)
+            if self.ctx.handle:  # a closed context already destroyed its arenas
+                self.lib.qxc_kv_destroy(self.handle)
             self.handle = None
 
     def __del__(self):

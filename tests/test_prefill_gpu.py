@@ -16,7 +16,7 @@ def run_prefill(ctx, L, seed):
     q = syn.to_bf16_bits(syn.normal(seed, (L, 16, 64), 0.5))
     k = syn.to_bf16_bits(syn.normal(seed + 1, (L, 8, 64), 0.5))
     v = syn.to_bf16_bits(syn.normal(seed + 2, (L, 8, 64), 0.5))
-    arena = KvArena(ctx, MODEL_GRANITE, 1, 1, max(L, 64), BF16, BF16)
+    arena = KvArena(ctx, MODEL_GRANITE, 1, 1, L + 64, BF16, BF16)
     dev = lambda a: torch.from_numpy(a.view(np.int16)).cuda()
     out = torch.zeros(L, 16, 64, device="cuda")
     arena.prefill(dev(q), dev(k), dev(v), out, L)
