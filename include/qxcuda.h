@@ -216,6 +216,44 @@ qxc_status qxc_decode_partials(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args*
 qxc_status qxc_lse_merge(qxc_ctx* ctx, int32_t model, int32_t n_parts, const float* partials, void* out,
                          int32_t out_dtype);
 
+/* ---- allocation-free decode ----------------------------------------------
+ * No counterpart in the reference (qx's Metal path has no such entry point).
+ * For callers that must not let a library allocate device memory: a host
+ * runtime that sizes one arena up front and forbids allocation afterwards,
+ * or code whose device memory comes from its own pool. One Granite decode
+ * step (RoPE, append into slot `position`, attention over slots
+ * [0, position]) on one layer's cache given as plain device pointers, with
+ * the split-KV scratch taken from a 128 KiB static device array inside the
+ * library instead of cudaMalloc. No context or arena is needed.
+ *   - The first call on each device (with that device current) does a
+ *     one-time set-up; make it before any stream capture on that device.
+ *   - Every call on a device shares the one static array: calls whose
+ *     kernels can overlap on the GPU race; order them on one stream.
+ *   - A request whose split-KV partials exceed the array returns
+ *     QXC_ERR_INVALID_ARG (use a larger `split`).
+ * Asynchronous on `cuda_stream`; `message` (may be NULL) receives the
+ * reason of a rejected call. */
+typedef struct qxc_static_decode_args {
+  void* key_cache;        /* device [capacity][8][64], key_dtype */
+  void* value_cache;      /* device [capacity][8][64], value_dtype */
+  int32_t capacity;       /* slots, 1..=4096 */
+  int32_t key_dtype;      /* F32/F32, F32/F16, F16/F32, F16/F16 or BF16/BF16 */
+  int32_t value_dtype;
+  int32_t position;       /* slot of the new token; slots [0, position) hold the prefix */
+  const void* q;          /* device [16][64], q_dtype */
+  const void* k;          /* device [8][64], in_dtype */
+  const void* v;          /* device [8][64], in_dtype */
+  void* out;              /* device [16][64], out_dtype */
+  int32_t q_dtype;
+  int32_t in_dtype;
+  int32_t out_dtype;
+  int32_t flags;          /* QXC_DECODE_NATIVE_EXP to use hardware exp2 */
+  int32_t split;          /* cache positions per split, multiple of 64; 0 = automatic */
+  unsigned* device_error; /* optional device word set non-zero on a device-side error */
+} qxc_static_decode_args;
+qxc_status qxc_granite_decode_static_scratch(const qxc_static_decode_args* args, void* cuda_stream, char* message,
+                                             size_t message_len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,15 @@ class PartialArgs(C.Structure):
                 ("in_dtype", C.c_int32), ("flags", C.c_int32), ("split", C.c_int32)]
 
 
+class StaticDecodeArgs(C.Structure):
+    """qxc_static_decode_args (allocation-free Granite decode)."""
+    _fields_ = [("key_cache", C.c_void_p), ("value_cache", C.c_void_p), ("capacity", C.c_int32),
+                ("key_dtype", C.c_int32), ("value_dtype", C.c_int32), ("position", C.c_int32),
+                ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("out", C.c_void_p),
+                ("q_dtype", C.c_int32), ("in_dtype", C.c_int32), ("out_dtype", C.c_int32),
+                ("flags", C.c_int32), ("split", C.c_int32), ("device_error", C.c_void_p)]
+
+
 _lib = None
 
 
@@ -90,6 +99,7 @@ def load() -> C.CDLL:
         "qxc_prefill": (C.c_int, [vp, vp, C.POINTER(PrefillArgs)]),
         "qxc_decode_partials": (C.c_int, [vp, vp, C.POINTER(PartialArgs)]),
         "qxc_lse_merge": (C.c_int, [vp, i32, i32, vp, vp, i32]),
+        "qxc_granite_decode_static_scratch": (C.c_int, [C.POINTER(StaticDecodeArgs), vp, C.c_char_p, C.c_size_t]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -598,7 +598,7 @@ __global__ void qx_lse_merge_kernel(const float* __restrict__ partials, int n_pa
 
 // ---- standalone RoPE (apply_granite_rope, qx-runtime lib.rs:434-442) -------
 // q [16][64] and k [8][64] f32 in place; one thread per rotation pair.
-__global__ void qx_granite_rope_kernel(float* q, float* k, int position, unsigned* err) {
+static __global__ void qx_granite_rope_kernel(float* q, float* k, int position, unsigned* err) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;  // 0 .. 24*32-1
   if (idx >= 24 * 32) return;
   const int head = idx >> 5, pair = idx & 31;
