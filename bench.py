@@ -171,9 +171,10 @@ def run_config1(args, world, rank, local):
     arena.set_len(0, P)
 
     lib = ctx.lib
+    flags = _lib.DECODE_NATIVE_EXP if args.native_exp else 0
     pos_arr = [(C.c_int32 * 1)(P + i) for i in range(cycle)]
     dargs = [_lib.DecodeArgs(0, LAYERS, 1, None, pos_arr[i], q[i].data_ptr(), k[i].data_ptr(), v[i].data_ptr(),
-                             out[i].data_ptr(), None, None, None, F32, F32, F32, 0, args.split)
+                             out[i].data_ptr(), None, None, None, F32, F32, F32, flags, args.split)
              for i in range(cycle)]
     dptrs = [C.byref(a) for a in dargs]
 
@@ -230,7 +231,7 @@ def run_config1(args, world, rank, local):
         hout = np.zeros((LAYERS, 1024), np.float32)
         hpos = [(C.c_int32 * 1)(P + i) for i in range(cycle)]
         hargs = [_lib.DecodeArgs(0, LAYERS, 1, None, hpos[i], hq[i].ctypes.data, hk[i].ctypes.data,
-                                 hv[i].ctypes.data, hout.ctypes.data, None, None, None, F32, F32, F32, 0, args.split)
+                                 hv[i].ctypes.data, hout.ctypes.data, None, None, None, F32, F32, F32, flags, args.split)
                  for i in range(cycle)]
         hptr = [C.byref(a) for a in hargs]
         E = min(K, args.e2e_steps)
@@ -278,7 +279,8 @@ def run_config1(args, world, rank, local):
                                f"positions {P}..{L - 1} cycled, batch 1",
                    "context": L, "layers": LAYERS, "kv_dtype": "f32", "batch_per_gpu": 1,
                    "l2": "inputs larger than L2: each step reads ~%.0f MB of KV" % (avg_bytes / 1e6),
-                   "parallelism": f"replicas x{world} (independent sequences, no collective)"},
+                   "parallelism": f"replicas x{world} (independent sequences, no collective)",
+                   "softmax_exp": "native exp2" if args.native_exp else "qx pinned exp_f32"},
         "hbm_gbs": achieved_gbs,
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                      "frac": achieved_gbs / peak, "peak_kind": peak_kind,
@@ -401,6 +403,7 @@ def main():
     ap.add_argument("--workload", default="config1", choices=["config1"])
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
+    ap.add_argument("--native-exp", action="store_true", help="hardware exp2 instead of qx's pinned exp_f32")
     ap.add_argument("--e2e-steps", type=int, default=640)
     ap.add_argument("--cpu-steps", type=int, default=16)
     ap.add_argument("--reference-budget-s", type=float, default=150.0)

@@ -93,12 +93,20 @@ struct DecodeParams {
 template <class M, typename KT, typename VT>
 struct DecodeCfg {
   static constexpr int T = 64;             // positions per pipeline stage
-  static constexpr int NWC = 4;            // consumer warps
-  static constexpr int NT = 32 * NWC + 32;  // + one producer warp
-  static constexpr int WT = T / NWC;       // positions per consumer warp per stage
+  // Consumer warps come in groups of four; group g takes stages g, g+NGROUP,
+  // ... and warp w of a group owns rows [16w, 16w+16) of each of them.
+  // Granite runs two groups (more resident warps to hide shared-memory
+  // latency); Qwen's 8-head state needs the registers of one group.
+  static constexpr int NWC = M::QWEN ? 4 : 8;  // consumer warps
+  static constexpr int NGROUP = NWC / 4;
+  static constexpr int NT = 32 * NWC + 32;     // + one producer warp
+  static constexpr int WT = T / 4;             // rows per consumer warp per stage
   static constexpr int D = M::D, G = M::G;
-  static constexpr int QPL = G * WT / 32;  // query heads per lane in QK (Granite 1, Qwen 4)
-  static constexpr int DPL = D / 32;       // dims per lane in P.V (Granite 2, Qwen 4)
+  static constexpr int QPL = G * WT / 32;      // query heads per lane in QK (Granite 1, Qwen 4)
+  // P.V: Granite lanes of each half-warp take alternate rows and 4 dims each
+  // (one 128-bit load of V per row); Qwen lanes take D/32 dims of every row.
+  static constexpr bool PVH = !M::QWEN;
+  static constexpr int DPL = PVH ? D / 16 : D / 32;
   static constexpr int KROW = D * (int)sizeof(KT), VROW = D * (int)sizeof(VT);
   // A stage arrives as 128-byte-wide TMA boxes ([64 rows][128 B], 128-byte
   // swizzle: chunk c of row t sits at chunk c ^ (t & 7)), so 128-bit shared
@@ -106,7 +114,14 @@ struct DecodeCfg {
   static constexpr int KB = KROW / 128, VB = VROW / 128;  // boxes per row
   static constexpr int BOX = T * 128;
   static constexpr int STAGE_K = KB * BOX, STAGE_V = VB * BOX;
-  static constexpr int STAGES = (STAGE_K + STAGE_V) <= 16384 ? 4 : 3;
+  // Tile t lives in stage t % STAGES and is consumed by group t % NGROUP.
+  // STAGES must be a multiple of NGROUP: then a stage is always consumed by
+  // the same group, which finished the stage's previous tile before waiting
+  // for the next one, so a full/empty barrier is never more than one phase
+  // ahead of its waiter (mbarrier parity only tells two phases apart).
+  static constexpr int STAGES = NGROUP == 2 ? ((STAGE_K + STAGE_V) <= 16384 ? 4 : 2)
+                                            : ((STAGE_K + STAGE_V) <= 16384 ? 4 : 3);
+  static_assert(STAGES % NGROUP == 0, "each stage must belong to one consumer group");
   static constexpr int OFF_K = 0;                         // 1024-aligned
   static constexpr int OFF_V = OFF_K + STAGES * STAGE_K;  // 1024-aligned
   static constexpr int OFF_Q = OFF_V + STAGES * STAGE_V;  // float [G][D]
@@ -149,8 +164,10 @@ __device__ __forceinline__ float half_sum(float v) {
   return v;
 }
 
-// Barrier over the 128 consumer threads only (the producer warp is busy).
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier 1 over the consumer threads only (the producer warp is busy).
+__device__ __forceinline__ void consumers_sync(int n) { asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); }
+// Barrier 2 over the first 128 threads (the output combine).
+__device__ __forceinline__ void combine_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 // Barrier 0 over the whole CTA, reached from the producer and the consumer
 // branches (PTX counts arrivals, wherever they come from).
 __device__ __forceinline__ void cta_sync() { asm volatile("bar.sync 0;" ::: "memory"); }
@@ -173,7 +190,7 @@ __device__ __forceinline__ int find_slot(const DecodeParams& p, SeqInfo* info) {
 }
 
 template <class M, typename KT, typename VT>
-__global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(const __grid_constant__ DecodeParams p) {
   using C = DecodeCfg<M, KT, VT>;
   constexpr int D = M::D, G = M::G, HKV = M::HKV, HQ = M::HQ, T = C::T, NWC = C::NWC, WT = C::WT;
   constexpr int QPL = C::QPL, DPL = C::DPL, STAGES = C::STAGES;
@@ -217,7 +234,7 @@ __global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ 
 #pragma unroll
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], NWC);
+      mbar_init(&empty[i], 4);  // the four warps of the group that consumes the stage
     }
     s_flag[1] = 0;
     fence_barrier_init();
@@ -291,7 +308,7 @@ __global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ 
         }
         st_inv[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 128.0f), 1.0e-6f)));
       }
-      consumers_sync();
+      consumers_sync(32 * NWC);
       const float2* tab = p.rope_table + (long long)si.rope_pos * 64;
       for (int idx = tid; idx < (G + 1) * 64; idx += 32 * NWC) {
         const int g = idx >> 6, i = idx & 63;
@@ -326,7 +343,7 @@ __global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ 
     if (has_new)
       for (int i = tid; i < D; i += 32 * NWC) newv[i] = Elem<VT>::from_f32(load_any(p.v, kvbase + i, p.in_dtype));
     if (bad) flag_error(p.err, QX_ERR_BIT_NONFINITE);
-    consumers_sync();
+    consumers_sync(32 * NWC);
     if (has_new) {
       // Append: slot new_slot of this kv head.
       char* kdst = const_cast<char*>(kunit) + ((long long)si.new_slot * HKV + h) * C::KROW;
@@ -350,7 +367,8 @@ __global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ 
       for (int e = 0; e < DPL; ++e) acc[g][e] = 0.0f;
     }
     float* Pw = P_s + warp * WT * G;
-    for (int tile = 0; tile < ntiles; ++tile) {
+    const int wg = warp & 3;
+    for (int tile = warp >> 2; tile < ntiles; tile += C::NGROUP) {
       const int st = tile % STAGES;
       if (!mbar_wait_bounded(&full[st], (uint32_t)(tile / STAGES) & 1u, p.err)) {
         s_flag[1] = 1;
@@ -359,7 +377,7 @@ __global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ 
       unsigned char* kt = ktiles + st * C::STAGE_K;
       unsigned char* vt = vtiles + st * C::STAGE_V;
       const int rows = min(T, end - (begin + tile * T));
-      const int r0 = warp * WT;
+      const int r0 = wg * WT;
       const int mine = max(0, min(WT, rows - r0));
       if (has_new && tile == ntiles - 1 && rows - 1 >= r0 && rows - 1 < r0 + WT) {
         // the appended slot comes from registers, not from the copy
@@ -432,6 +450,22 @@ __global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ 
 #pragma unroll
           for (int e = 0; e < DPL; ++e) acc[g][e] *= a;
         }
+        if constexpr (C::PVH) {
+          // P.V: half-warp h2 takes rows h2, h2+2, ...; lane owns 4 dims of all G heads
+          const int h2 = lane >> 4, dl = lane & 15;
+          for (int tt = h2; tt < mine; tt += 2) {
+            const float4 v4 = lds4<VT>(reinterpret_cast<const VT*>(vt + swz<C::BOX>(r0 + tt, dl * 4 * (int)sizeof(VT))));
+            const float* prow = &Pw[tt * G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              const float pw = prow[g];
+              acc[g][0] = fmaf(pw, v4.x, acc[g][0]);
+              acc[g][1] = fmaf(pw, v4.y, acc[g][1]);
+              acc[g][2] = fmaf(pw, v4.z, acc[g][2]);
+              acc[g][3] = fmaf(pw, v4.w, acc[g][3]);
+            }
+          }
+        } else
         // P.V: lane owns dims [lane*DPL, lane*DPL + DPL) of all G heads
         for (int tt = 0; tt < mine; ++tt) {
           float vv[DPL];
@@ -458,8 +492,15 @@ __global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ 
         stat[(warp * G + g) * 2 + 1] = l_run[g];
       }
     }
+    if constexpr (C::PVH) {
+      // fold the two half-warps (alternate rows) together
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[g][e] += __shfl_xor_sync(0xffffffffu, acc[g][e], 16);
+    }
     // stash acc once every warp has left the stage buffers
-    cta_sync();  // (A) all 160 threads
+    cta_sync();  // (A) whole CTA
     if (!s_flag[1]) {
       float* mbuf = reinterpret_cast<float*>(sm + C::OFF_K);  // [NWC][G][D]
 #pragma unroll
@@ -468,15 +509,17 @@ __global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ 
 #pragma unroll
         for (int w = 0; w < NWC; ++w) mx = fmaxf(mx, stat[(w * G + g) * 2]);
         const float sc_w = (m_run[g] == -INFINITY) ? 0.0f : softmax_exp(m_run[g] - mx, pinned);
+        if (!C::PVH || lane < 16) {
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) mbuf[(warp * G + g) * D + lane * DPL + e] = acc[g][e] * sc_w;
+          for (int e = 0; e < DPL; ++e) mbuf[(warp * G + g) * D + (C::PVH ? (lane & 15) : lane) * DPL + e] = acc[g][e] * sc_w;
+        }
       }
     }
   }
   if (warp == NWC) cta_sync();  // (A) for the producer warp
   cta_sync();                  // (B) merge buffer complete
   if (s_flag[1]) return;             // a bounded wait gave up; error recorded
-  if (warp == NWC) return;
+  if (tid >= 128) return;             // the combine runs on the first 128 threads
 
   // ---- combine the warps: thread -> outputs (g, d) = idx / D, idx % D --------
   constexpr int OPT = G * D / 128;  // outputs per consumer thread
@@ -535,10 +578,10 @@ __global__ void __launch_bounds__(160) qx_decode_kernel(const __grid_constant__ 
     }
   }
   __threadfence();
-  consumers_sync();
+  combine_sync();
   int* ticket = p.tickets + cu * HKV + h;
   if (tid == 0) s_flag[0] = (atomicAdd(ticket, 1) == nsplit - 1);
-  consumers_sync();
+  combine_sync();
   if (!s_flag[0]) return;
   __threadfence();
 

@@ -153,15 +153,50 @@ qxc_status grow(qxc_ctx* ctx, T** ptr, size_t* cap, size_t need, bool zero) {
   return QXC_OK;
 }
 
-// Positions per split: multiple of 64, chosen so the grid covers the GPU
-// several times over (split-KV exists to fill 148 SMs at batch 1).
-int auto_chunk(const qxc_ctx* ctx, long long total_slots, int max_attend) {
-  const long long target = (long long)ctx->sm_count * 8;
-  long long c = (total_slots + target - 1) / target;
-  c = std::max<long long>(c, 256);
-  c = ((c + 63) / 64) * 64;
-  c = std::min<long long>(c, std::max(64, ((max_attend + 63) / 64) * 64));
-  return (int)std::max<long long>(c, 64);
+// Resident CTAs per SM of one decode instantiation (occupancy API).
+template <class M, typename KT, typename VT>
+int blocks_per_sm() {
+  using C = DecodeCfg<M, KT, VT>;
+  cudaFuncSetAttribute(qx_decode_kernel<M, KT, VT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  int n = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qx_decode_kernel<M, KT, VT>, C::NT, C::SMEM) != cudaSuccess)
+    n = 1;
+  return n > 0 ? n : 1;
+}
+
+int decode_blocks_per_sm(const qxc_kv* kv) {
+  const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
+  if (kv->desc.model == QXC_MODEL_QWEN3)
+    return kd == QXC_BF16 ? blocks_per_sm<Qwen3, __nv_bfloat16, __nv_bfloat16>() : blocks_per_sm<Qwen3, __half, __half>();
+  if (kd == QXC_F32 && vd == QXC_F32) return blocks_per_sm<Granite, float, float>();
+  if (kd == QXC_F32 && vd == QXC_F16) return blocks_per_sm<Granite, float, __half>();
+  if (kd == QXC_F16 && vd == QXC_F32) return blocks_per_sm<Granite, __half, float>();
+  if (kd == QXC_F16 && vd == QXC_F16) return blocks_per_sm<Granite, __half, __half>();
+  return blocks_per_sm<Granite, __nv_bfloat16, __nv_bfloat16>();
+}
+
+// Positions per split (a multiple of 64). Split-KV exists to fill 148 SMs
+// at small batch; too many splits add per-CTA overhead, and a grid that
+// leaves the last wave nearly empty wastes the tail. Model the time as
+// waves x (64-row tiles per CTA + a fixed per-CTA cost) and take the
+// cheapest split, preferring fewer splits on ties.
+int auto_chunk(int slots, const int* attend, int n, int units_per_seq) {
+  int max_attend = 1;
+  for (int i = 0; i < n; ++i) max_attend = std::max(max_attend, attend[i]);
+  const int top = ((max_attend + 63) / 64) * 64;
+  double best = 1e300;
+  int best_c = top;
+  for (int c = top; c >= 64; c -= 64) {
+    long long items = 0;
+    for (int i = 0; i < n; ++i) items += (long long)units_per_seq * ((attend[i] + c - 1) / c);
+    const long long waves = (items + slots - 1) / slots;
+    const double cost = (double)waves * (c / 64.0 + 3.0);
+    if (cost < best - 1e-9) {
+      best = cost;
+      best_c = c;
+    }
+  }
+  return best_c;
 }
 
 using KernelFn = void (*)(DecodeParams);
@@ -232,14 +267,17 @@ struct CallPlan {
 // `rope_pos[i]` per sequence entry.
 qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* seq_ids, const int* attend,
                      const int* new_slot, const int* rope_pos, int layer_count, int split, CallPlan* out) {
-  long long total_slots = 0;
-  int max_attend = 0;
-  for (int i = 0; i < seq_count; ++i) {
-    total_slots += (long long)attend[i] * layer_count * kv->hkv;
-    max_attend = std::max(max_attend, attend[i]);
-  }
   int chunk = split;
-  if (chunk == 0) chunk = auto_chunk(ctx, total_slots, max_attend);
+  if (chunk == 0) {
+    static int cached_slots[64][8] = {};  // [device][arena type] resident CTAs on the GPU
+    const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
+    const int type = kv->desc.model == QXC_MODEL_QWEN3 ? (kd == QXC_BF16 ? 5 : 6)
+                     : kd == QXC_BF16                  ? 4
+                                                       : (kd == QXC_F16 ? 2 : 0) + (vd == QXC_F16 ? 1 : 0);
+    int& slots = cached_slots[ctx->device & 63][type];
+    if (!slots) slots = ctx->sm_count * decode_blocks_per_sm(kv);
+    chunk = auto_chunk(slots, attend, seq_count, layer_count * kv->hkv);
+  }
   if (chunk <= 0 || chunk % 64 != 0) return fail(ctx, QXC_ERR_INVALID_ARG, "split %d must be a positive multiple of 64", split);
   out->chunk = chunk;
   out->tab.resize(seq_count);

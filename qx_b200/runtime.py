@@ -83,10 +83,18 @@ class Context:
     def check(self, status: int):
         _check(self.lib, self.handle, status)
 
+    CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the implicitly synchronising default stream
+
     def set_stream(self, stream) -> None:
-        """Borrow a CUDA stream (torch.cuda.Stream, raw handle int, or None for the own stream)."""
+        """Borrow a CUDA stream: a torch.cuda.Stream or a raw handle. torch's
+        default stream (handle 0) maps to cudaStreamLegacy so work stays
+        ordered with torch; None restores the context's own stream."""
+        if stream is None:
+            self.check(self.lib.qxc_set_stream(self.handle, None))
+            return
         raw = getattr(stream, "cuda_stream", stream)
-        self.check(self.lib.qxc_set_stream(self.handle, C.c_void_p(raw) if raw else None))
+        raw = raw or self.CUDA_STREAM_LEGACY
+        self.check(self.lib.qxc_set_stream(self.handle, C.c_void_p(raw)))
 
     @property
     def stream(self) -> int:

@@ -28,5 +28,7 @@ def gpu_ctx():
         pytest.skip("no CUDA device")
     from qx_b200 import Context
     ctx = Context(0)
+    # run on torch's stream so torch-made inputs/outputs are ordered with our kernels
+    ctx.set_stream(torch.cuda.current_stream())
     yield ctx
     ctx.close()
