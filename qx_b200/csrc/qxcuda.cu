@@ -55,6 +55,9 @@ struct qxc_ctx {
   // Qwen RoPE (cos, sin) for every position 0..kQwenMaxPositions-1, shared
   // by all Qwen arenas of this context (created with the first one).
   float2* qwen_rope = nullptr;
+  // prefill's rotated-query scratch (bf16 elements)
+  unsigned short* prefill_q = nullptr;
+  size_t prefill_q_cap = 0;
 };
 
 constexpr int kQwenMaxPositions = 40960;  // max_position_embeddings, qx-model lib.rs:308
@@ -376,6 +379,25 @@ qxc_status encode_kv_map(qxc_ctx* ctx, CUtensorMap* map, void* base, int dtype, 
   return QXC_OK;
 }
 
+// 3-D map {inner, heads, rows} with box {box_inner, 1, box_rows}, 128-byte swizzle.
+qxc_status encode_tile_map(qxc_ctx* ctx, CUtensorMap* map, void* base, int dtype, int heads, int inner, size_t rows,
+                           int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(ctx, QXC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const size_t es = dtype_size(dtype);
+  const CUtensorMapDataType t = dtype == QXC_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                : dtype == QXC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)heads, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)(inner * es), (cuuint64_t)(heads * inner * es)};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / es), 1, (cuuint32_t)box_rows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, t, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, QXC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return QXC_OK;
+}
+
 qxc_status ensure_qwen_rope(qxc_ctx* ctx) {
   if (ctx->qwen_rope) return QXC_OK;
   // cos/sin of position * 1e6^(-i/64) with the platform's single-precision
@@ -455,6 +477,7 @@ void qxc_destroy(qxc_ctx* ctx) {
   }
   cudaFree(ctx->stage_dev);
   cudaFree(ctx->qwen_rope);
+  cudaFree(ctx->prefill_q);
   if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -918,22 +941,38 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
   void *kc, *vc;
   kv_view(kv, a->seq, a->layer, true, &kc, nullptr);
   kv_view(kv, a->seq, a->layer, false, &vc, nullptr);
+  // rotated-query scratch, L x 16 x 64 bf16
+  st = grow(ctx, &ctx->prefill_q, &ctx->prefill_q_cap, (size_t)a->length * 1024, false);
+  if (st != QXC_OK) return st;
   PrefillParams p;
   memset(&p, 0, sizeof(p));
+  st = encode_tile_map(ctx, &p.tmq, ctx->prefill_q, QXC_BF16, 16, 64, a->length, 64);
+  if (st == QXC_OK) st = encode_tile_map(ctx, &p.tmk, kc, QXC_BF16, 8, 64, a->length, 64);
+  if (st == QXC_OK) st = encode_tile_map(ctx, &p.tmv, vc, QXC_BF16, 8, 64, a->length, 64);
+  if (st != QXC_OK) return st;
   p.q = static_cast<const __nv_bfloat16*>(a->q);
   p.k = static_cast<const __nv_bfloat16*>(a->k);
   p.v = static_cast<const __nv_bfloat16*>(a->v);
+  p.q_rot = reinterpret_cast<__nv_bfloat16*>(ctx->prefill_q);
   p.k_cache = static_cast<__nv_bfloat16*>(kc);
   p.v_cache = static_cast<__nv_bfloat16*>(vc);
   p.out = a->out;
   p.out_dtype = a->out_dtype;
   p.length = a->length;
-  p.pinned_exp = (a->flags & QXC_DECODE_NATIVE_EXP) ? 0 : 1;
   p.err = ctx->err_dev;
-  int launches = 0;
-  cudaError_t e = launch_prefill(p, ctx->stream, &launches);
-  if (e != cudaSuccess) return fail(ctx, QXC_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e));
-  ctx->launches += launches;
+  static unsigned long long configured = 0;
+  const unsigned long long bit = 1ull << (ctx->device & 63);
+  if (!(configured & bit)) {
+    QXC_CUDA(ctx, cudaFuncSetAttribute(qx_prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       PrefillCfg::SMEM));
+    configured |= bit;
+  }
+  qx_prefill_rope_kernel<<<a->length, 256, 0, ctx->stream>>>(p);
+  QXC_CUDA(ctx, cudaGetLastError());
+  dim3 grid((a->length + 63) / 64, 8);
+  qx_prefill_attn_tc_kernel<<<grid, PrefillCfg::NT, PrefillCfg::SMEM, ctx->stream>>>(p);
+  QXC_CUDA(ctx, cudaGetLastError());
+  ctx->launches += 2;
   if (!(a->flags & QXC_DECODE_NO_ADVANCE)) kv->len[a->seq] = a->length;
   return QXC_OK;
 }
