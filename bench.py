@@ -331,6 +331,330 @@ def cpu_baseline_config1(L, threads, steps):
 
 
 # ---------------------------------------------------------------------------------------
+# shared timing harness for the other workloads
+# ---------------------------------------------------------------------------------------
+def tensor_peak():
+    try:
+        with open(PEAKS_PATH) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def timed_steps(step, K, W, stream, world, dev, local, ctx):
+    """W warm-up then K timed steps, each bracketed by CUDA events on `stream`;
+    returns (max-over-ranks total ms, per-step ms list, clocks, launches)."""
+    import torch
+    for i in range(W):
+        step(i)
+    stream.synchronize()
+    ctx.sync()
+    barrier(world)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ctx.launch_count
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(K):
+            ev[i][0].record(stream)
+            step(W + i)
+            ev[i][1].record(stream)
+        end.record(stream)
+        stream.synchronize()
+    ctx.sync()
+    total = allreduce_max(start.elapsed_time(end), world, dev)
+    per = [a.elapsed_time(b) for a, b in ev]
+    return total, per, clk.summary(), ctx.launch_count - launches0
+
+
+def base_line(metric, value, unit, world, K, W, total_ms, higher, scaling, dtype, config, clocks, launches):
+    return {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": total_ms / K, "higher_is_better": higher, "scaling": scaling, "vs_baseline": None,
+            "dtype": dtype, "data": "synthetic: seeded N(0,1)", "config": config, "clocks": clocks,
+            "gpu_launches": int(launches)}
+
+
+def hbm_roofline(bytes_per_launch, per_ms, kernel):
+    peak, kind = hbm_peak()
+    ach = bytes_per_launch / (float(np.mean(per_ms)) / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": kind,
+            "traffic": None, "kernel": kernel, "algorithmic_bytes_per_launch": bytes_per_launch,
+            "avg_launch_us": float(np.mean(per_ms)) * 1e3}
+
+
+def run_config0(args, world, rank, local):
+    """Config 0: one Granite layer, fp32, 511 cached rows + the new token at 511."""
+    import torch
+    from qx_b200 import F32, MODEL_GRANITE, Context, KvArena
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    ctx = Context(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    arena = KvArena(ctx, MODEL_GRANITE, 1, 1, 512, F32, F32)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0x51580000)
+    with torch.cuda.stream(stream):
+        arena.tensor(0, 0, True)[:511].normal_(generator=g)
+        arena.tensor(0, 0, False)[:511].normal_(generator=g)
+        q = torch.randn(1, 1024, device=dev, generator=g)
+        k = torch.randn(1, 512, device=dev, generator=g)
+        v = torch.randn(1, 512, device=dev, generator=g)
+        out = torch.zeros(1, 1024, device=dev)
+    stream.synchronize()
+
+    def one(i):
+        arena.set_len(0, 511)
+        arena.decode(q, k, v, out, [511], split=args.split)
+
+    # A single call is a few microseconds of GPU work, less than the host's
+    # launch path, so the calls are captured in a CUDA graph (R per replay)
+    # and the graph is replayed: the timing is then the device's own.
+    R = 100
+    for i in range(3):
+        one(i)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(R):
+            one(i)
+
+    def step(i):
+        graph.replay()
+
+    K, W = max(1, args.steps // R), max(3, args.warmup // R)
+    with torch.cuda.stream(stream):  # graph.replay() launches on the current stream
+        total, per, clk, launches = timed_steps(step, K, W, stream, world, dev, local, ctx)
+    launches = K * R
+    per = [x / R for x in per]
+    total = total / R
+    K = K * R
+    B = 2 * 512 * 8 * 64 * 4 + 4 * 64 * (2 * 16 + 2 * 8)
+    us = float(np.mean(per)) * 1e3
+    line = base_line("single-layer Granite GQA decode latency (us per call)", us, "us", world, K, W, total, False,
+                     "weak", "f32", {"workload": "config0: Granite 1 layer, fp32 KV, 511 cached + new token at 511",
+                                     "l2": "2.1 MB working set stays in L2 (latency-bound case)",
+                                     "timing": "100 calls per CUDA graph replay; per-call device time"}, clk, launches)
+    line["roofline"] = hbm_roofline(B, per, "qx_decode_kernel<Granite,float,float>")
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import py_oracle as o
+        from qx_b200 import synthetic as syn
+        o.build()
+        c = o.KvCache(512)
+        c.keys[:511] = syn.normal(1, (511, 8, 64))
+        c.values[:511] = syn.normal(2, (511, 8, 64))
+        qq, kk, vv = syn.normal(3, (1024,)), syn.normal(4, (512,)), syn.normal(5, (512,))
+        n = 200
+        t0 = time.perf_counter()
+        for _ in range(n):
+            c.length.value = 511
+            o.granite_attention_decode(qq, kk, vv, 511, c)
+        dt = (time.perf_counter() - t0) / n
+        line["cpu_baseline"] = {"value": dt * 1e6, "unit": "us", "cores": 1, "kind": "port",
+                                "sample": f"{n} calls of the oracle granite_attention_decode at context 512"}
+    arena.close()
+    ctx.close()
+    return line
+
+
+def run_config2(args, world, rank, local):
+    """Config 2: Granite causal prefill, bf16 in, f32 accumulate, L = --context (512 or 2048)."""
+    import torch
+    from qx_b200 import BF16, MODEL_GRANITE, Context, KvArena
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L = args.prefill_len
+    ctx = Context(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    arena = KvArena(ctx, MODEL_GRANITE, 1, 1, L, BF16, BF16)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0x51580200)
+    with torch.cuda.stream(stream):
+        q = (torch.randn(L, 16, 64, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        k = (torch.randn(L, 8, 64, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        v = (torch.randn(L, 8, 64, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        out = torch.zeros(L, 16, 64, device=dev)
+    stream.synchronize()
+
+    def step(i):
+        arena.reset(0)
+        arena.prefill(q, k, v, out, L)
+
+    K, W = args.steps, args.warmup
+    total, per, clk, launches = timed_steps(step, K, W, stream, world, dev, local, ctx)
+    flops = 2 * 16 * 64 * L * (L + 1)
+    peak, kind = tensor_peak()
+    ach = flops / (float(np.mean(per)) / 1e3) / 1e12
+    line = base_line("Granite causal GQA prefill TFLOP/s", world * flops * K / (total / 1e3) / 1e12, "TFLOP/s",
+                     world, K, W, total, True, "weak", "bf16",
+                     {"workload": f"config2: Granite causal prefill, L={L}, 16/8 heads, d=64, bf16 in, f32 acc",
+                      "l2": "per-step working set (q/k/v/out ~9 MB at L=2048) fits L2; compute-bound",
+                      "flops_per_step": flops}, clk, launches)
+    line["roofline"] = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                        "peak_kind": kind, "traffic": None,
+                        "kernel": "qx_prefill_rope_kernel + qx_prefill_attn_tc_kernel (timed together)",
+                        "algorithmic_flops_per_launch": flops, "avg_launch_us": float(np.mean(per)) * 1e3}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import py_oracle as o
+        from qx_b200 import synthetic as syn
+        o.build()
+        Ls = 512
+        qs = syn.to_bf16_bits(syn.normal(1, (Ls, 16, 64), 0.5))
+        ks = syn.to_bf16_bits(syn.normal(2, (Ls, 8, 64), 0.5))
+        vs = syn.to_bf16_bits(syn.normal(3, (Ls, 8, 64), 0.5))
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        o.granite_prefill(qs, ks, vs, o.BF16, o.BF16, threads=threads)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": 2 * 16 * 64 * Ls * (Ls + 1) / dt / 1e12, "unit": "TFLOP/s",
+                                "cores": threads, "kind": "port",
+                                "sample": f"oracle prefill (iterated decode) at L={Ls} on {threads} threads"}
+    arena.close()
+    ctx.close()
+    return line
+
+
+def run_config3(args, world, rank, local):
+    """Config 3: Qwen3 attention decode, bf16 KV, KV length 32768; N>1 splits the KV length."""
+    import torch
+    from qx_b200 import BF16, MODEL_QWEN3, Context, KvArena
+    from qx_b200.distributed import all_gather_partials, kv_ranges
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L = 32768
+    P = L - 1
+    b, e = kv_ranges(L, world)[rank]
+    owner = rank == world - 1
+    ctx = Context(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    arena = KvArena(ctx, MODEL_QWEN3, 1, 1, e - b, BF16, BF16, first_position=b)
+    cached = min(e, P) - b
+    g = torch.Generator(device=dev)
+    g.manual_seed(0x51580300 + rank)
+    with torch.cuda.stream(stream):
+        arena.tensor(0, 0, True)[:cached].view(torch.bfloat16).normal_(generator=g)
+        arena.tensor(0, 0, False)[:cached].view(torch.bfloat16).normal_(generator=g)
+        gq = torch.Generator(device=dev)
+        gq.manual_seed(0x51580301)  # q/k/v identical on every rank
+        q = torch.randn(1, 4096, device=dev, generator=gq).to(torch.bfloat16)
+        k = torch.randn(1, 512, device=dev, generator=gq).to(torch.bfloat16)
+        v = torch.randn(1, 512, device=dev, generator=gq).to(torch.bfloat16)
+        out = torch.zeros(1, 4096, device=dev)
+        parts = torch.zeros(32, 130, device=dev)
+        merged = torch.zeros(4096, device=dev)
+    stream.synchronize()
+    arena.set_len(0, cached)
+
+    def step(i):
+        if world == 1:
+            arena.set_len(0, P)
+            arena.decode(q, k, v, out, [P], split=args.split)
+            return
+        arena.set_len(0, cached)
+        arena.decode_partials(q, k, v, parts, P, append=owner, split=args.split)
+        allp = all_gather_partials(parts)
+        ctx.lse_merge(MODEL_QWEN3, world, allp, merged)
+
+    K, W = args.steps, args.warmup
+    with torch.cuda.stream(stream):
+        total, per, clk, launches = timed_steps(step, K, W, stream, world, dev, local, ctx)
+    B = 2 * 32768 * 4 * 128 * 2 + 4 * 128 * (2 * 32 + 2 * 4)
+    line = base_line("Qwen3-30B-A3B attention decode tok/s (KV 32768, bf16)", K / (total / 1e3), "tok/s", world, K,
+                     W, total, True, "strong", "bf16",
+                     {"workload": "config3: Qwen3 layer decode, 32 q / 4 kv heads, d=128, bf16 KV, length 32768",
+                      "l2": "67 MB of KV per step (inputs below L2 size; repeated steps partly hit L2)",
+                      "parallelism": "single GPU" if world == 1 else
+                      f"KV length split x{world}, NCCL all-gather of (m,l,O) partials + LSE merge"}, clk, launches)
+    per_rank_bytes = 2 * (e - b) * 4 * 128 * 2
+    line["roofline"] = hbm_roofline(B if world == 1 else per_rank_bytes, per,
+                                    "qx_decode_kernel<Qwen3,bf16,bf16>" + ("" if world == 1 else " + merge"))
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import py_oracle as o
+        from qx_b200 import synthetic as syn
+        o.build()
+        conv = syn.to_bf16_bits
+        qb_, kb_, vb_ = conv(syn.normal(1, (32, 128))), conv(syn.normal(2, (4, 128))), conv(syn.normal(3, (4, 128)))
+        kc = conv(syn.normal(4, (L, 4, 128)))
+        vc = conv(syn.normal(5, (L, 4, 128)))
+        ones = np.ones(128, np.float32)
+        t0 = time.perf_counter()
+        o.qwen_decode(qb_, kb_, vb_, ones, ones, kc, vc, P, o.BF16, threads=1)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": 1.0 / dt, "unit": "tok/s", "cores": 1, "kind": "port",
+                                "sample": "one oracle Qwen decode step (qk-norm RoPE, store, GQA over 32768)"}
+    arena.close()
+    ctx.close()
+    return line
+
+
+def run_config4(args, world, rank, local):
+    """Config 4: 256 independent Granite sequences, lengths U{128..4096}, bf16 KV,
+    one decode step through 24 layers; sequences sharded over ranks by LPT on KV bytes."""
+    import ctypes as C
+    import torch
+    from qx_b200 import BF16, F32, MODEL_GRANITE, Context, KvArena
+    from qx_b200 import _lib
+    from qx_b200 import synthetic as syn
+    from qx_b200.distributed import lpt_shard, sequence_kv_bytes
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    lengths = [int(x) for x in syn.uniform_int(0x51580400, 256, 128, 4096)]
+    assignment, _ = lpt_shard([sequence_kv_bytes(L) for L in lengths], world)
+    mine = assignment[rank]
+    n = len(mine)
+    ctx = Context(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    arena = KvArena(ctx, MODEL_GRANITE, LAYERS, n, 4096, BF16, BF16)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0x51580401 + rank)
+    with torch.cuda.stream(stream):
+        for s, i in enumerate(mine):
+            for l in range(LAYERS):
+                arena.tensor(s, l, True)[:lengths[i] - 1].view(torch.bfloat16).normal_(generator=g)
+                arena.tensor(s, l, False)[:lengths[i] - 1].view(torch.bfloat16).normal_(generator=g)
+        q = torch.randn(n, LAYERS, 1024, device=dev, generator=g)
+        k = torch.randn(n, LAYERS, 512, device=dev, generator=g)
+        v = torch.randn(n, LAYERS, 512, device=dev, generator=g)
+        out = torch.zeros(n, LAYERS, 1024, device=dev)
+    stream.synchronize()
+    positions = [lengths[i] - 1 for i in mine]
+    pos = (C.c_int32 * n)(*positions)
+    dargs = _lib.DecodeArgs(0, LAYERS, n, None, pos, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                            None, None, None, F32, F32, F32, 0, args.split)
+    lib = ctx.lib
+
+    def step(i):
+        for s in range(n):
+            lib.qxc_kv_set_len(arena.handle, s, positions[s])
+        st = lib.qxc_decode(ctx.handle, arena.handle, C.byref(dargs))
+        if st != 0:
+            raise RuntimeError(lib.qxc_last_error(ctx.handle).decode())
+
+    K, W = args.steps, args.warmup
+    total, per, clk, launches = timed_steps(step, K, W, stream, world, dev, local, ctx)
+    my_bytes = sum(LAYERS * (2 * lengths[i] * 8 * 64 * 2 + 4 * 64 * (2 * 16 + 2 * 8)) for i in mine)
+    line = base_line("multi-sequence Granite decode tok/s (256 sequences x 24 layers)", 256 * K / (total / 1e3),
+                     "tok/s", world, K, W, total, True, "strong", "f32 q/k/v, bf16 KV",
+                     {"workload": "config4: 256 Granite sequences, lengths U{128..4096} (seed 0x51580400), "
+                                  "24 layers, bf16 KV, one decode step each",
+                      "l2": "26.6 GB of KV per step",
+                      "parallelism": f"sequences sharded x{world} by LPT on KV bytes, no collective"},
+                     clk, launches)
+    line["roofline"] = hbm_roofline(my_bytes, per, "qx_decode_kernel<Granite,bf16,bf16>")
+    arena.close()
+    ctx.close()
+    return line
+
+
+# ---------------------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------------------
 def run_reference(args, world, rank):
@@ -400,9 +724,10 @@ def main():
     ap.add_argument("--steps", type=int, default=3200)
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config1", choices=["config1"])
+    ap.add_argument("--workload", default="config1", choices=["config0", "config1", "config2", "config3", "config4"])
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
+    ap.add_argument("--prefill-len", type=int, default=2048, help="config2 prompt length (512 or 2048)")
     ap.add_argument("--native-exp", action="store_true", help="hardware exp2 instead of qx's pinned exp_f32")
     ap.add_argument("--e2e-steps", type=int, default=640)
     ap.add_argument("--cpu-steps", type=int, default=16)
@@ -428,7 +753,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     try:
-        line = run_config1(args, world, rank, local)
+        run = {"config0": run_config0, "config1": run_config1, "config2": run_config2, "config3": run_config3,
+               "config4": run_config4}[args.workload]
+        line = run(args, world, rank, local)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

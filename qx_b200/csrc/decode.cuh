@@ -126,13 +126,18 @@ struct DecodeCfg {
   static constexpr int OFF_V = OFF_K + STAGES * STAGE_K;  // 1024-aligned
   static constexpr int OFF_Q = OFF_V + STAGES * STAGE_V;  // float [G][D]
   static constexpr int OFF_P = OFF_Q + G * D * 4;         // float [NWC][WT][G]
-  static constexpr int OFF_NEWK = OFF_P + NWC * WT * G * 4;
+  // Qwen: raw q heads and the k head staged as f32 for the RMSNorm prologue
+  static constexpr int RAW_FLOATS = M::QWEN ? (G + 1) * D : 0;
+  static constexpr int OFF_RAW = OFF_P + NWC * WT * G * 4;
+  static constexpr int OFF_NEWK = OFF_RAW + RAW_FLOATS * 4;
   static constexpr int OFF_NEWV = OFF_NEWK + ((KROW + 15) / 16) * 16;
   static constexpr int OFF_STAT = OFF_NEWV + ((VROW + 15) / 16) * 16;  // float [NWC][G][2], inv[G+1]
   static constexpr int OFF_BAR = ((OFF_STAT + 4 * (NWC * G * 2 + G + 1) + 15) / 16) * 16;
   static constexpr int SMEM = OFF_BAR + 16 * STAGES + 16 + 1024;  // + slack to align the base to 1024
   // after the main loop the stage buffers hold the per-warp merge [NWC][G][D]
   static_assert(NWC * G * D * 4 <= STAGES * (STAGE_K + STAGE_V), "merge buffer must fit the stages");
+  // the last CTA's split merge stages 2 x G x nsplit floats there too
+  static constexpr int MAX_SPLITS = (STAGES * (STAGE_K + STAGE_V)) / (8 * G);
 };
 
 // Byte offset of byte `b` of row `t` inside a swizzled [64][128 B] box stack.
@@ -297,15 +302,21 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
         newk[pair + 32] = Elem<KT>::from_f32(b);
       }
     } else {
-      // Per-head RMSNorm with the reference's sequential sum of squares
-      // (bit-exact K); one thread per head.
+      // Stage the raw q heads (and k) in shared memory with parallel loads,
+      // then per-head RMSNorm with the reference's sequential sum of squares
+      // (bit-exact K); one thread per head sums from shared memory.
+      float* raw = reinterpret_cast<float*>(sm + C::OFF_RAW);  // [G + 1][D]
+      for (int i = tid; i < (G + 1) * D; i += 32 * NWC) {
+        const int g = i / D, e = i - g * D;
+        raw[i] = g < G ? load_any(p.q, qbase + g * D + e, p.q_dtype)
+                       : (has_new ? load_any(p.k, kvbase + e, p.in_dtype) : 0.0f);
+      }
+      consumers_sync(32 * NWC);
       if (tid < G || (tid == G && has_new)) {
-        const bool is_q = tid < G;
+        const float* row = raw + tid * D;
         float sum = 0.0f;
-        for (int i = 0; i < D; ++i) {
-          float x = is_q ? load_any(p.q, qbase + tid * D + i, p.q_dtype) : load_any(p.k, kvbase + i, p.in_dtype);
-          sum = __fadd_rn(sum, __fmul_rn(x, x));
-        }
+#pragma unroll
+        for (int i = 0; i < D; ++i) sum = __fadd_rn(sum, __fmul_rn(row[i], row[i]));
         st_inv[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 128.0f), 1.0e-6f)));
       }
       consumers_sync(32 * NWC);
@@ -316,8 +327,7 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
         const bool is_q = g < G;
         const float inv = st_inv[g];
         const float* wn = is_q ? p.q_norm : p.k_norm;
-        float x = is_q ? load_any(p.q, qbase + g * D + i, p.q_dtype) : load_any(p.k, kvbase + i, p.in_dtype);
-        float y = is_q ? load_any(p.q, qbase + g * D + i + 64, p.q_dtype) : load_any(p.k, kvbase + i + 64, p.in_dtype);
+        const float x = raw[g * D + i], y = raw[g * D + i + 64];
         float left = __fmul_rn(__fmul_rn(x, inv), wn ? wn[i] : 1.0f);
         float right = __fmul_rn(__fmul_rn(y, inv), wn ? wn[64 + i] : 1.0f);
         const float2 cssn = tab[i];
@@ -585,20 +595,57 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
   if (!s_flag[0]) return;
   __threadfence();
 
+  // Merge the nsplit partials of this (sequence, layer, kv head) in three
+  // parallel steps: stage every split's (m, l) in shared memory; one warp
+  // per head reduces M = max m_i and L = sum e^(m_i - M) l_i and leaves the
+  // weights e^(m_i - M); every output then sums nsplit weighted partials
+  // with independent loads (4 accumulators).
   const float* first = p.partials + (long long)(blockIdx.x - s) * G * (D + 2);
+  float* wts = reinterpret_cast<float*>(sm + C::OFF_K);  // [G][nsplit] m_i, then weights
+  float* lsp = wts + G * nsplit;                          // [G][nsplit] l_i
+  float* hml = stat;                                      // [G] M, [G] L
+  for (int i = tid; i < nsplit * G; i += 128) {
+    const int sp = i / G, g = i - sp * G;
+    const float* pi = first + ((long long)sp * G + g) * (D + 2);
+    wts[g * nsplit + sp] = __ldcg(pi + D);
+    lsp[g * nsplit + sp] = __ldcg(pi + D + 1);
+  }
+  combine_sync();
+  for (int g = warp; g < G; g += 4) {
+    float mx = -INFINITY;
+    for (int i = lane; i < nsplit; i += 32) mx = fmaxf(mx, wts[g * nsplit + i]);
+    mx = warp_max(mx);
+    float L = 0.0f;
+    for (int i = lane; i < nsplit; i += 32) {
+      const float w = softmax_exp(wts[g * nsplit + i] - mx, pinned);
+      wts[g * nsplit + i] = w;
+      L = fmaf(w, lsp[g * nsplit + i], L);
+    }
+    L = warp_sum(L);
+    if (lane == 0) {
+      hml[g] = mx;
+      hml[G + g] = L;
+    }
+  }
+  combine_sync();
   bool nonfinite = false;
 #pragma unroll
   for (int k = 0; k < OPT; ++k) {
     const int idx = tid + k * 128, g = idx / D, d = idx % D;
-    float mx = -INFINITY;
-    for (int i = 0; i < nsplit; ++i) mx = fmaxf(mx, __ldcg(first + ((long long)i * G + g) * (D + 2) + D));
-    float L = 0.0f, o = 0.0f;
-    for (int i = 0; i < nsplit; ++i) {
-      const float* pi = first + ((long long)i * G + g) * (D + 2);
-      const float w = softmax_exp(__ldcg(pi + D) - mx, pinned);
-      L = fmaf(w, __ldcg(pi + D + 1), L);
-      o = fmaf(w, __ldcg(pi + d), o);
+    const float* col = first + (long long)g * (D + 2) + d;
+    const long long stride = (long long)G * (D + 2);
+    const float* wg = wts + g * nsplit;
+    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
+    int i = 0;
+    for (; i + 4 <= nsplit; i += 4) {
+      o0 = fmaf(wg[i], __ldcg(col + i * stride), o0);
+      o1 = fmaf(wg[i + 1], __ldcg(col + (i + 1) * stride), o1);
+      o2 = fmaf(wg[i + 2], __ldcg(col + (i + 2) * stride), o2);
+      o3 = fmaf(wg[i + 3], __ldcg(col + (i + 3) * stride), o3);
     }
+    for (; i < nsplit; ++i) o0 = fmaf(wg[i], __ldcg(col + i * stride), o0);
+    const float o = (o0 + o1) + (o2 + o3);
+    const float mx = hml[g], L = hml[G + g];
     if (p.emit_partials) {
       float* dst = reinterpret_cast<float*>(p.out) + (cu * HQ + (long long)h * G + g) * (D + 2);
       dst[d] = o;

@@ -3,8 +3,8 @@
 //
 // Every wait on an mbarrier is bounded: after kMaxWaitNs it gives up,
 // records QX_ERR_BIT_TIMEOUT in the context's error word and returns
-// false, so a kernel never spins forever. No copy issued here uses cluster
-// multicast.
+// false, so a kernel never spins forever. No copy issued here is
+// broadcast to other CTAs.
 #pragma once
 #include <stdint.h>
 

@@ -178,22 +178,36 @@ int decode_blocks_per_sm(const qxc_kv* kv) {
   return blocks_per_sm<Granite, __nv_bfloat16, __nv_bfloat16>();
 }
 
+int decode_max_splits(const qxc_kv* kv) {
+  const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
+  if (kv->desc.model == QXC_MODEL_QWEN3)
+    return kd == QXC_BF16 ? DecodeCfg<Qwen3, __nv_bfloat16, __nv_bfloat16>::MAX_SPLITS
+                          : DecodeCfg<Qwen3, __half, __half>::MAX_SPLITS;
+  if (kd == QXC_F32 && vd == QXC_F32) return DecodeCfg<Granite, float, float>::MAX_SPLITS;
+  if (kd == QXC_F32 && vd == QXC_F16) return DecodeCfg<Granite, float, __half>::MAX_SPLITS;
+  if (kd == QXC_F16 && vd == QXC_F32) return DecodeCfg<Granite, __half, float>::MAX_SPLITS;
+  if (kd == QXC_F16 && vd == QXC_F16) return DecodeCfg<Granite, __half, __half>::MAX_SPLITS;
+  return DecodeCfg<Granite, __nv_bfloat16, __nv_bfloat16>::MAX_SPLITS;
+}
+
 // Positions per split (a multiple of 64). Split-KV exists to fill 148 SMs
 // at small batch; too many splits add per-CTA overhead, and a grid that
 // leaves the last wave nearly empty wastes the tail. Model the time as
 // waves x (64-row tiles per CTA + a fixed per-CTA cost) and take the
 // cheapest split, preferring fewer splits on ties.
-int auto_chunk(int slots, const int* attend, int n, int units_per_seq) {
+int auto_chunk(int slots, const int* attend, int n, int units_per_seq, int max_splits) {
   int max_attend = 1;
   for (int i = 0; i < n; ++i) max_attend = std::max(max_attend, attend[i]);
   const int top = ((max_attend + 63) / 64) * 64;
   double best = 1e300;
   int best_c = top;
   for (int c = top; c >= 64; c -= 64) {
+    if ((max_attend + c - 1) / c > max_splits) break;
     long long items = 0;
     for (int i = 0; i < n; ++i) items += (long long)units_per_seq * ((attend[i] + c - 1) / c);
     const long long waves = (items + slots - 1) / slots;
-    const double cost = (double)waves * (c / 64.0 + 3.0);
+    // + the last CTA's merge, which grows with the split count
+    const double cost = (double)waves * (c / 64.0 + 3.0) + 0.05 * ((max_attend + c - 1) / c);
     if (cost < best - 1e-9) {
       best = cost;
       best_c = c;
@@ -279,7 +293,14 @@ qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* s
                                                        : (kd == QXC_F16 ? 2 : 0) + (vd == QXC_F16 ? 1 : 0);
     int& slots = cached_slots[ctx->device & 63][type];
     if (!slots) slots = ctx->sm_count * decode_blocks_per_sm(kv);
-    chunk = auto_chunk(slots, attend, seq_count, layer_count * kv->hkv);
+    chunk = auto_chunk(slots, attend, seq_count, layer_count * kv->hkv, decode_max_splits(kv));
+  }
+  {
+    int max_attend = 1;
+    for (int i = 0; i < seq_count; ++i) max_attend = std::max(max_attend, attend[i]);
+    if ((max_attend + chunk - 1) / chunk > decode_max_splits(kv))
+      return fail(ctx, QXC_ERR_INVALID_ARG, "split %d gives %d splits; at most %d fit the merge", chunk,
+                  (max_attend + chunk - 1) / chunk, decode_max_splits(kv));
   }
   if (chunk <= 0 || chunk % 64 != 0) return fail(ctx, QXC_ERR_INVALID_ARG, "split %d must be a positive multiple of 64", split);
   out->chunk = chunk;
