@@ -194,6 +194,127 @@ __device__ __forceinline__ int find_slot(const DecodeParams& p, SeqInfo* info) {
   return lo;
 }
 
+// Outputs of one work item, then (when the cache was split) the split merge.
+// Thread tid < 128 holds outputs idx = tid + k*128 (head g = idx / D, dim
+// d = idx % D) as unnormalised O[k] with head max Mg[k] and sum Lg[k].
+// One split: O / L goes straight to `out` (or (O, m, l) when emitting
+// partials). Several: every split stores its (O, m, l) partial; the last
+// CTA of the (sequence, layer, kv head) to finish (atomic ticket, no
+// spinning) merges them by log-sum-exp and resets the ticket.
+// merge_smem must hold 2 * G * nsplit floats, stat_smem 2 * G floats.
+template <int G, int D, int HKV, int HQ, int OPT>
+__device__ __forceinline__ void finish_outputs(const DecodeParams& p, const float* O, const float* Mg, const float* Lg,
+                                               int nsplit, int s, long long cu, int h, int tid, int warp, int lane,
+                                               bool pinned, float* merge_smem, float* stat_smem, int* s_flag) {
+  const long long obase = (cu * HQ + (long long)h * G) * D;
+  if (nsplit == 1) {
+    bool nonfinite = false;
+#pragma unroll
+    for (int k = 0; k < OPT; ++k) {
+      const int idx = tid + k * 128, g = idx / D, d = idx % D;
+      if (p.emit_partials) {
+        float* part = reinterpret_cast<float*>(p.out) + (cu * HQ + (long long)h * G + g) * (D + 2);
+        part[d] = O[k];
+        if (d == 0) {
+          part[D] = Mg[k];
+          part[D + 1] = Lg[k];
+        }
+      } else {
+        const float o = O[k] / Lg[k];
+        nonfinite |= !isfinite(o);
+        store_any(p.out, obase + idx, p.out_dtype, o);
+      }
+    }
+    if (nonfinite) flag_error(p.err, QX_ERR_BIT_NONFINITE);
+    return;
+  }
+
+  float* part = p.partials + (long long)blockIdx.x * G * (D + 2);
+#pragma unroll
+  for (int k = 0; k < OPT; ++k) {
+    const int idx = tid + k * 128, g = idx / D, d = idx % D;
+    part[g * (D + 2) + d] = O[k];
+    if (d == 0) {
+      part[g * (D + 2) + D] = Mg[k];
+      part[g * (D + 2) + D + 1] = Lg[k];
+    }
+  }
+  __threadfence();
+  combine_sync();
+  int* ticket = p.tickets + cu * HKV + h;
+  if (tid == 0) s_flag[0] = (atomicAdd(ticket, 1) == nsplit - 1);
+  combine_sync();
+  if (!s_flag[0]) return;
+  __threadfence();
+
+  // Merge the nsplit partials of this (sequence, layer, kv head) in three
+  // parallel steps: stage every split's (m, l) in shared memory; one warp
+  // per head reduces M = max m_i and L = sum e^(m_i - M) l_i and leaves the
+  // weights e^(m_i - M); every output then sums nsplit weighted partials
+  // with independent loads (4 accumulators).
+  const float* first = p.partials + (long long)(blockIdx.x - s) * G * (D + 2);
+  float* wts = merge_smem;  // [G][nsplit] m_i, then weights
+  float* lsp = wts + G * nsplit;                          // [G][nsplit] l_i
+  float* hml = stat_smem;  // [G] M, [G] L
+  for (int i = tid; i < nsplit * G; i += 128) {
+    const int sp = i / G, g = i - sp * G;
+    const float* pi = first + ((long long)sp * G + g) * (D + 2);
+    wts[g * nsplit + sp] = __ldcg(pi + D);
+    lsp[g * nsplit + sp] = __ldcg(pi + D + 1);
+  }
+  combine_sync();
+  for (int g = warp; g < G; g += 4) {
+    float mx = -INFINITY;
+    for (int i = lane; i < nsplit; i += 32) mx = fmaxf(mx, wts[g * nsplit + i]);
+    mx = warp_max(mx);
+    float L = 0.0f;
+    for (int i = lane; i < nsplit; i += 32) {
+      const float w = softmax_exp(wts[g * nsplit + i] - mx, pinned);
+      wts[g * nsplit + i] = w;
+      L = fmaf(w, lsp[g * nsplit + i], L);
+    }
+    L = warp_sum(L);
+    if (lane == 0) {
+      hml[g] = mx;
+      hml[G + g] = L;
+    }
+  }
+  combine_sync();
+  bool nonfinite = false;
+#pragma unroll
+  for (int k = 0; k < OPT; ++k) {
+    const int idx = tid + k * 128, g = idx / D, d = idx % D;
+    const float* col = first + (long long)g * (D + 2) + d;
+    const long long stride = (long long)G * (D + 2);
+    const float* wg = wts + g * nsplit;
+    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
+    int i = 0;
+    for (; i + 4 <= nsplit; i += 4) {
+      o0 = fmaf(wg[i], __ldcg(col + i * stride), o0);
+      o1 = fmaf(wg[i + 1], __ldcg(col + (i + 1) * stride), o1);
+      o2 = fmaf(wg[i + 2], __ldcg(col + (i + 2) * stride), o2);
+      o3 = fmaf(wg[i + 3], __ldcg(col + (i + 3) * stride), o3);
+    }
+    for (; i < nsplit; ++i) o0 = fmaf(wg[i], __ldcg(col + i * stride), o0);
+    const float o = (o0 + o1) + (o2 + o3);
+    const float mx = hml[g], L = hml[G + g];
+    if (p.emit_partials) {
+      float* dst = reinterpret_cast<float*>(p.out) + (cu * HQ + (long long)h * G + g) * (D + 2);
+      dst[d] = o;
+      if (d == 0) {
+        dst[D] = mx;
+        dst[D + 1] = L;
+      }
+    } else {
+      const float v = o / L;
+      nonfinite |= !isfinite(v);
+      store_any(p.out, obase + idx, p.out_dtype, v);
+    }
+  }
+  if (nonfinite) flag_error(p.err, QX_ERR_BIT_NONFINITE);
+  if (tid == 0) *ticket = 0;  // ready for the next call
+}
+
 template <class M, typename KT, typename VT>
 __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(const __grid_constant__ DecodeParams p) {
   using C = DecodeCfg<M, KT, VT>;
@@ -554,113 +675,8 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
     Lg[k] = L;
   }
 
-  const long long obase = (cu * HQ + (long long)h * G) * D;
-  if (nsplit == 1) {
-    bool nonfinite = false;
-#pragma unroll
-    for (int k = 0; k < OPT; ++k) {
-      const int idx = tid + k * 128, g = idx / D, d = idx % D;
-      if (p.emit_partials) {
-        float* part = reinterpret_cast<float*>(p.out) + (cu * HQ + (long long)h * G + g) * (D + 2);
-        part[d] = O[k];
-        if (d == 0) {
-          part[D] = Mg[k];
-          part[D + 1] = Lg[k];
-        }
-      } else {
-        const float o = O[k] / Lg[k];
-        nonfinite |= !isfinite(o);
-        store_any(p.out, obase + idx, p.out_dtype, o);
-      }
-    }
-    if (nonfinite) flag_error(p.err, QX_ERR_BIT_NONFINITE);
-    return;
-  }
-
-  float* part = p.partials + (long long)blockIdx.x * G * (D + 2);
-#pragma unroll
-  for (int k = 0; k < OPT; ++k) {
-    const int idx = tid + k * 128, g = idx / D, d = idx % D;
-    part[g * (D + 2) + d] = O[k];
-    if (d == 0) {
-      part[g * (D + 2) + D] = Mg[k];
-      part[g * (D + 2) + D + 1] = Lg[k];
-    }
-  }
-  __threadfence();
-  combine_sync();
-  int* ticket = p.tickets + cu * HKV + h;
-  if (tid == 0) s_flag[0] = (atomicAdd(ticket, 1) == nsplit - 1);
-  combine_sync();
-  if (!s_flag[0]) return;
-  __threadfence();
-
-  // Merge the nsplit partials of this (sequence, layer, kv head) in three
-  // parallel steps: stage every split's (m, l) in shared memory; one warp
-  // per head reduces M = max m_i and L = sum e^(m_i - M) l_i and leaves the
-  // weights e^(m_i - M); every output then sums nsplit weighted partials
-  // with independent loads (4 accumulators).
-  const float* first = p.partials + (long long)(blockIdx.x - s) * G * (D + 2);
-  float* wts = reinterpret_cast<float*>(sm + C::OFF_K);  // [G][nsplit] m_i, then weights
-  float* lsp = wts + G * nsplit;                          // [G][nsplit] l_i
-  float* hml = stat;                                      // [G] M, [G] L
-  for (int i = tid; i < nsplit * G; i += 128) {
-    const int sp = i / G, g = i - sp * G;
-    const float* pi = first + ((long long)sp * G + g) * (D + 2);
-    wts[g * nsplit + sp] = __ldcg(pi + D);
-    lsp[g * nsplit + sp] = __ldcg(pi + D + 1);
-  }
-  combine_sync();
-  for (int g = warp; g < G; g += 4) {
-    float mx = -INFINITY;
-    for (int i = lane; i < nsplit; i += 32) mx = fmaxf(mx, wts[g * nsplit + i]);
-    mx = warp_max(mx);
-    float L = 0.0f;
-    for (int i = lane; i < nsplit; i += 32) {
-      const float w = softmax_exp(wts[g * nsplit + i] - mx, pinned);
-      wts[g * nsplit + i] = w;
-      L = fmaf(w, lsp[g * nsplit + i], L);
-    }
-    L = warp_sum(L);
-    if (lane == 0) {
-      hml[g] = mx;
-      hml[G + g] = L;
-    }
-  }
-  combine_sync();
-  bool nonfinite = false;
-#pragma unroll
-  for (int k = 0; k < OPT; ++k) {
-    const int idx = tid + k * 128, g = idx / D, d = idx % D;
-    const float* col = first + (long long)g * (D + 2) + d;
-    const long long stride = (long long)G * (D + 2);
-    const float* wg = wts + g * nsplit;
-    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
-    int i = 0;
-    for (; i + 4 <= nsplit; i += 4) {
-      o0 = fmaf(wg[i], __ldcg(col + i * stride), o0);
-      o1 = fmaf(wg[i + 1], __ldcg(col + (i + 1) * stride), o1);
-      o2 = fmaf(wg[i + 2], __ldcg(col + (i + 2) * stride), o2);
-      o3 = fmaf(wg[i + 3], __ldcg(col + (i + 3) * stride), o3);
-    }
-    for (; i < nsplit; ++i) o0 = fmaf(wg[i], __ldcg(col + i * stride), o0);
-    const float o = (o0 + o1) + (o2 + o3);
-    const float mx = hml[g], L = hml[G + g];
-    if (p.emit_partials) {
-      float* dst = reinterpret_cast<float*>(p.out) + (cu * HQ + (long long)h * G + g) * (D + 2);
-      dst[d] = o;
-      if (d == 0) {
-        dst[D] = mx;
-        dst[D + 1] = L;
-      }
-    } else {
-      const float v = o / L;
-      nonfinite |= !isfinite(v);
-      store_any(p.out, obase + idx, p.out_dtype, v);
-    }
-  }
-  if (nonfinite) flag_error(p.err, QX_ERR_BIT_NONFINITE);
-  if (tid == 0) *ticket = 0;  // ready for the next call
+  finish_outputs<G, D, HKV, HQ, OPT>(p, O, Mg, Lg, nsplit, s, cu, h, tid, warp, lane, pinned,
+                                     reinterpret_cast<float*>(sm + C::OFF_K), stat, s_flag);
 }
 
 // ---- log-sum-exp merge of partial sets (KV-length split across GPUs) -------

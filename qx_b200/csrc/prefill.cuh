@@ -31,13 +31,6 @@
 
 namespace qx {
 
-// Hardware base-2 exponential (MUFU.EX2); exp2(-inf) = +0.
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 struct PrefillParams {
   CUtensorMap tmq;  // rotated queries [L][16][64] bf16: box {64, 1, 64}, 128-byte swizzle
   CUtensorMap tmk;  // key cache [L][8][64] bf16, same box

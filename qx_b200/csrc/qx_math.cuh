@@ -54,6 +54,13 @@ __device__ __forceinline__ float native_exp(float x) {
   return y;
 }
 
+// Hardware base-2 exponential (MUFU.EX2); exp2(-inf) = +0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float softmax_exp(float x, bool pinned) {
   return pinned ? pinned_exp(x) : native_exp(x);
 }

@@ -64,6 +64,12 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int M, int N, bool b_
          ((uint32_t)(M >> 4) << 24);
 }
 
+// kind::f16 with both operands f16 (fmt 0) or both bf16 (fmt 1), f32 accumulate.
+__host__ __device__ constexpr uint32_t umma_idesc_16bit(int M, int N, int fmt, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 // 32 consecutive f32 columns of this thread's TMEM lane (warp w reads lanes
 // 32*(w%4) .. +31; taddr carries that lane base in bits [16,32)).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
@@ -75,6 +81,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 8 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 }  // namespace qx

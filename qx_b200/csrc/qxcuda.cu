@@ -22,6 +22,7 @@
 
 #include "../../include/qxcuda.h"
 #include "decode.cuh"
+#include "decode_tc.cuh"
 #include "prefill.cuh"
 
 using namespace qx;
@@ -167,10 +168,19 @@ int blocks_per_sm() {
   return n > 0 ? n : 1;
 }
 
+template <typename KT>
+int tc_blocks_per_sm() {
+  using C = TcCfg<KT>;
+  cudaFuncSetAttribute(qx_decode_tc_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  int n = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qx_decode_tc_kernel<KT>, C::NT, C::SMEM) != cudaSuccess) n = 1;
+  return n > 0 ? n : 1;
+}
+
 int decode_blocks_per_sm(const qxc_kv* kv) {
   const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
   if (kv->desc.model == QXC_MODEL_QWEN3)
-    return kd == QXC_BF16 ? blocks_per_sm<Qwen3, __nv_bfloat16, __nv_bfloat16>() : blocks_per_sm<Qwen3, __half, __half>();
+    return kd == QXC_BF16 ? tc_blocks_per_sm<__nv_bfloat16>() : tc_blocks_per_sm<__half>();
   if (kd == QXC_F32 && vd == QXC_F32) return blocks_per_sm<Granite, float, float>();
   if (kd == QXC_F32 && vd == QXC_F16) return blocks_per_sm<Granite, float, __half>();
   if (kd == QXC_F16 && vd == QXC_F32) return blocks_per_sm<Granite, __half, float>();
@@ -178,11 +188,13 @@ int decode_blocks_per_sm(const qxc_kv* kv) {
   return blocks_per_sm<Granite, __nv_bfloat16, __nv_bfloat16>();
 }
 
+// Cache rows per pipeline tile: 128 for the tensor-core Qwen kernel, else 64.
+int decode_tile(const qxc_kv* kv) { return kv->desc.model == QXC_MODEL_QWEN3 ? 128 : 64; }
+
 int decode_max_splits(const qxc_kv* kv) {
   const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
   if (kv->desc.model == QXC_MODEL_QWEN3)
-    return kd == QXC_BF16 ? DecodeCfg<Qwen3, __nv_bfloat16, __nv_bfloat16>::MAX_SPLITS
-                          : DecodeCfg<Qwen3, __half, __half>::MAX_SPLITS;
+    return kd == QXC_BF16 ? TcCfg<__nv_bfloat16>::MAX_SPLITS : TcCfg<__half>::MAX_SPLITS;
   if (kd == QXC_F32 && vd == QXC_F32) return DecodeCfg<Granite, float, float>::MAX_SPLITS;
   if (kd == QXC_F32 && vd == QXC_F16) return DecodeCfg<Granite, float, __half>::MAX_SPLITS;
   if (kd == QXC_F16 && vd == QXC_F32) return DecodeCfg<Granite, __half, float>::MAX_SPLITS;
@@ -195,19 +207,19 @@ int decode_max_splits(const qxc_kv* kv) {
 // leaves the last wave nearly empty wastes the tail. Model the time as
 // waves x (64-row tiles per CTA + a fixed per-CTA cost) and take the
 // cheapest split, preferring fewer splits on ties.
-int auto_chunk(int slots, const int* attend, int n, int units_per_seq, int max_splits) {
+int auto_chunk(int slots, const int* attend, int n, int units_per_seq, int max_splits, int tile) {
   int max_attend = 1;
   for (int i = 0; i < n; ++i) max_attend = std::max(max_attend, attend[i]);
-  const int top = ((max_attend + 63) / 64) * 64;
+  const int top = ((max_attend + tile - 1) / tile) * tile;
   double best = 1e300;
   int best_c = top;
-  for (int c = top; c >= 64; c -= 64) {
+  for (int c = top; c >= tile; c -= tile) {
     if ((max_attend + c - 1) / c > max_splits) break;
     long long items = 0;
     for (int i = 0; i < n; ++i) items += (long long)units_per_seq * ((attend[i] + c - 1) / c);
     const long long waves = (items + slots - 1) / slots;
     // + the last CTA's merge, which grows with the split count
-    const double cost = (double)waves * (c / 64.0 + 3.0) + 0.05 * ((max_attend + c - 1) / c);
+    const double cost = (double)waves * ((double)c / tile + 3.0) * tile / 64.0 + 0.05 * ((max_attend + c - 1) / c);
     if (cost < best - 1e-9) {
       best = cost;
       best_c = c;
@@ -234,11 +246,27 @@ qxc_status launch_typed(qxc_ctx* ctx, const DecodeParams& p, int items) {
   return QXC_OK;
 }
 
+template <typename KT>
+qxc_status launch_tc(qxc_ctx* ctx, const DecodeParams& p, int items) {
+  using C = TcCfg<KT>;
+  static unsigned long long configured = 0;
+  const unsigned long long bit = 1ull << (ctx->device & 63);
+  if (!(configured & bit)) {
+    QXC_CUDA(ctx, cudaFuncSetAttribute(qx_decode_tc_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured |= bit;
+  }
+  qx_decode_tc_kernel<KT><<<items, C::NT, C::SMEM, ctx->stream>>>(p);
+  QXC_CUDA(ctx, cudaGetLastError());
+  ctx->launches++;
+  return QXC_OK;
+}
+
 qxc_status launch_decode(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams& p, int items) {
   const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
   if (kv->desc.model == QXC_MODEL_QWEN3) {
-    if (kd == QXC_BF16) return launch_typed<Qwen3, __nv_bfloat16, __nv_bfloat16>(ctx, p, items);
-    return launch_typed<Qwen3, __half, __half>(ctx, p, items);
+    // group-8 attention runs on the tensor cores (decode_tc.cuh)
+    if (kd == QXC_BF16) return launch_tc<__nv_bfloat16>(ctx, p, items);
+    return launch_tc<__half>(ctx, p, items);
   }
   if (kd == QXC_F32 && vd == QXC_F32) return launch_typed<Granite, float, float>(ctx, p, items);
   if (kd == QXC_F32 && vd == QXC_F16) return launch_typed<Granite, float, __half>(ctx, p, items);
@@ -293,7 +321,7 @@ qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* s
                                                        : (kd == QXC_F16 ? 2 : 0) + (vd == QXC_F16 ? 1 : 0);
     int& slots = cached_slots[ctx->device & 63][type];
     if (!slots) slots = ctx->sm_count * decode_blocks_per_sm(kv);
-    chunk = auto_chunk(slots, attend, seq_count, layer_count * kv->hkv, decode_max_splits(kv));
+    chunk = auto_chunk(slots, attend, seq_count, layer_count * kv->hkv, decode_max_splits(kv), decode_tile(kv));
   }
   {
     int max_attend = 1;
@@ -302,7 +330,8 @@ qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* s
       return fail(ctx, QXC_ERR_INVALID_ARG, "split %d gives %d splits; at most %d fit the merge", chunk,
                   (max_attend + chunk - 1) / chunk, decode_max_splits(kv));
   }
-  if (chunk <= 0 || chunk % 64 != 0) return fail(ctx, QXC_ERR_INVALID_ARG, "split %d must be a positive multiple of 64", split);
+  if (chunk <= 0 || chunk % decode_tile(kv) != 0)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "split %d must be a positive multiple of %d", split, decode_tile(kv));
   out->chunk = chunk;
   out->tab.resize(seq_count);
   long long items = 0;

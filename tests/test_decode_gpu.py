@@ -290,7 +290,7 @@ def test_qwen_decode(gpu_ctx, oracle, prefix, dtype):
     out = torch.zeros(1, 4096, device="cuda")
     qrot = torch.zeros(1, 4096, device="cuda")
     arena.decode(tq, tk, tv, out, [prefix], q_rot_out=qrot, q_norm=torch.from_numpy(qn).cuda(),
-                 k_norm=torch.from_numpy(kn).cuda(), split=64 if prefix > 100 else 0)
+                 k_norm=torch.from_numpy(kn).cuda(), split=128 if prefix > 200 else 0)
     gpu_ctx.sync()
     got = out.cpu().numpy()[0]
     assert normwise(got, ref) <= 2e-2
