@@ -82,6 +82,8 @@ qxc_status qxc_sync(qxc_ctx* ctx);
 const char* qxc_last_error(const qxc_ctx* ctx);
 /* Number of kernels this context has launched so far. */
 uint64_t qxc_launch_count(const qxc_ctx* ctx);
+/* Cache positions per split chosen by the last decode call on this context. */
+int32_t qxc_last_split(const qxc_ctx* ctx);
 
 /* ---- KV cache arena ---------------------------------------------------- */
 typedef struct qxc_kv_desc {

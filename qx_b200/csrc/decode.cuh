@@ -85,6 +85,7 @@ struct DecodeParams {
   int q_dtype, in_dtype, out_dtype;
   int pinned_exp;
   int emit_partials;  // write (O, m, l) per query head instead of O / l
+  int external_merge;  // splits only store partials; qx_split_merge_kernel merges them
   float* partials;    // scratch [items][G][D+2]
   int* tickets;       // scratch [n_seq][layer_count][HKV], zero between calls
   unsigned* err;
@@ -239,6 +240,7 @@ __device__ __forceinline__ void finish_outputs(const DecodeParams& p, const floa
       part[g * (D + 2) + D + 1] = Lg[k];
     }
   }
+  if (p.external_merge) return;  // qx_split_merge_kernel, launched next, merges
   __threadfence();
   combine_sync();
   int* ticket = p.tickets + cu * HKV + h;
@@ -280,33 +282,35 @@ __device__ __forceinline__ void finish_outputs(const DecodeParams& p, const floa
     }
   }
   combine_sync();
+  // splits outer, outputs inner: every iteration has OPT independent loads,
+  // and unrolling by 4 keeps 4 x OPT of them in flight
+  const long long stride = (long long)G * (D + 2);
+  float o[OPT];
+#pragma unroll
+  for (int k = 0; k < OPT; ++k) o[k] = 0.0f;
+#pragma unroll 4
+  for (int i = 0; i < nsplit; ++i) {
+    const float* pi = first + i * stride;
+#pragma unroll
+    for (int k = 0; k < OPT; ++k) {
+      const int idx = tid + k * 128, g = idx / D, d = idx % D;
+      o[k] = fmaf(wts[g * nsplit + i], __ldcg(pi + g * (D + 2) + d), o[k]);
+    }
+  }
   bool nonfinite = false;
 #pragma unroll
   for (int k = 0; k < OPT; ++k) {
     const int idx = tid + k * 128, g = idx / D, d = idx % D;
-    const float* col = first + (long long)g * (D + 2) + d;
-    const long long stride = (long long)G * (D + 2);
-    const float* wg = wts + g * nsplit;
-    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
-    int i = 0;
-    for (; i + 4 <= nsplit; i += 4) {
-      o0 = fmaf(wg[i], __ldcg(col + i * stride), o0);
-      o1 = fmaf(wg[i + 1], __ldcg(col + (i + 1) * stride), o1);
-      o2 = fmaf(wg[i + 2], __ldcg(col + (i + 2) * stride), o2);
-      o3 = fmaf(wg[i + 3], __ldcg(col + (i + 3) * stride), o3);
-    }
-    for (; i < nsplit; ++i) o0 = fmaf(wg[i], __ldcg(col + i * stride), o0);
-    const float o = (o0 + o1) + (o2 + o3);
     const float mx = hml[g], L = hml[G + g];
     if (p.emit_partials) {
       float* dst = reinterpret_cast<float*>(p.out) + (cu * HQ + (long long)h * G + g) * (D + 2);
-      dst[d] = o;
+      dst[d] = o[k];
       if (d == 0) {
         dst[D] = mx;
         dst[D + 1] = L;
       }
     } else {
-      const float v = o / L;
+      const float v = o[k] / L;
       nonfinite |= !isfinite(v);
       store_any(p.out, obase + idx, p.out_dtype, v);
     }
@@ -677,6 +681,93 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
 
   finish_outputs<G, D, HKV, HQ, OPT>(p, O, Mg, Lg, nsplit, s, cu, h, tid, warp, lane, pinned,
                                      reinterpret_cast<float*>(sm + C::OFF_K), stat, s_flag);
+}
+
+// ---- split merge as its own kernel (many splits) ----------------------------
+// When a cache is cut into many splits, merging them in the last CTA of each
+// kv head serialises a long chain of L2 reads on 128 threads. This kernel
+// gives every query head of every (sequence, layer) its own CTA of 256
+// threads: the split weights e^(m_i - M) / L are computed once into shared
+// memory, then SPT = 256 / D threads share each output dim and split the
+// sum over the splits between them.
+// Grid: one CTA per (call unit cu, kv head h, query head g of the group);
+// blockIdx.x = (cu * HKV + h) * G + g. The (cu, h) partial rows are found
+// from the same sequence table the decode kernel used.
+template <int G, int D, int HKV, int HQ>
+__global__ void __launch_bounds__(256) qx_split_merge_kernel(const __grid_constant__ DecodeParams p) {
+  constexpr int SPT = 256 / D;  // threads per output dim
+  __shared__ float w_s[2048];
+  __shared__ float red[256];
+  __shared__ float ml[2];
+  const int blk = blockIdx.x;
+  const int g = blk % G, uh = blk / G;
+  const int h = uh % HKV;
+  const long long cu = uh / HKV;
+  const int slot = (int)(cu / p.layer_count), lloc = (int)(cu % p.layer_count);
+  const SeqInfo si = p.seq_table ? p.seq_table[slot] : p.single;
+  const int n = (si.attend + p.chunk - 1) / p.chunk;
+  if (n <= 1) return;  // the decode kernel wrote this head's output itself
+  const long long item0 = si.item_begin + (long long)(lloc * HKV + h) * n;
+  const float* first = p.partials + item0 * G * (D + 2) + (long long)g * (D + 2);
+  const long long stride = (long long)G * (D + 2);
+  const bool pinned = p.pinned_exp != 0;
+  const int tid = threadIdx.x;
+  // M = max m_i
+  float mx = -INFINITY;
+  for (int i = tid; i < n; i += 256) {
+    const float m = __ldcg(first + i * stride + D);
+    w_s[i] = m;
+    mx = fmaxf(mx, m);
+  }
+  red[tid] = mx;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (tid < o) red[tid] = fmaxf(red[tid], red[tid + o]);
+    __syncthreads();
+  }
+  const float M = red[0];
+  __syncthreads();
+  float L = 0.0f;
+  for (int i = tid; i < n; i += 256) {
+    const float w = softmax_exp(w_s[i] - M, pinned);
+    w_s[i] = w;
+    L = fmaf(w, __ldcg(first + i * stride + D + 1), L);
+  }
+  red[tid] = L;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (tid < o) red[tid] += red[tid + o];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    ml[0] = M;
+    ml[1] = red[0];
+  }
+  __syncthreads();
+  const int d = tid % D, part = tid / D;
+  float acc = 0.0f;
+#pragma unroll 8
+  for (int i = part; i < n; i += SPT) acc = fmaf(w_s[i], __ldcg(first + i * stride + d), acc);
+  red[tid] = acc;
+  __syncthreads();
+  if (part == 0) {
+    float o = acc;
+#pragma unroll
+    for (int q = 1; q < SPT; ++q) o += red[q * D + d];
+    const long long qh = (long long)h * G + g;
+    if (p.emit_partials) {
+      float* dst = reinterpret_cast<float*>(p.out) + (cu * HQ + qh) * (D + 2);
+      dst[d] = o;
+      if (d == 0) {
+        dst[D] = ml[0];
+        dst[D + 1] = ml[1];
+      }
+    } else {
+      const float v = o / ml[1];
+      if (!isfinite(v)) flag_error(p.err, QX_ERR_BIT_NONFINITE);
+      store_any(p.out, (cu * HQ + qh) * D + d, p.out_dtype, v);
+    }
+  }
 }
 
 // ---- log-sum-exp merge of partial sets (KV-length split across GPUs) -------

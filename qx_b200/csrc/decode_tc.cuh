@@ -14,9 +14,10 @@
 // Accumulators live in TMEM (32 columns). Thread t of the four consumer
 // warps owns TMEM lane t: position t of S^T (its 8 head scores) and dim t
 // of O^T. The softmax is per head over the tile's 128 positions: warp
-// shuffles plus a four-warp shared-memory step. A producer warp streams
-// 64 KB tiles (K and V) through a two-stage TMA ring; a stage is released
-// when the P.V tcgen05.mma reading it has completed.
+// shuffles plus a four-warp shared-memory step. A producer warp streams K
+// and V (32 KB each per tile) into one buffer each: K is released once the
+// S MMA has read it, so the next tile's K loads during this tile's softmax
+// and P.V; V is released once the P.V MMA has read it.
 //
 // Prologue (RMSNorm with the reference's sequential sum, rotate-half RoPE
 // from the host cos/sin table, the appended row) and the split merge are
@@ -36,10 +37,12 @@ struct TcCfg {
   static constexpr int NPAD = 16;       // MMA N (8 heads + 8 zero rows)
   static constexpr int BLK = T * 128;   // one 64-dim column block [128 rows][128 B]
   static constexpr int STAGE = 2 * BLK;  // K (or V) of one tile: 32 KB
-  static constexpr int STAGES = 2;
+  // One K buffer and one V buffer (78 KB per CTA, two CTAs per SM). The
+  // next tile's K streams in as soon as the S MMA has consumed the current
+  // one, overlapping the softmax and the P.V MMA; V follows after P.V.
   static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = OFF_K + STAGES * STAGE;
-  static constexpr int OFF_Q = OFF_V + STAGES * STAGE;   // 2 blocks [16 rows][128 B]
+  static constexpr int OFF_V = OFF_K + STAGE;
+  static constexpr int OFF_Q = OFF_V + STAGE;            // 2 blocks [16 rows][128 B]
   static constexpr int OFF_P = OFF_Q + 2 * NPAD * 128;   // 2 blocks [16 rows][128 B]
   static constexpr int OFF_RAW = OFF_P + 2 * NPAD * 128;  // f32 [(G + 1)][D]
   static constexpr int OFF_NEWK = OFF_RAW + (G + 1) * D * 4;
@@ -51,7 +54,7 @@ struct TcCfg {
   static constexpr int NT = 160;                     // 4 consumer warps + 1 producer warp
   static constexpr uint32_t TMEM_COLS = 32;          // S^T in [0,16), O^T tile in [16,32)
   static constexpr int FMT = std::is_same<KT, __nv_bfloat16>::value ? 1 : 0;  // MMA operand format
-  static constexpr int MAX_SPLITS = (STAGES * 2 * STAGE) / (8 * G);
+  static constexpr int MAX_SPLITS = (2 * STAGE) / (8 * G);
 };
 
 template <typename KT>
@@ -67,11 +70,15 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
   float* red_sum = red_max + 4 * G;                              // [4][G]
   float* stat = reinterpret_cast<float*>(sm + C::OFF_STAT);     // [2G] merge stats
   float* st_inv = stat + 2 * G;                                  // [G + 1]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
-  uint64_t* empty = full + 2;
-  uint64_t* mbar = full + 4;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 5);
-  int* s_flag = reinterpret_cast<int*>(full + 6);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
+  uint64_t* fullK = bars + 0;   // TMA landed
+  uint64_t* fullV = bars + 1;
+  uint64_t* emptyK = bars + 2;  // buffer free again (its MMA completed)
+  uint64_t* emptyV = bars + 3;
+  uint64_t* mbarS = bars + 4;   // tcgen05.commit of the S MMAs
+  uint64_t* mbarPV = bars + 5;  // tcgen05.commit of the P.V MMAs
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 6);
+  int* s_flag = reinterpret_cast<int*>(bars + 7);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -95,11 +102,7 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
   const bool last_split = (s == nsplit - 1);
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-    }
-    mbar_init(mbar, 1);
+    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);
     s_flag[1] = 0;
     fence_barrier_init();
   }
@@ -118,23 +121,31 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
       prefetch_tmap(&p.tmk);
       prefetch_tmap(&p.tmv);
       const int z0 = (int)(unit * p.capacity) + begin;
+      unsigned char* kt = sm + C::OFF_K;
+      unsigned char* vt = sm + C::OFF_V;
       for (int tile = 0; tile < ntiles; ++tile) {
-        const int st = tile & 1;
-        if (tile >= 2 && !mbar_wait_bounded(&empty[st], (uint32_t)((tile >> 1) - 1) & 1u, p.err)) {
+        const uint32_t prev = (uint32_t)(tile - 1) & 1u;
+        const int z = z0 + tile * T;
+        if (tile >= 1 && !mbar_wait_bounded(emptyK, prev, p.err)) {
           s_flag[1] = 1;
           break;
         }
-        unsigned char* kt = sm + C::OFF_K + st * C::STAGE;
-        unsigned char* vt = sm + C::OFF_V + st * C::STAGE;
-        mbar_arrive_expect_tx(&full[st], 2u * C::STAGE);
-        const int z = z0 + tile * T;
+        mbar_arrive_expect_tx(fullK, (uint32_t)C::STAGE);
 #pragma unroll
         for (int b = 0; b < 2; ++b)
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            tma_load_3d(kt + b * C::BLK + half * 8192, &p.tmk, b * 64, h, z + half * 64, &full[st]);
-            tma_load_3d(vt + b * C::BLK + half * 8192, &p.tmv, b * 64, h, z + half * 64, &full[st]);
-          }
+          for (int half = 0; half < 2; ++half)
+            tma_load_3d(kt + b * C::BLK + half * 8192, &p.tmk, b * 64, h, z + half * 64, fullK);
+        if (tile >= 1 && !mbar_wait_bounded(emptyV, prev, p.err)) {
+          s_flag[1] = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(fullV, (uint32_t)C::STAGE);
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+#pragma unroll
+          for (int half = 0; half < 2; ++half)
+            tma_load_3d(vt + b * C::BLK + half * 8192, &p.tmv, b * 64, h, z + half * 64, fullV);
       }
     }
   } else {
@@ -217,45 +228,33 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
       l_run[g] = 0.0f;
       O[g] = 0.0f;
     }
-    uint32_t mphase = 0;
     bool ok = true;
     // every consumer runs every iteration (the named barriers need all 128);
     // after a timed-out wait a thread stops waiting and the result is discarded
+    unsigned char* kt = sm + C::OFF_K;
+    unsigned char* vt = sm + C::OFF_V;
+    const uint32_t sK = smem_addr(kt), sV = smem_addr(vt);
     for (int tile = 0; tile < ntiles; ++tile) {
-      const int st = tile & 1;
-      if (ok) ok = mbar_wait_bounded(&full[st], (uint32_t)(tile >> 1) & 1u, p.err);
-      unsigned char* kt = sm + C::OFF_K + st * C::STAGE;
-      unsigned char* vt = sm + C::OFF_V + st * C::STAGE;
+      const uint32_t ph = (uint32_t)tile & 1u;
       const int rows = min(T, end - (begin + tile * T));
-      if (has_new && tile == ntiles - 1) {
-        // the appended slot comes from registers, not from the copy
-        if (tid < 16)
-          *reinterpret_cast<uint4*>(kt + swz<C::BLK>(rows - 1, tid * 16)) = reinterpret_cast<const uint4*>(newk)[tid];
-        else if (tid < 32)
-          *reinterpret_cast<uint4*>(vt + swz<C::BLK>(rows - 1, (tid - 16) * 16)) =
-              reinterpret_cast<const uint4*>(newv)[tid - 16];
-      }
-      // rows past the cache end carry zero probability; zero their values so
-      // the tensor core never multiplies 0 by a stale non-finite element
-      for (int i = tid; i < (T - rows) * 16; i += 128) {
-        const int rr = rows + (i >> 4);
-        *reinterpret_cast<uint4*>(vt + swz<C::BLK>(rr, (i & 15) * 16)) = make_uint4(0u, 0u, 0u, 0u);
-      }
+      const bool last = has_new && tile == ntiles - 1;
+      if (ok) ok = mbar_wait_bounded(fullK, ph, p.err);
+      if (last && tid < 16)  // the appended key comes from registers, not from the copy
+        *reinterpret_cast<uint4*>(kt + swz<C::BLK>(rows - 1, tid * 16)) = reinterpret_cast<const uint4*>(newk)[tid];
       fence_proxy_async_shared();
       tc_fence_before();
       consumers_sync(128);
       if (tid == 0) {
         tc_fence_after();
-        const uint32_t sK = smem_addr(kt);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           tc_mma_bf16(tbase, umma_desc_sw128(sK + (kk >> 2) * C::BLK + (kk & 3) * 32, 16, 1024),
                       umma_desc_sw128(sQ + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), IDESC_S, kk > 0);
-        tc_commit(mbar);
+        tc_commit(mbarS);
       }
-      if (ok) ok = mbar_wait_bounded(mbar, mphase, p.err);
-      mphase ^= 1u;
+      if (ok) ok = mbar_wait_bounded(mbarS, ph, p.err);
       tc_fence_after();
+      if (tid == 0) mbar_arrive(emptyK);  // the S MMAs are done with K
       float x[G];
       tmem_ld8(tbase + lane_base, x);
       tmem_wait_ld();
@@ -281,26 +280,33 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
         const float ws = warp_sum(pw);
         if (lane == 0) red_sum[warp * G + g] = ws;
       }
+      if (ok) ok = mbar_wait_bounded(fullV, ph, p.err);
+      if (last && tid < 16)
+        *reinterpret_cast<uint4*>(vt + swz<C::BLK>(rows - 1, tid * 16)) = reinterpret_cast<const uint4*>(newv)[tid];
+      // rows past the cache end carry zero probability; zero their values so
+      // the tensor core never multiplies 0 by a stale non-finite element
+      for (int i = tid; i < (T - rows) * 16; i += 128) {
+        const int rr = rows + (i >> 4);
+        *reinterpret_cast<uint4*>(vt + swz<C::BLK>(rr, (i & 15) * 16)) = make_uint4(0u, 0u, 0u, 0u);
+      }
       fence_proxy_async_shared();
       tc_fence_before();
       consumers_sync(128);
       if (tid == 0) {
         tc_fence_after();
-        const uint32_t sV = smem_addr(vt);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           tc_mma_bf16(tbase + 16, umma_desc_sw128(sV + kk * 2048, C::BLK, 1024),
                       umma_desc_sw128(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), IDESC_PV, kk > 0);
-        tc_commit(mbar);
+        tc_commit(mbarPV);
       }
 #pragma unroll
       for (int g = 0; g < G; ++g)
         l_run[g] = fmaf(l_run[g], alpha[g],
                         (red_sum[g] + red_sum[G + g]) + (red_sum[2 * G + g] + red_sum[3 * G + g]));
-      if (ok) ok = mbar_wait_bounded(mbar, mphase, p.err);
-      mphase ^= 1u;
+      if (ok) ok = mbar_wait_bounded(mbarPV, ph, p.err);
       tc_fence_after();
-      if (tid == 0) mbar_arrive(&empty[st]);  // both MMAs reading this stage are done
+      if (tid == 0) mbar_arrive(emptyV);  // the P.V MMAs are done with V
       float pv[G];
       tmem_ld8(tbase + lane_base + 16, pv);
       tmem_wait_ld();

@@ -10,8 +10,9 @@
 //      query and 8 key heads (same operations as rotate_heads, qx-runtime
 //      lib.rs:2439-2453); keys go into the cache as bf16 (bit-identical to
 //      the oracle), values are copied, rotated queries go to a bf16 scratch;
-//   2. qx_prefill_attn_tc_kernel: one CTA per (64-position query block, kv
-//      head). Its 128 accumulator rows are the kv head's two query heads x
+//   2. qx_prefill_attn_tc_kernel: one CTA per (64-position query block,
+//      chunk of at most kc of its causal key tiles, kv head); the chunks of a
+//      block merge by log-sum-exp in the last one to finish (atomic ticket). Its 128 accumulator rows are the kv head's two query heads x
 //      64 positions, so both heads of the GQA group share every K/V tile.
 //      TMA brings 128-byte-swizzled Q, K and V tiles into shared memory;
 //      one thread issues tcgen05.mma for S = Q K^T (M=128, N=64, K=64) into
@@ -45,7 +46,19 @@ struct PrefillParams {
   int out_dtype;
   int length;
   unsigned* err;
+  // split of the key range: a query block's key tiles 0..qb are cut into
+  // chunks of at most kc tiles, one CTA each; several chunks merge through
+  // partials [item][8 heads][128 rows][68] (O[64], m, l, 2 pad: rows stay
+  // 16-byte aligned for the float4 accesses) and a ticket per block
+  int kc;
+  float* partials;
+  int* tickets;
+  // diagnostics only (QXC_PREFILL_TRACE): per CTA, %globaltimer at stage
+  // boundaries, kTraceSlots entries, written by thread 0
+  unsigned long long* trace;
 };
+
+constexpr int kTraceSlots = 32;
 
 // One CTA per position: sin/cos of the 32 pairs once, 24 heads rotated.
 __global__ void __launch_bounds__(256) qx_prefill_rope_kernel(const __grid_constant__ PrefillParams p) {
@@ -97,8 +110,19 @@ __global__ void __launch_bounds__(128) qx_prefill_attn_tc_kernel(const __grid_co
   uint64_t* mbar = full + 3;  // tcgen05.commit target
   uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 4);
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int qb = blockIdx.x, h = blockIdx.y;
-  const int nk = qb + 1;  // causal: key tiles 0..qb
+  const int h = blockIdx.y;
+  // work item -> (query block qb, chunk c of its key tiles 0..qb)
+  int qb = 0, c = blockIdx.x;
+  for (;;) {
+    const int n = (qb + p.kc) / p.kc;
+    if (c < n) break;
+    c -= n;
+    ++qb;
+  }
+  const int nc = (qb + p.kc) / p.kc;      // chunks of this query block
+  const int item0 = blockIdx.x - c;       // its first chunk's item
+  const int j0 = c * p.kc;                // key tiles [j0, j1)
+  const int j1 = min(j0 + p.kc, qb + 1);
   const uint32_t sQ = smem_addr(sm + C::OFF_Q), sK = smem_addr(sm + C::OFF_K), sV = smem_addr(sm + C::OFF_V),
                  sP = smem_addr(sm + C::OFF_P);
 
@@ -117,15 +141,21 @@ __global__ void __launch_bounds__(128) qx_prefill_attn_tc_kernel(const __grid_co
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
+  unsigned long long* tr = p.trace ? p.trace + ((long long)blockIdx.y * gridDim.x + blockIdx.x) * kTraceSlots : nullptr;
+  int tn = 0;
+  auto mark = [&]() {
+    if (tr && tid == 0 && tn < kTraceSlots) tr[tn++] = global_ns();
+  };
+  mark();  // 0: after TMEM allocation
 
   if (tid == 0) {
     mbar_arrive_expect_tx(qbar, 2 * C::TILE);
     tma_load_3d(sm + C::OFF_Q, &p.tmq, 0, 2 * h, 64 * qb, qbar);
     tma_load_3d(sm + C::OFF_Q + C::TILE, &p.tmq, 0, 2 * h + 1, 64 * qb, qbar);
-    for (int j = 0; j < 2 && j < nk; ++j) {
-      mbar_arrive_expect_tx(&full[j], 2 * C::TILE);
-      tma_load_3d(sm + C::OFF_K + j * C::TILE, &p.tmk, 0, h, 64 * j, &full[j]);
-      tma_load_3d(sm + C::OFF_V + j * C::TILE, &p.tmv, 0, h, 64 * j, &full[j]);
+    for (int t = 0; t < 2 && j0 + t < j1; ++t) {
+      mbar_arrive_expect_tx(&full[t], 2 * C::TILE);
+      tma_load_3d(sm + C::OFF_K + t * C::TILE, &p.tmk, 0, h, 64 * (j0 + t), &full[t]);
+      tma_load_3d(sm + C::OFF_V + t * C::TILE, &p.tmv, 0, h, 64 * (j0 + t), &full[t]);
     }
   }
 
@@ -139,14 +169,16 @@ __global__ void __launch_bounds__(128) qx_prefill_attn_tc_kernel(const __grid_co
   constexpr float SCALE_LOG2 = 0.015625f * 1.4426950408889634f;
 
   bool ok = mbar_wait_bounded(qbar, 0, p.err);
+  mark();  // 1: Q landed
   float m = -INFINITY, l = 0.0f, O[64];
 #pragma unroll
   for (int i = 0; i < 64; ++i) O[i] = 0.0f;
   uint32_t mphase = 0;
 
-  for (int j = 0; j < nk; ++j) {
-    const int s = j & 1;
-    ok &= mbar_wait_bounded(&full[s], (uint32_t)(j >> 1) & 1u, p.err);
+  for (int j = j0; j < j1; ++j) {
+    const int s = (j - j0) & 1;
+    ok &= mbar_wait_bounded(&full[s], (uint32_t)((j - j0) >> 1) & 1u, p.err);
+    mark();  // tile: K/V landed
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
@@ -157,6 +189,7 @@ __global__ void __launch_bounds__(128) qx_prefill_attn_tc_kernel(const __grid_co
     }
     ok &= mbar_wait_bounded(mbar, mphase, p.err);
     mphase ^= 1u;
+    mark();  // tile: S MMA done
     tc_fence_after();
     float sv[64];
     tmem_ld32(tbase + lane_base, sv);
@@ -195,6 +228,7 @@ __global__ void __launch_bounds__(128) qx_prefill_attn_tc_kernel(const __grid_co
     fence_proxy_async_shared();  // generic-proxy stores -> tensor-core reads
     tc_fence_before();
     __syncthreads();
+    mark();  // tile: softmax + P written
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
@@ -205,8 +239,9 @@ __global__ void __launch_bounds__(128) qx_prefill_attn_tc_kernel(const __grid_co
     }
     ok &= mbar_wait_bounded(mbar, mphase, p.err);
     mphase ^= 1u;
+    mark();  // tile: P.V MMA done
     tc_fence_after();
-    if (tid == 0 && j + 2 < nk) {  // both MMAs reading stage s are done
+    if (tid == 0 && j + 2 < j1) {  // both MMAs reading stage s are done
       mbar_arrive_expect_tx(&full[s], 2 * C::TILE);
       tma_load_3d(sm + C::OFF_K + s * C::TILE, &p.tmk, 0, h, 64 * (j + 2), &full[s]);
       tma_load_3d(sm + C::OFF_V + s * C::TILE, &p.tmv, 0, h, 64 * (j + 2), &full[s]);
@@ -222,10 +257,56 @@ __global__ void __launch_bounds__(128) qx_prefill_attn_tc_kernel(const __grid_co
     tc_fence_before();
   }
 
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, C::TMEM_COLS);
+  }
+  mark();  // loop done, TMEM freed
+  bool nonfinite = !ok;
+  const long long ob = ((long long)pos * 16 + qh) * 64;
+  if (nc > 1) {
+    // this chunk's row partial: O (relative to m), m (base-2 units), l
+    float* prow = p.partials + (((long long)(blockIdx.x) * 8 + h) * 128 + r) * 68;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      reinterpret_cast<float4*>(prow)[i] = make_float4(O[4 * i], O[4 * i + 1], O[4 * i + 2], O[4 * i + 3]);
+    prow[64] = m;
+    prow[65] = l;
+    __threadfence();
+    __syncthreads();
+    int* ticket = p.tickets + qb * 8 + h;
+    __shared__ int last;
+    if (tid == 0) last = (atomicAdd(ticket, 1) == nc - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // merge the nc chunks of this row by log-sum-exp
+    float M = -INFINITY;
+    for (int cc = 0; cc < nc; ++cc)
+      M = fmaxf(M, __ldcg(p.partials + (((long long)(item0 + cc) * 8 + h) * 128 + r) * 68 + 64));
+    l = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) O[i] = 0.0f;
+    for (int cc = 0; cc < nc; ++cc) {
+      const float* pc = p.partials + (((long long)(item0 + cc) * 8 + h) * 128 + r) * 68;
+      const float w = fast_exp2(__ldcg(pc + 64) - M);
+      l = fmaf(w, __ldcg(pc + 65), l);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 v4 = __ldcg(reinterpret_cast<const float4*>(pc) + i);
+        O[4 * i] = fmaf(w, v4.x, O[4 * i]);
+        O[4 * i + 1] = fmaf(w, v4.y, O[4 * i + 1]);
+        O[4 * i + 2] = fmaf(w, v4.z, O[4 * i + 2]);
+        O[4 * i + 3] = fmaf(w, v4.w, O[4 * i + 3]);
+      }
+    }
+    if (tid == 0) *ticket = 0;  // ready for the next call
+    mark();  // merge done
+  }
   if (pos < p.length) {
     const float inv = 1.0f / l;
-    const long long ob = ((long long)pos * 16 + qh) * 64;
-    bool nonfinite = !ok;
     if (p.out_dtype == 0) {
       float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + ob);
 #pragma unroll
@@ -239,12 +320,6 @@ __global__ void __launch_bounds__(128) qx_prefill_attn_tc_kernel(const __grid_co
       for (int i = 0; i < 64; ++i) store_any(p.out, ob + i, p.out_dtype, O[i] * inv);
     }
     if (nonfinite) flag_error(p.err, ok ? QX_ERR_BIT_NONFINITE : QX_ERR_BIT_TIMEOUT);
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    tmem_dealloc(tbase, C::TMEM_COLS);
   }
 }
 

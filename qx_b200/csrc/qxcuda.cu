@@ -15,6 +15,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <string>
@@ -53,12 +54,15 @@ struct qxc_ctx {
   char* stage_host = nullptr;
   size_t stage_host_cap = 0;
   unsigned long long launches = 0;
+  int last_split = 0;
   // Qwen RoPE (cos, sin) for every position 0..kQwenMaxPositions-1, shared
   // by all Qwen arenas of this context (created with the first one).
   float2* qwen_rope = nullptr;
-  // prefill's rotated-query scratch (bf16 elements)
+  // prefill's rotated-query scratch (bf16 elements) and chunk-merge tickets
   unsigned short* prefill_q = nullptr;
   size_t prefill_q_cap = 0;
+  int* prefill_tickets = nullptr;
+  size_t prefill_tickets_cap = 0;
 };
 
 constexpr int kQwenMaxPositions = 40960;  // max_position_embeddings, qx-model lib.rs:308
@@ -261,7 +265,29 @@ qxc_status launch_tc(qxc_ctx* ctx, const DecodeParams& p, int items) {
   return QXC_OK;
 }
 
+qxc_status launch_decode_kernel(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams& p, int items);
+
+// Splits beyond which the merge runs as its own kernel.
+constexpr int kInKernelMergeMaxSplits = 8;
+
+qxc_status launch_split_merge(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams& p) {
+  const int blocks = p.n_seq * p.layer_count * kv->hq;
+  if (kv->desc.model == QXC_MODEL_QWEN3)
+    qx_split_merge_kernel<8, 128, 4, 32><<<blocks, 256, 0, ctx->stream>>>(p);
+  else
+    qx_split_merge_kernel<2, 64, 8, 16><<<blocks, 256, 0, ctx->stream>>>(p);
+  QXC_CUDA(ctx, cudaGetLastError());
+  ctx->launches++;
+  return QXC_OK;
+}
+
 qxc_status launch_decode(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams& p, int items) {
+  qxc_status st = launch_decode_kernel(ctx, kv, p, items);
+  if (st != QXC_OK || !p.external_merge) return st;
+  return launch_split_merge(ctx, kv, p);
+}
+
+qxc_status launch_decode_kernel(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams& p, int items) {
   const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
   if (kv->desc.model == QXC_MODEL_QWEN3) {
     // group-8 attention runs on the tensor cores (decode_tc.cuh)
@@ -333,6 +359,7 @@ qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* s
   if (chunk <= 0 || chunk % decode_tile(kv) != 0)
     return fail(ctx, QXC_ERR_INVALID_ARG, "split %d must be a positive multiple of %d", split, decode_tile(kv));
   out->chunk = chunk;
+  ctx->last_split = chunk;
   out->tab.resize(seq_count);
   long long items = 0;
   for (int i = 0; i < seq_count; ++i) {
@@ -382,6 +409,9 @@ qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer
   if (st != QXC_OK) return st;
   p->partials = ctx->partials;
   p->tickets = ctx->tickets;
+  int max_split = 1;
+  for (const SeqInfo& si : plan.tab) max_split = std::max(max_split, (si.attend + plan.chunk - 1) / plan.chunk);
+  p->external_merge = max_split > kInKernelMergeMaxSplits ? 1 : 0;
   return QXC_OK;
 }
 
@@ -528,6 +558,7 @@ void qxc_destroy(qxc_ctx* ctx) {
   cudaFree(ctx->stage_dev);
   cudaFree(ctx->qwen_rope);
   cudaFree(ctx->prefill_q);
+  cudaFree(ctx->prefill_tickets);
   if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -562,6 +593,8 @@ qxc_status qxc_sync(qxc_ctx* ctx) {
 const char* qxc_last_error(const qxc_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
 
 uint64_t qxc_launch_count(const qxc_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+int32_t qxc_last_split(const qxc_ctx* ctx) { return ctx ? ctx->last_split : 0; }
 
 // ---- KV arena ---------------------------------------------------------------
 qxc_status qxc_kv_bytes(const qxc_kv_desc* d, size_t* key_bytes, size_t* value_bytes) {
@@ -982,6 +1015,9 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
   if (st != QXC_OK) return st;
   if (a->layer < 0 || a->layer >= kv->desc.layers) return fail(ctx, QXC_ERR_INVALID_ARG, "layer %d out of range", a->layer);
   if (!a->q || !a->k || !a->v || !a->out) return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
+  // the prefill kernels move q/k/v rows and output rows with 16-byte accesses
+  if (((uintptr_t)a->q | (uintptr_t)a->k | (uintptr_t)a->v | (uintptr_t)a->out) & 15u)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "prefill tensors must be 16-byte aligned");
   if (kv->len[a->seq] != 0)
     return fail(ctx, QXC_ERR_POSITION, "KV position 0 does not follow cache length %d", kv->len[a->seq]);
   if (a->length < 1 || a->length > kv->desc.capacity)
@@ -1010,6 +1046,16 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
   p.out_dtype = a->out_dtype;
   p.length = a->length;
   p.err = ctx->err_dev;
+  // key-range split: the diagonal CTA would otherwise walk all L/64 tiles
+  const int nqb = (a->length + 63) / 64;
+  p.kc = std::max(2, nqb / 4);
+  int items = 0;
+  for (int qb = 0; qb < nqb; ++qb) items += (qb + p.kc) / p.kc;
+  st = grow(ctx, &ctx->partials, &ctx->partials_cap, (size_t)items * 8 * 128 * 68, false);
+  if (st == QXC_OK) st = grow(ctx, &ctx->prefill_tickets, &ctx->prefill_tickets_cap, (size_t)nqb * 8, true);
+  if (st != QXC_OK) return st;
+  p.partials = ctx->partials;
+  p.tickets = ctx->prefill_tickets;
   static unsigned long long configured = 0;
   const unsigned long long bit = 1ull << (ctx->device & 63);
   if (!(configured & bit)) {
@@ -1017,11 +1063,36 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
                                        PrefillCfg::SMEM));
     configured |= bit;
   }
+  // diagnostics: QXC_PREFILL_TRACE=1 prints each CTA's stage timeline (ns)
+  static const bool trace = getenv("QXC_PREFILL_TRACE") != nullptr;
+  unsigned long long* tbuf = nullptr;
+  const size_t tcount = (size_t)items * 8 * kTraceSlots;
+  if (trace) {
+    QXC_CUDA(ctx, cudaMalloc(&tbuf, tcount * sizeof(unsigned long long)));
+    QXC_CUDA(ctx, cudaMemsetAsync(tbuf, 0, tcount * sizeof(unsigned long long), ctx->stream));
+    p.trace = tbuf;
+  }
   qx_prefill_rope_kernel<<<a->length, 256, 0, ctx->stream>>>(p);
   QXC_CUDA(ctx, cudaGetLastError());
-  dim3 grid((a->length + 63) / 64, 8);
+  dim3 grid(items, 8);
   qx_prefill_attn_tc_kernel<<<grid, PrefillCfg::NT, PrefillCfg::SMEM, ctx->stream>>>(p);
   QXC_CUDA(ctx, cudaGetLastError());
+  if (trace) {
+    std::vector<unsigned long long> h(tcount);
+    QXC_CUDA(ctx, cudaMemcpyAsync(h.data(), tbuf, tcount * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                                  ctx->stream));
+    QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    cudaFree(tbuf);
+    unsigned long long t0 = ~0ull;
+    for (unsigned long long v : h)
+      if (v && v < t0) t0 = v;
+    for (size_t cta = 0; cta < (size_t)items * 8; ++cta) {
+      fprintf(stderr, "prefill-trace cta %zu:", cta);
+      for (int i = 0; i < kTraceSlots && h[cta * kTraceSlots + i]; ++i)
+        fprintf(stderr, " %llu", h[cta * kTraceSlots + i] - t0);
+      fprintf(stderr, "\n");
+    }
+  }
   ctx->launches += 2;
   if (!(a->flags & QXC_DECODE_NO_ADVANCE)) kv->len[a->seq] = a->length;
   return QXC_OK;

@@ -107,6 +107,11 @@ class Context:
     def launch_count(self) -> int:
         return int(self.lib.qxc_launch_count(self.handle))
 
+    @property
+    def last_split(self) -> int:
+        """Cache positions per split chosen by the last decode call."""
+        return int(self.lib.qxc_last_split(self.handle))
+
     def lse_merge(self, model: int, n_parts: int, partials, out, out_dtype: int = F32) -> None:
         self.check(self.lib.qxc_lse_merge(self.handle, model, n_parts, _ptr(partials), _ptr(out), out_dtype))
 
