@@ -89,6 +89,7 @@ struct DecodeParams {
   float* partials;    // scratch [items][G][D+2]
   int* tickets;       // scratch [n_seq][layer_count][HKV], zero between calls
   unsigned* err;
+  unsigned long long* trace;  // stage timeline (diagnostics), or null
 };
 
 template <class M, typename KT, typename VT>
@@ -712,6 +713,8 @@ __global__ void __launch_bounds__(256) qx_split_merge_kernel(const __grid_consta
   const long long stride = (long long)G * (D + 2);
   const bool pinned = p.pinned_exp != 0;
   const int tid = threadIdx.x;
+  StageTrace trace(p.trace, blk, tid == 0);
+  trace.mark();  // start
   // M = max m_i
   float mx = -INFINITY;
   for (int i = tid; i < n; i += 256) {
@@ -768,6 +771,7 @@ __global__ void __launch_bounds__(256) qx_split_merge_kernel(const __grid_consta
       store_any(p.out, (cu * HQ + qh) * D + d, p.out_dtype, v);
     }
   }
+  trace.mark();  // done
 }
 
 // ---- log-sum-exp merge of partial sets (KV-length split across GPUs) -------

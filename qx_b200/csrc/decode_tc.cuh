@@ -114,6 +114,8 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
+  StageTrace trace(p.trace, blockIdx.x, tid == 0);
+  trace.mark();  // TMEM allocated
 
   if (warp == 4) {
     // ---- producer: K and V tiles, 4 TMA boxes each ([64 rows][128 B]) ------
@@ -213,6 +215,7 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
       else if (tid < 32) reinterpret_cast<uint4*>(vdst)[tid - 16] = reinterpret_cast<const uint4*>(newv)[tid - 16];
     }
     fence_proxy_async_shared();  // Q / P padding written by threads, read by tcgen05.mma
+    trace.mark();  // prologue done
 
     // ---- consumers: tiles ----------------------------------------------------
     const bool pinned = p.pinned_exp != 0;
@@ -239,6 +242,7 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
       const int rows = min(T, end - (begin + tile * T));
       const bool last = has_new && tile == ntiles - 1;
       if (ok) ok = mbar_wait_bounded(fullK, ph, p.err);
+      trace.mark();  // tile: K landed
       if (last && tid < 16)  // the appended key comes from registers, not from the copy
         *reinterpret_cast<uint4*>(kt + swz<C::BLK>(rows - 1, tid * 16)) = reinterpret_cast<const uint4*>(newk)[tid];
       fence_proxy_async_shared();
@@ -253,6 +257,7 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
         tc_commit(mbarS);
       }
       if (ok) ok = mbar_wait_bounded(mbarS, ph, p.err);
+      trace.mark();  // tile: S MMA done
       tc_fence_after();
       if (tid == 0) mbar_arrive(emptyK);  // the S MMAs are done with K
       float x[G];
@@ -281,6 +286,7 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
         if (lane == 0) red_sum[warp * G + g] = ws;
       }
       if (ok) ok = mbar_wait_bounded(fullV, ph, p.err);
+      trace.mark();  // tile: softmax done, V landed
       if (last && tid < 16)
         *reinterpret_cast<uint4*>(vt + swz<C::BLK>(rows - 1, tid * 16)) = reinterpret_cast<const uint4*>(newv)[tid];
       // rows past the cache end carry zero probability; zero their values so
@@ -305,6 +311,7 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
         l_run[g] = fmaf(l_run[g], alpha[g],
                         (red_sum[g] + red_sum[G + g]) + (red_sum[2 * G + g] + red_sum[3 * G + g]));
       if (ok) ok = mbar_wait_bounded(mbarPV, ph, p.err);
+      trace.mark();  // tile: P.V MMA done
       tc_fence_after();
       if (tid == 0) mbar_arrive(emptyV);  // the P.V MMAs are done with V
       float pv[G];
@@ -329,8 +336,10 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
       tmem_dealloc(tbase, C::TMEM_COLS);
     }
     if (s_flag[1]) return;
+    trace.mark();  // tiles done
     finish_outputs<G, D, HKV, HQ, G>(p, O, Mg, Lg, nsplit, s, cu, h, tid, warp, lane, pinned,
                                      reinterpret_cast<float*>(sm + C::OFF_K), stat, s_flag);
+    trace.mark();  // outputs (or partials) written
     return;
   }
   cta_sync();  // (A) for the producer warp

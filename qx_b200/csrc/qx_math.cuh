@@ -55,10 +55,39 @@ __device__ __forceinline__ float native_exp(float x) {
 }
 
 // Hardware base-2 exponential (MUFU.EX2); exp2(-inf) = +0.
+// 2^a, 2^b for two f32 exponents, evaluated and returned as packed bf16
+// (ex2.approx on bf16x2: the arguments are rounded to bf16 first; a in the
+// low half). Exact zero for -inf.
+__device__ __forceinline__ uint32_t exp2_bf16x2(float a, float b) {
+  const __nv_bfloat162 x = __floats2bfloat162_rn(a, b);
+  uint32_t y;
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(*reinterpret_cast<const uint32_t*>(&x)));
+  return y;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x for x <= 0 on the FMA pipe, for kernels whose exponentials would
+// otherwise all queue on the special-function unit. Cody-Waite split
+// x = n + f with n = round(x) (adding and removing 1.5 * 2^23 rounds to an
+// integer held in the low mantissa bits) and f in [-0.5, 0.5]; 2^f from a
+// degree-3 polynomial fitted here for minimum relative error on that
+// interval (max relative error 7.5e-5, far below the bf16 rounding of its
+// callers); 2^n joins through the exponent field. 0 below 2^-125.
+__device__ __forceinline__ float exp2_poly(float x) {
+  const float xc = fmaxf(x, -125.0f);
+  const float j = __fadd_rn(xc, 12582912.0f);
+  const float n = __fsub_rn(j, 12582912.0f);
+  const float f = __fsub_rn(xc, n);
+  float p = __fmaf_rn(0.05517132207751274f, f, 0.24261054396629333f);
+  p = __fmaf_rn(p, f, 0.6932609677314758f);
+  p = __fmaf_rn(p, f, 0.9999281167984009f);
+  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+  return x < -125.0f ? 0.0f : r;
 }
 
 __device__ __forceinline__ float softmax_exp(float x, bool pinned) {

@@ -32,6 +32,35 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
+// Stage timeline for diagnostics (host switch QXC_TRACE): one writer thread
+// per CTA stores %globaltimer at stage boundaries into kTraceSlots slots of a
+// per-launch buffer; a null buffer makes every mark a no-op.
+constexpr int kTraceSlots = 48;
+
+struct StageTrace {
+  unsigned long long* slot;
+  int n;
+  __device__ __forceinline__ StageTrace(unsigned long long* base, long long cta, bool writer)
+      : slot(base && writer ? base + cta * kTraceSlots : nullptr), n(0) {}
+  __device__ __forceinline__ void mark() {
+    if (slot && n < kTraceSlots) slot[n++] = global_ns();
+  }
+};
+
+// Programmatic dependent launch: the running grid lets the next grid in the
+// stream start its prologue; the dependent grid waits for this grid's
+// completion (and its memory) before touching what it produced.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Named barrier `id` among the `n` threads (a multiple of 32) that execute
+// it; id 0 is the one __syncthreads uses.
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -58,11 +58,10 @@ struct qxc_ctx {
   // Qwen RoPE (cos, sin) for every position 0..kQwenMaxPositions-1, shared
   // by all Qwen arenas of this context (created with the first one).
   float2* qwen_rope = nullptr;
-  // prefill's rotated-query scratch (bf16 elements) and chunk-merge tickets
+  float2* granite_rope = nullptr;  // pinned (sin, cos) [4096][32], built on first prefill
+  // prefill's rotated-query scratch (bf16 elements)
   unsigned short* prefill_q = nullptr;
   size_t prefill_q_cap = 0;
-  int* prefill_tickets = nullptr;
-  size_t prefill_tickets_cap = 0;
 };
 
 constexpr int kQwenMaxPositions = 40960;  // max_position_embeddings, qx-model lib.rs:308
@@ -234,6 +233,39 @@ int auto_chunk(int slots, const int* attend, int n, int units_per_seq, int max_s
 
 using KernelFn = void (*)(DecodeParams);
 
+// Diagnostics: with QXC_TRACE set in the environment, a launch gets a zeroed
+// stage-timeline buffer (kTraceSlots per CTA) and, once it completes, one
+// line per CTA goes to stderr: "<kernel> trace cta N: t0 t1 ..." in absolute
+// %globaltimer nanoseconds. Tracing synchronises the stream after every
+// launch and allocates, so it cannot run under stream capture.
+struct TraceRun {
+  qxc_ctx* ctx;
+  const char* name;
+  size_t ctas;
+  unsigned long long* buf = nullptr;
+  TraceRun(qxc_ctx* c, const char* n, size_t k) : ctx(c), name(n), ctas(k) {
+    static const bool on = getenv("QXC_TRACE") != nullptr;
+    if (!on) return;
+    if (cudaMalloc(&buf, ctas * kTraceSlots * sizeof(unsigned long long)) != cudaSuccess) {
+      buf = nullptr;
+      return;
+    }
+    cudaMemsetAsync(buf, 0, ctas * kTraceSlots * sizeof(unsigned long long), ctx->stream);
+  }
+  ~TraceRun() {
+    if (!buf) return;
+    std::vector<unsigned long long> h(ctas * kTraceSlots);
+    cudaMemcpyAsync(h.data(), buf, h.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost, ctx->stream);
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(buf);
+    for (size_t cta = 0; cta < ctas; ++cta) {
+      fprintf(stderr, "%s trace cta %zu:", name, cta);
+      for (int i = 0; i < kTraceSlots && h[cta * kTraceSlots + i]; ++i) fprintf(stderr, " %llu", h[cta * kTraceSlots + i]);
+      fprintf(stderr, "\n");
+    }
+  }
+};
+
 template <class M, typename KT, typename VT>
 qxc_status launch_typed(qxc_ctx* ctx, const DecodeParams& p, int items) {
   using C = DecodeCfg<M, KT, VT>;
@@ -281,9 +313,17 @@ qxc_status launch_split_merge(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams
   return QXC_OK;
 }
 
-qxc_status launch_decode(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams& p, int items) {
-  qxc_status st = launch_decode_kernel(ctx, kv, p, items);
+qxc_status launch_decode(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams& p0, int items) {
+  DecodeParams p = p0;
+  qxc_status st;
+  {
+    TraceRun tr(ctx, "decode", items);
+    p.trace = tr.buf;
+    st = launch_decode_kernel(ctx, kv, p, items);
+  }
   if (st != QXC_OK || !p.external_merge) return st;
+  TraceRun tr(ctx, "merge", (size_t)p.n_seq * p.layer_count * kv->hq);
+  p.trace = tr.buf;
   return launch_split_merge(ctx, kv, p);
 }
 
@@ -478,6 +518,21 @@ qxc_status encode_tile_map(qxc_ctx* ctx, CUtensorMap* map, void* base, int dtype
   return QXC_OK;
 }
 
+qxc_status ensure_granite_rope(qxc_ctx* ctx) {
+  if (ctx->granite_rope) return QXC_OK;
+  float2* tab = nullptr;
+  QXC_CUDA(ctx, cudaMalloc(&tab, (size_t)kGraniteRopePositions * 32 * sizeof(float2)));
+  qx_granite_rope_table_kernel<<<kGraniteRopePositions * 32 / 256, 256, 0, ctx->stream>>>(tab, ctx->err_dev);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFree(tab);
+    return fail(ctx, QXC_ERR_CUDA, "CUDA error: %s", cudaGetErrorString(e));
+  }
+  ctx->launches++;
+  ctx->granite_rope = tab;
+  return QXC_OK;
+}
+
 qxc_status ensure_qwen_rope(qxc_ctx* ctx) {
   if (ctx->qwen_rope) return QXC_OK;
   // cos/sin of position * 1e6^(-i/64) with the platform's single-precision
@@ -557,8 +612,8 @@ void qxc_destroy(qxc_ctx* ctx) {
   }
   cudaFree(ctx->stage_dev);
   cudaFree(ctx->qwen_rope);
+  cudaFree(ctx->granite_rope);
   cudaFree(ctx->prefill_q);
-  cudaFree(ctx->prefill_tickets);
   if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -1030,8 +1085,11 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
   // rotated-query scratch, L x 16 x 64 bf16
   st = grow(ctx, &ctx->prefill_q, &ctx->prefill_q_cap, (size_t)a->length * 1024, false);
   if (st != QXC_OK) return st;
+  st = ensure_granite_rope(ctx);
+  if (st != QXC_OK) return st;
   PrefillParams p;
   memset(&p, 0, sizeof(p));
+  p.rope = ctx->granite_rope;
   st = encode_tile_map(ctx, &p.tmq, ctx->prefill_q, QXC_BF16, 16, 64, a->length, 64);
   if (st == QXC_OK) st = encode_tile_map(ctx, &p.tmk, kc, QXC_BF16, 8, 64, a->length, 64);
   if (st == QXC_OK) st = encode_tile_map(ctx, &p.tmv, vc, QXC_BF16, 8, 64, a->length, 64);
@@ -1046,16 +1104,8 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
   p.out_dtype = a->out_dtype;
   p.length = a->length;
   p.err = ctx->err_dev;
-  // key-range split: the diagonal CTA would otherwise walk all L/64 tiles
   const int nqb = (a->length + 63) / 64;
-  p.kc = std::max(2, nqb / 4);
-  int items = 0;
-  for (int qb = 0; qb < nqb; ++qb) items += (qb + p.kc) / p.kc;
-  st = grow(ctx, &ctx->partials, &ctx->partials_cap, (size_t)items * 8 * 128 * 68, false);
-  if (st == QXC_OK) st = grow(ctx, &ctx->prefill_tickets, &ctx->prefill_tickets_cap, (size_t)nqb * 8, true);
-  if (st != QXC_OK) return st;
-  p.partials = ctx->partials;
-  p.tickets = ctx->prefill_tickets;
+  p.nqb = nqb;
   static unsigned long long configured = 0;
   const unsigned long long bit = 1ull << (ctx->device & 63);
   if (!(configured & bit)) {
@@ -1063,36 +1113,25 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
                                        PrefillCfg::SMEM));
     configured |= bit;
   }
-  // diagnostics: QXC_PREFILL_TRACE=1 prints each CTA's stage timeline (ns)
-  static const bool trace = getenv("QXC_PREFILL_TRACE") != nullptr;
-  unsigned long long* tbuf = nullptr;
-  const size_t tcount = (size_t)items * 8 * kTraceSlots;
-  if (trace) {
-    QXC_CUDA(ctx, cudaMalloc(&tbuf, tcount * sizeof(unsigned long long)));
-    QXC_CUDA(ctx, cudaMemsetAsync(tbuf, 0, tcount * sizeof(unsigned long long), ctx->stream));
-    p.trace = tbuf;
-  }
-  qx_prefill_rope_kernel<<<a->length, 256, 0, ctx->stream>>>(p);
+  TraceRun tr(ctx, "prefill", (size_t)nqb * 8 * 3);  // softmax timeline, then the two MMA issuers'
+  p.trace = tr.buf;
+  qx_prefill_rope_kernel<<<(a->length + kRopePositions - 1) / kRopePositions, 256, 0, ctx->stream>>>(p);
   QXC_CUDA(ctx, cudaGetLastError());
-  dim3 grid(items, 8);
-  qx_prefill_attn_tc_kernel<<<grid, PrefillCfg::NT, PrefillCfg::SMEM, ctx->stream>>>(p);
-  QXC_CUDA(ctx, cudaGetLastError());
-  if (trace) {
-    std::vector<unsigned long long> h(tcount);
-    QXC_CUDA(ctx, cudaMemcpyAsync(h.data(), tbuf, tcount * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
-                                  ctx->stream));
-    QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-    cudaFree(tbuf);
-    unsigned long long t0 = ~0ull;
-    for (unsigned long long v : h)
-      if (v && v < t0) t0 = v;
-    for (size_t cta = 0; cta < (size_t)items * 8; ++cta) {
-      fprintf(stderr, "prefill-trace cta %zu:", cta);
-      for (int i = 0; i < kTraceSlots && h[cta * kTraceSlots + i]; ++i)
-        fprintf(stderr, " %llu", h[cta * kTraceSlots + i] - t0);
-      fprintf(stderr, "\n");
-    }
-  }
+  // the attention grid is a programmatic dependent of the RoPE grid: its CTAs
+  // initialise barriers and TMEM while the RoPE grid drains, and wait for it
+  // (griddepcontrol.wait) before the first TMA load
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(nqb * 8);
+  cfg.blockDim = dim3(PrefillCfg::NT);
+  cfg.dynamicSmemBytes = PrefillCfg::SMEM;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QXC_CUDA(ctx, cudaLaunchKernelEx(&cfg, qx_prefill_attn_tc_kernel, p));
   ctx->launches += 2;
   if (!(a->flags & QXC_DECODE_NO_ADVANCE)) kv->len[a->seq] = a->length;
   return QXC_OK;
