@@ -86,6 +86,7 @@ struct DecodeParams {
   int pinned_exp;
   int emit_partials;  // write (O, m, l) per query head instead of O / l
   int external_merge;  // splits only store partials; qx_split_merge_kernel merges them
+  int early_trigger;   // one-wave grid: let the merge grid launch at once (griddepcontrol)
   float* partials;    // scratch [items][G][D+2]
   int* tickets;       // scratch [n_seq][layer_count][HKV], zero between calls
   unsigned* err;
@@ -323,6 +324,7 @@ __device__ __forceinline__ void finish_outputs(const DecodeParams& p, const floa
 template <class M, typename KT, typename VT>
 __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(const __grid_constant__ DecodeParams p) {
   using C = DecodeCfg<M, KT, VT>;
+  if (p.early_trigger) pdl_launch_dependents();  // the merge grid may get resident meanwhile
   constexpr int D = M::D, G = M::G, HKV = M::HKV, HQ = M::HQ, T = C::T, NWC = C::NWC, WT = C::WT;
   constexpr int QPL = C::QPL, DPL = C::DPL, STAGES = C::STAGES;
   extern __shared__ __align__(1024) unsigned char sm_raw[];
@@ -340,6 +342,19 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
   int* s_flag = reinterpret_cast<int*>(empty + STAGES);  // [0] last-CTA flag, [1] abort
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+#pragma unroll
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);  // the four warps of the group that consumes the stage
+    }
+    s_flag[1] = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  // launched as a programmatic dependent: everything above overlapped the
+  // previous grid; from here on its memory is visible
+  pdl_wait();
 
   // ---- work item ---------------------------------------------------------
   SeqInfo si;
@@ -361,16 +376,6 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
   const long long cu = (long long)slot * p.layer_count + lloc;  // packed q/k/v/out index
   const bool last_split = (s == nsplit - 1);
 
-  if (tid == 0) {
-#pragma unroll
-    for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 4);  // the four warps of the group that consumes the stage
-    }
-    s_flag[1] = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
 
   if (warp == NWC) {
     // ---- producer warp: TMA boxes into the stage ring -----------------------
@@ -686,24 +691,32 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
 
 // ---- split merge as its own kernel (many splits) ----------------------------
 // When a cache is cut into many splits, merging them in the last CTA of each
-// kv head serialises a long chain of L2 reads on 128 threads. This kernel
-// gives every query head of every (sequence, layer) its own CTA of 256
-// threads: the split weights e^(m_i - M) / L are computed once into shared
-// memory, then SPT = 256 / D threads share each output dim and split the
-// sum over the splits between them.
-// Grid: one CTA per (call unit cu, kv head h, query head g of the group);
-// blockIdx.x = (cu * HKV + h) * G + g. The (cu, h) partial rows are found
-// from the same sequence table the decode kernel used.
+// kv head serialises a long chain of L2 reads on one CTA. Here four lanes
+// share each output dim: lane q of the quad loads (m_i, l_i, O_i[d]) of
+// splits i = q, q + 4, ... (kMergeLoads of them per pass, all in flight at
+// once), and the quad combines its log-sum-exp terms with shuffles. The
+// kernel has no shared memory and little code, so its CTAs can be resident
+// beside the decode CTAs: it is launched as a programmatic dependent of the
+// decode grid and waits for it (and its memory) in griddepcontrol.wait.
+// Grid: one CTA per 32 output dims of one (call unit cu, kv head h, query
+// head g of the group): blockIdx.x = ((cu * HKV + h) * G + g) * (D / 32) +
+// dim block. The (cu, h) partial rows are found from the same sequence table
+// the decode kernel used.
+constexpr int kMergeLoads = 16;
+
 template <int G, int D, int HKV, int HQ>
-__global__ void __launch_bounds__(256) qx_split_merge_kernel(const __grid_constant__ DecodeParams p) {
-  constexpr int SPT = 256 / D;  // threads per output dim
-  __shared__ float w_s[2048];
-  __shared__ float red[256];
-  __shared__ float ml[2];
+__global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_constant__ DecodeParams p) {
+  const int tid = threadIdx.x, q = tid & 3;
   const int blk = blockIdx.x;
-  const int g = blk % G, uh = blk / G;
+  const int d = (blk % (D / 32)) * 32 + (tid >> 2);
+  const int row = blk / (D / 32);
+  const int g = row % G, uh = row / G;
   const int h = uh % HKV;
   const long long cu = uh / HKV;
+  StageTrace trace(p.trace, blk, tid == 0);
+  pdl_launch_dependents();  // the next grid may get resident meanwhile
+  pdl_wait();  // the decode grid's partials
+  trace.mark();  // start
   const int slot = (int)(cu / p.layer_count), lloc = (int)(cu % p.layer_count);
   const SeqInfo si = p.seq_table ? p.seq_table[slot] : p.single;
   const int n = (si.attend + p.chunk - 1) / p.chunk;
@@ -712,61 +725,50 @@ __global__ void __launch_bounds__(256) qx_split_merge_kernel(const __grid_consta
   const float* first = p.partials + item0 * G * (D + 2) + (long long)g * (D + 2);
   const long long stride = (long long)G * (D + 2);
   const bool pinned = p.pinned_exp != 0;
-  const int tid = threadIdx.x;
-  StageTrace trace(p.trace, blk, tid == 0);
-  trace.mark();  // start
-  // M = max m_i
-  float mx = -INFINITY;
-  for (int i = tid; i < n; i += 256) {
-    const float m = __ldcg(first + i * stride + D);
-    w_s[i] = m;
-    mx = fmaxf(mx, m);
-  }
-  red[tid] = mx;
-  __syncthreads();
-  for (int o = 128; o > 0; o >>= 1) {
-    if (tid < o) red[tid] = fmaxf(red[tid], red[tid + o]);
-    __syncthreads();
-  }
-  const float M = red[0];
-  __syncthreads();
-  float L = 0.0f;
-  for (int i = tid; i < n; i += 256) {
-    const float w = softmax_exp(w_s[i] - M, pinned);
-    w_s[i] = w;
-    L = fmaf(w, __ldcg(first + i * stride + D + 1), L);
-  }
-  red[tid] = L;
-  __syncthreads();
-  for (int o = 128; o > 0; o >>= 1) {
-    if (tid < o) red[tid] += red[tid + o];
-    __syncthreads();
-  }
-  if (tid == 0) {
-    ml[0] = M;
-    ml[1] = red[0];
-  }
-  __syncthreads();
-  const int d = tid % D, part = tid / D;
-  float acc = 0.0f;
-#pragma unroll 8
-  for (int i = part; i < n; i += SPT) acc = fmaf(w_s[i], __ldcg(first + i * stride + d), acc);
-  red[tid] = acc;
-  __syncthreads();
-  if (part == 0) {
-    float o = acc;
+  float M = -INFINITY, L = 0.0f, o = 0.0f;
+  for (int base = 0; base < n; base += 4 * kMergeLoads) {
+    float mv[kMergeLoads], lv[kMergeLoads], ov[kMergeLoads];
 #pragma unroll
-    for (int q = 1; q < SPT; ++q) o += red[q * D + d];
+    for (int k = 0; k < kMergeLoads; ++k) {
+      const int i = base + q + 4 * k;
+      const float* pi = first + (long long)i * stride;
+      mv[k] = i < n ? __ldcg(pi + D) : -INFINITY;
+      lv[k] = i < n ? __ldcg(pi + D + 1) : 0.0f;
+      ov[k] = i < n ? __ldcg(pi + d) : 0.0f;
+    }
+    float mx = mv[0];
+#pragma unroll
+    for (int k = 1; k < kMergeLoads; ++k) mx = fmaxf(mx, mv[k]);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float Mn = fmaxf(M, mx);
+    const float a = M == -INFINITY ? 0.0f : softmax_exp(M - Mn, pinned);
+    float Ls = 0.0f, os = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kMergeLoads; ++k) {
+      const float w = mv[k] == -INFINITY ? 0.0f : softmax_exp(mv[k] - Mn, pinned);
+      Ls = fmaf(w, lv[k], Ls);
+      os = fmaf(w, ov[k], os);
+    }
+    Ls += __shfl_xor_sync(0xffffffffu, Ls, 1);
+    os += __shfl_xor_sync(0xffffffffu, os, 1);
+    Ls += __shfl_xor_sync(0xffffffffu, Ls, 2);
+    os += __shfl_xor_sync(0xffffffffu, os, 2);
+    L = fmaf(L, a, Ls);
+    o = fmaf(o, a, os);
+    M = Mn;
+  }
+  if (q == 0) {
     const long long qh = (long long)h * G + g;
     if (p.emit_partials) {
       float* dst = reinterpret_cast<float*>(p.out) + (cu * HQ + qh) * (D + 2);
       dst[d] = o;
       if (d == 0) {
-        dst[D] = ml[0];
-        dst[D + 1] = ml[1];
+        dst[D] = M;
+        dst[D + 1] = L;
       }
     } else {
-      const float v = o / ml[1];
+      const float v = o / L;
       if (!isfinite(v)) flag_error(p.err, QX_ERR_BIT_NONFINITE);
       store_any(p.out, (cu * HQ + qh) * D + d, p.out_dtype, v);
     }

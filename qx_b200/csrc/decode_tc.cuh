@@ -8,16 +8,19 @@
 //   S^T [128 rows x 16]  = K [128 rows x 128 dims] . Q^T      (tcgen05.mma
 //       M=128, N=16 = the 8 query heads padded with zero rows, K=128;
 //       K straight from its TMA tile, 128-byte swizzle, K-major)
-//   O^T [128 dims x 16] = V^T [128 dims x 128 rows] . P^T      (M=128 dims,
+//   O^T [128 dims x 16] += V^T [128 dims x 128 rows] . P^T     (M=128 dims,
 //       V consumed MN-major from the same kind of tile, P^T K-major)
 //
-// Accumulators live in TMEM (32 columns). Thread t of the four consumer
-// warps owns TMEM lane t: position t of S^T (its 8 head scores) and dim t
-// of O^T. The softmax is per head over the tile's 128 positions: warp
-// shuffles plus a four-warp shared-memory step. A producer warp streams K
-// and V (32 KB each per tile) into one buffer each: K is released once the
-// S MMA has read it, so the next tile's K loads during this tile's softmax
-// and P.V; V is released once the P.V MMA has read it.
+// One CTA per SM streams its split through a three-stage ring of K tiles and
+// one of V tiles (warp 4: lane 0 loads K, lane 1 loads V). Warp 5 issues the
+// MMAs: S(t+1) goes out before P(t).V, so the scores of the next tile are
+// ready when the softmax of this one ends. O^T accumulates in TMEM across
+// the whole split. The softmax (warps 0-3, thread t = cache row t of the
+// tile) keeps one max per head for the CTA and takes P = 2^(s - m) against
+// it; m moves only when some row exceeds it by 2^8, and only then does the
+// CTA reduce the tile's max and rescale O^T in TMEM and its row-sum
+// partials. Each thread sums its own rows' P per head; the sums meet once,
+// after the last tile.
 //
 // Prologue (RMSNorm with the reference's sequential sum, rotate-half RoPE
 // from the host cos/sin table, the appended row) and the split merge are
@@ -34,54 +37,82 @@ template <typename KT>
 struct TcCfg {
   static constexpr int T = 128;  // cache rows per tile
   static constexpr int D = 128, G = 8, HKV = 4, HQ = 32;
-  static constexpr int NPAD = 16;       // MMA N (8 heads + 8 zero rows)
-  static constexpr int BLK = T * 128;   // one 64-dim column block [128 rows][128 B]
+  static constexpr int NPAD = 16;        // MMA N (8 heads + 8 zero rows)
+  static constexpr int BLK = T * 128;    // one 64-dim column block [128 rows][128 B]
   static constexpr int STAGE = 2 * BLK;  // K (or V) of one tile: 32 KB
-  // One K buffer and one V buffer (78 KB per CTA, two CTAs per SM). The
-  // next tile's K streams in as soon as the S MMA has consumed the current
-  // one, overlapping the softmax and the P.V MMA; V follows after P.V.
+  static constexpr int NS = 3;           // ring stages of K and of V
   static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = OFF_K + STAGE;
-  static constexpr int OFF_Q = OFF_V + STAGE;            // 2 blocks [16 rows][128 B]
-  static constexpr int OFF_P = OFF_Q + 2 * NPAD * 128;   // 2 blocks [16 rows][128 B]
-  static constexpr int OFF_RAW = OFF_P + 2 * NPAD * 128;  // f32 [(G + 1)][D]
+  static constexpr int OFF_V = OFF_K + NS * STAGE;
+  static constexpr int OFF_Q = OFF_V + NS * STAGE;             // 2 blocks [16 rows][128 B]
+  static constexpr int OFF_P = OFF_Q + 2 * NPAD * 128;         // 2 buffers x 2 blocks [16 rows][128 B]
+  static constexpr int OFF_RAW = OFF_P + 2 * 2 * NPAD * 128;   // f32 [(G + 1)][D]
   static constexpr int OFF_NEWK = OFF_RAW + (G + 1) * D * 4;
   static constexpr int OFF_NEWV = OFF_NEWK + D * 2;
-  static constexpr int OFF_RED = OFF_NEWV + D * 2;  // f32 [2][4 warps][G]
-  static constexpr int OFF_STAT = OFF_RED + 2 * 4 * G * 4;  // f32 [2 * G]; inv [G + 1]
+  static constexpr int OFF_RED = OFF_NEWV + D * 2;         // f32 [4 warps][G], then u32 [2][4] flags
+  static constexpr int OFF_STAT = OFF_RED + 4 * G * 4 + 32;  // f32 [2 * G]; inv [G + 1]
   static constexpr int OFF_BAR = ((OFF_STAT + 4 * (3 * G + 1) + 15) / 16) * 16;
-  static constexpr int SMEM = OFF_BAR + 64 + 1024;  // + slack to align the base to 1024
-  static constexpr int NT = 160;                     // 4 consumer warps + 1 producer warp
-  static constexpr uint32_t TMEM_COLS = 32;          // S^T in [0,16), O^T tile in [16,32)
+  static constexpr int NBAR = 4 * NS + 2 + 2 + 2 + 3;
+  static constexpr int SMEM = OFF_BAR + (NBAR + 2) * 8 + 1024;  // + TMEM slot and flags, + slack to align
+  static constexpr int NT = 192;  // consumer warps 0-3, TMA warp 4, MMA warp 5
+  static constexpr uint32_t TMEM_COLS = 64;  // S^T buffers [0,16) [16,32); O^T [32,48)
   static constexpr int FMT = std::is_same<KT, __nv_bfloat16>::value ? 1 : 0;  // MMA operand format
-  static constexpr int MAX_SPLITS = (2 * STAGE) / (8 * G);
+  static constexpr int MAX_SPLITS = 1024;
+  static constexpr float TAU = 8.0f;  // base-2 headroom of the lazily moved max
 };
 
 template <typename KT>
-__global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_constant__ DecodeParams p) {
   using C = TcCfg<KT>;
-  constexpr int D = C::D, G = C::G, HKV = C::HKV, HQ = C::HQ, T = C::T;
+  if (p.early_trigger) pdl_launch_dependents();  // the merge grid may get resident meanwhile
+  constexpr int D = C::D, G = C::G, HKV = C::HKV, HQ = C::HQ, T = C::T, NS = C::NS;
   extern __shared__ __align__(1024) unsigned char sm_raw[];
   unsigned char* sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
   float* raw = reinterpret_cast<float*>(sm + C::OFF_RAW);
   KT* newk = reinterpret_cast<KT*>(sm + C::OFF_NEWK);
   KT* newv = reinterpret_cast<KT*>(sm + C::OFF_NEWV);
-  float* red_max = reinterpret_cast<float*>(sm + C::OFF_RED);  // [4][G]
-  float* red_sum = red_max + 4 * G;                              // [4][G]
-  float* stat = reinterpret_cast<float*>(sm + C::OFF_STAT);     // [2G] merge stats
-  float* st_inv = stat + 2 * G;                                  // [G + 1]
+  float* red = reinterpret_cast<float*>(sm + C::OFF_RED);  // [4][G]
+  uint32_t* red_flag = reinterpret_cast<uint32_t*>(red + 4 * G);  // [tile parity][4 warps]
+  float* stat = reinterpret_cast<float*>(sm + C::OFF_STAT);      // [2G] merge stats
+  float* st_inv = stat + 2 * G;                                   // [G + 1]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
-  uint64_t* fullK = bars + 0;   // TMA landed
-  uint64_t* fullV = bars + 1;
-  uint64_t* emptyK = bars + 2;  // buffer free again (its MMA completed)
-  uint64_t* emptyV = bars + 3;
-  uint64_t* mbarS = bars + 4;   // tcgen05.commit of the S MMAs
-  uint64_t* mbarPV = bars + 5;  // tcgen05.commit of the P.V MMAs
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 6);
-  int* s_flag = reinterpret_cast<int*>(bars + 7);
+  uint64_t* kfull = bars;           // [NS] K tile landed
+  uint64_t* kempty = kfull + NS;    // [NS] S MMA done with the K stage
+  uint64_t* vfull = kempty + NS;    // [NS] V tile landed
+  uint64_t* vempty = vfull + NS;    // [NS] P.V MMA done with the V stage
+  uint64_t* sfull = vempty + NS;    // [2] S^T in TMEM
+  uint64_t* pfull = sfull + 2;      // [2] P^T written by the four consumer warps
+  uint64_t* pdone = pfull + 2;      // [2] P.V of that P^T completed (buffer free, O^T current)
+  uint64_t* qready = pdone + 2;     // Q in shared memory
+  uint64_t* kpatch = qready + 1;    // the appended key is in its K stage
+  uint64_t* mdone = kpatch + 1;     // every MMA completed
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mdone + 1);
+  int* s_flag = reinterpret_cast<int*>(mdone + 2);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+  if (tid == 0) {
+    for (int i = 0; i < 4 * NS; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sfull[i], 1);
+      mbar_init(&pfull[i], 4);
+      mbar_init(&pdone[i], 1);
+    }
+    mbar_init(qready, 1);
+    mbar_init(kpatch, 1);
+    mbar_init(mdone, 1);
+    s_flag[1] = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // launched as a programmatic dependent: everything above overlapped the
+  // previous grid; from here on its memory is visible
+  pdl_wait();
   SeqInfo si;
   const int slot = find_slot(p, &si);
   const int nsplit = (si.attend + p.chunk - 1) / p.chunk;
@@ -100,70 +131,102 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
   const int ntiles = (end - begin + T - 1) / T;
   const long long cu = (long long)slot * p.layer_count + lloc;
   const bool last_split = (s == nsplit - 1);
+  const int last_rows = end - (begin + (ntiles - 1) * T);  // rows of the last tile
 
-  if (tid == 0) {
-    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);
-    s_flag[1] = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(tslot, C::TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
   const uint32_t tbase = *tslot;
   StageTrace trace(p.trace, blockIdx.x, tid == 0);
   trace.mark();  // TMEM allocated
+  bool ok = true;
 
   if (warp == 4) {
-    // ---- producer: K and V tiles, 4 TMA boxes each ([64 rows][128 B]) ------
-    if (lane == 0) {
-      prefetch_tmap(&p.tmk);
-      prefetch_tmap(&p.tmv);
+    // ---- TMA producers: lane 0 streams K tiles, lane 1 V tiles (4 boxes of [64 rows][128 B] each)
+    if (lane < 2) {
+      const CUtensorMap* map = lane == 0 ? &p.tmk : &p.tmv;
+      uint64_t* full = lane == 0 ? kfull : vfull;
+      uint64_t* empty = lane == 0 ? kempty : vempty;
+      unsigned char* ring = sm + (lane == 0 ? C::OFF_K : C::OFF_V);
+      prefetch_tmap(map);
       const int z0 = (int)(unit * p.capacity) + begin;
-      unsigned char* kt = sm + C::OFF_K;
-      unsigned char* vt = sm + C::OFF_V;
-      for (int tile = 0; tile < ntiles; ++tile) {
-        const uint32_t prev = (uint32_t)(tile - 1) & 1u;
-        const int z = z0 + tile * T;
-        if (tile >= 1 && !mbar_wait_bounded(emptyK, prev, p.err)) {
-          s_flag[1] = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(fullK, (uint32_t)C::STAGE);
+      for (int t = 0; t < ntiles; ++t) {
+        const int st = t % NS;
+        if (t >= NS) ok &= mbar_wait_bounded(&empty[st], (uint32_t)(t / NS - 1) & 1u, p.err);
+        mbar_arrive_expect_tx(&full[st], (uint32_t)C::STAGE);
 #pragma unroll
         for (int b = 0; b < 2; ++b)
 #pragma unroll
           for (int half = 0; half < 2; ++half)
-            tma_load_3d(kt + b * C::BLK + half * 8192, &p.tmk, b * 64, h, z + half * 64, fullK);
-        if (tile >= 1 && !mbar_wait_bounded(emptyV, prev, p.err)) {
-          s_flag[1] = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(fullV, (uint32_t)C::STAGE);
-#pragma unroll
-        for (int b = 0; b < 2; ++b)
-#pragma unroll
-          for (int half = 0; half < 2; ++half)
-            tma_load_3d(vt + b * C::BLK + half * 8192, &p.tmv, b * 64, h, z + half * 64, fullV);
+            tma_load_3d(ring + st * C::STAGE + b * C::BLK + half * 8192, map, b * 64, h, z0 + t * T + half * 64,
+                        &full[st]);
       }
+      // no copy may still be landing when the CTA exits
+      for (int t = ntiles > NS ? ntiles - NS : 0; t < ntiles; ++t)
+        ok &= mbar_wait_bounded(&full[t % NS], (uint32_t)(t / NS) & 1u, p.err);
     }
+  } else if (warp == 5) {
+    // ---- MMA issuer ----------------------------------------------------------
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = umma_idesc_16bit(128, C::NPAD, C::FMT, false, false);
+      constexpr uint32_t IDESC_PV = umma_idesc_16bit(128, C::NPAD, C::FMT, true, false);
+      const uint32_t sQ = smem_addr(sm + C::OFF_Q), sP = smem_addr(sm + C::OFF_P);
+      const uint32_t sK = smem_addr(sm + C::OFF_K), sV = smem_addr(sm + C::OFF_V);
+      ok &= mbar_wait_bounded(qready, 0, p.err);
+      // S^T(t) into buffer t & 1: its previous reader, the softmax of t-2,
+      // finished before P(t-2) was handed over, i.e. before P(t-2).V issued
+      auto issue_s = [&](int t) {
+        const int st = t % NS, b = t & 1;
+        ok &= mbar_wait_bounded(&kfull[st], (uint32_t)(t / NS) & 1u, p.err);
+        if (has_new && t == ntiles - 1) ok &= mbar_wait_bounded(kpatch, 0, p.err);
+        tc_fence_after();
+        const uint32_t kb = sK + st * C::STAGE;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_bf16(tbase + 16 * b, umma_desc_sw128(kb + (kk >> 2) * C::BLK + (kk & 3) * 32, 16, 1024),
+                      umma_desc_sw128(sQ + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), IDESC_S, kk > 0);
+        tc_commit(&sfull[b]);
+        tc_commit(&kempty[st]);
+      };
+      // O^T += V^T(t) . P^T(t)
+      auto issue_pv = [&](int t) {
+        const int st = t % NS, b = t & 1;
+        ok &= mbar_wait_bounded(&pfull[b], (uint32_t)(t >> 1) & 1u, p.err);
+        ok &= mbar_wait_bounded(&vfull[st], (uint32_t)(t / NS) & 1u, p.err);
+        tc_fence_after();
+        const uint32_t vb = sV + st * C::STAGE, pb = sP + b * 2 * 2048;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_bf16(tbase + 32, umma_desc_sw128(vb + kk * 2048, C::BLK, 1024),
+                      umma_desc_sw128(pb + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), IDESC_PV,
+                      (t > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&pdone[b]);
+        tc_commit(&vempty[st]);
+      };
+      issue_s(0);
+      for (int t = 0; t < ntiles; ++t) {
+        if (t + 1 < ntiles) issue_s(t + 1);
+        issue_pv(t);
+      }
+      tc_commit(mdone);  // TMEM is released only after every MMA completed
+      ok &= mbar_wait_bounded(mdone, 0, p.err);
+    }
+    if (!ok) s_flag[1] = 1;
   } else {
-    // ---- consumers: prologue ------------------------------------------------
+    // ---- consumers: prologue, one round of global loads --------------------
     const long long qbase = (cu * HQ + (long long)h * G) * D;
     const long long kvbase = (cu * HKV + h) * D;
-    bool bad = false;
+    const int pi = tid & 63;  // the rotation pair of every prologue item of this thread
     for (int i = tid; i < (G + 1) * D; i += 128) {
       const int g = i / D, e = i - g * D;
       raw[i] = g < G ? load_any(p.q, qbase + g * D + e, p.q_dtype)
                      : (has_new ? load_any(p.k, kvbase + e, p.in_dtype) : 0.0f);
     }
-    // zero the padding rows 8..15 of Q and P (both column blocks)
-    for (int i = tid; i < 4 * 128; i += 128) {
-      const int blk = i >> 7, j = i & 127;  // blk 0,1: Q blocks; 2,3: P blocks
-      unsigned char* base = sm + (blk < 2 ? C::OFF_Q : C::OFF_P) + (blk & 1) * 2048 + 1024;
+    const float2 cssn = p.rope_table[(long long)si.rope_pos * 64 + pi];
+    const float wq0 = p.q_norm ? p.q_norm[pi] : 1.0f, wq1 = p.q_norm ? p.q_norm[64 + pi] : 1.0f;
+    const float wk0 = p.k_norm ? p.k_norm[pi] : 1.0f, wk1 = p.k_norm ? p.k_norm[64 + pi] : 1.0f;
+    const float vnew = has_new ? load_any(p.v, kvbase + tid, p.in_dtype) : 0.0f;
+    // zero the padding rows 8..15 of Q and of both P^T buffers (both column blocks)
+    for (int i = tid; i < 6 * 128; i += 128) {
+      const int blk = i >> 7, j = i & 127;  // blk 0,1: Q blocks; 2..5: P blocks
+      unsigned char* base = sm + (blk < 2 ? C::OFF_Q + blk * 2048 : C::OFF_P + (blk - 2) * 2048) + 1024;
       reinterpret_cast<uint2*>(base)[j] = make_uint2(0u, 0u);
     }
     consumers_sync(128);
@@ -175,162 +238,173 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
       st_inv[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 128.0f), 1.0e-6f)));
     }
     consumers_sync(128);
-    const float2* tab = p.rope_table + (long long)si.rope_pos * 64;
+    bool bad = false;
     for (int idx = tid; idx < (G + 1) * 64; idx += 128) {
-      const int g = idx >> 6, i = idx & 63;
+      const int g = idx >> 6;
       if (g == G && !has_new) break;
       const bool is_q = g < G;
       const float inv = st_inv[g];
-      const float* wn = is_q ? p.q_norm : p.k_norm;
-      const float x = raw[g * D + i], y = raw[g * D + i + 64];
-      const float left = __fmul_rn(__fmul_rn(x, inv), wn ? wn[i] : 1.0f);
-      const float right = __fmul_rn(__fmul_rn(y, inv), wn ? wn[64 + i] : 1.0f);
-      const float2 cssn = tab[i];
+      const float x = raw[g * D + pi], y = raw[g * D + pi + 64];
+      const float left = __fmul_rn(__fmul_rn(x, inv), is_q ? wq0 : wk0);
+      const float right = __fmul_rn(__fmul_rn(y, inv), is_q ? wq1 : wk1);
       const float a = __fsub_rn(__fmul_rn(left, cssn.x), __fmul_rn(right, cssn.y));
       const float b = __fadd_rn(__fmul_rn(right, cssn.x), __fmul_rn(left, cssn.y));
       bad |= !(isfinite(a) && isfinite(b));
       const KT ka = Elem<KT>::from_f32(a), kb = Elem<KT>::from_f32(b);
       if (is_q) {
-        // Q row g (K-major, 128-byte swizzle): dims i and i+64 in blocks 0 and 1
-        const int c = (i & 63) >> 3, off = (i & 7) * 2;
+        // Q row g (K-major, 128-byte swizzle): dims pi and pi+64 in blocks 0 and 1
+        const int c = pi >> 3, off = (pi & 7) * 2;
         *reinterpret_cast<KT*>(sm + C::OFF_Q + g * 128 + ((c ^ (g & 7)) << 4) + off) = ka;
         *reinterpret_cast<KT*>(sm + C::OFF_Q + 2048 + g * 128 + ((c ^ (g & 7)) << 4) + off) = kb;
         if (p.q_rot_out && last_split) {
-          p.q_rot_out[qbase + g * D + i] = Elem<KT>::to_f32(ka);
-          p.q_rot_out[qbase + g * D + i + 64] = Elem<KT>::to_f32(kb);
+          p.q_rot_out[qbase + g * D + pi] = Elem<KT>::to_f32(ka);
+          p.q_rot_out[qbase + g * D + pi + 64] = Elem<KT>::to_f32(kb);
         }
       } else {
-        newk[i] = ka;
-        newk[i + 64] = kb;
+        newk[pi] = ka;
+        newk[pi + 64] = kb;
       }
     }
-    if (has_new)
-      for (int i = tid; i < D; i += 128) newv[i] = Elem<KT>::from_f32(load_any(p.v, kvbase + i, p.in_dtype));
+    if (has_new) newv[tid] = Elem<KT>::from_f32(vnew);
     if (bad) flag_error(p.err, QX_ERR_BIT_NONFINITE);
+    fence_proxy_async_shared();  // Q and the P padding are read by tcgen05.mma
     consumers_sync(128);
+    if (tid == 0) mbar_arrive(qready);
     if (has_new) {
       char* kdst = const_cast<char*>(kunit) + ((long long)si.new_slot * HKV + h) * (D * 2);
       char* vdst = const_cast<char*>(vunit) + ((long long)si.new_slot * HKV + h) * (D * 2);
       if (tid < 16) reinterpret_cast<uint4*>(kdst)[tid] = reinterpret_cast<const uint4*>(newk)[tid];
       else if (tid < 32) reinterpret_cast<uint4*>(vdst)[tid - 16] = reinterpret_cast<const uint4*>(newv)[tid - 16];
     }
-    fence_proxy_async_shared();  // Q / P padding written by threads, read by tcgen05.mma
     trace.mark();  // prologue done
 
     // ---- consumers: tiles ----------------------------------------------------
     const bool pinned = p.pinned_exp != 0;
     constexpr float SCALE_LOG2 = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
-    constexpr uint32_t IDESC_S = umma_idesc_16bit(128, C::NPAD, C::FMT, false, false);
-    constexpr uint32_t IDESC_PV = umma_idesc_16bit(128, C::NPAD, C::FMT, true, false);
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const uint32_t sQ = smem_addr(sm + C::OFF_Q), sP = smem_addr(sm + C::OFF_P);
-    float m_run[G], l_run[G], O[G];
+    unsigned char* kring = sm + C::OFF_K;
+    unsigned char* vring = sm + C::OFF_V;
+    float m_run[G], l_part[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       m_run[g] = -INFINITY;
-      l_run[g] = 0.0f;
-      O[g] = 0.0f;
+      l_part[g] = 0.0f;
     }
-    bool ok = true;
-    // every consumer runs every iteration (the named barriers need all 128);
-    // after a timed-out wait a thread stops waiting and the result is discarded
-    unsigned char* kt = sm + C::OFF_K;
-    unsigned char* vt = sm + C::OFF_V;
-    const uint32_t sK = smem_addr(kt), sV = smem_addr(vt);
-    for (int tile = 0; tile < ntiles; ++tile) {
-      const uint32_t ph = (uint32_t)tile & 1u;
-      const int rows = min(T, end - (begin + tile * T));
-      const bool last = has_new && tile == ntiles - 1;
-      if (ok) ok = mbar_wait_bounded(fullK, ph, p.err);
-      trace.mark();  // tile: K landed
-      if (last && tid < 16)  // the appended key comes from registers, not from the copy
-        *reinterpret_cast<uint4*>(kt + swz<C::BLK>(rows - 1, tid * 16)) = reinterpret_cast<const uint4*>(newk)[tid];
-      fence_proxy_async_shared();
-      tc_fence_before();
-      consumers_sync(128);
-      if (tid == 0) {
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          tc_mma_bf16(tbase, umma_desc_sw128(sK + (kk >> 2) * C::BLK + (kk & 3) * 32, 16, 1024),
-                      umma_desc_sw128(sQ + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), IDESC_S, kk > 0);
-        tc_commit(mbarS);
+    // P^T column tid (a cache row) of head g: K-major, 128-byte swizzle
+    const int pb = tid >> 6, pc = (tid & 63) >> 3, poff = (tid & 7) * 2;
+    for (int t = 0; t < ntiles; ++t) {
+      const int b = t & 1, st = t % NS;
+      const bool last = t == ntiles - 1;
+      const int rows = last ? last_rows : T;
+      if (last && has_new) {
+        // the appended key comes from registers, not from the copy
+        ok &= mbar_wait_bounded(&kfull[st], (uint32_t)(t / NS) & 1u, p.err);
+        if (tid < 16)
+          *reinterpret_cast<uint4*>(kring + st * C::STAGE + swz<C::BLK>(rows - 1, tid * 16)) =
+              reinterpret_cast<const uint4*>(newk)[tid];
+        fence_proxy_async_shared();
+        consumers_sync(128);
+        if (tid == 0) mbar_arrive(kpatch);
       }
-      if (ok) ok = mbar_wait_bounded(mbarS, ph, p.err);
-      trace.mark();  // tile: S MMA done
+      ok &= mbar_wait_bounded(&sfull[b], (uint32_t)(t >> 1) & 1u, p.err);
+      __syncwarp();
       tc_fence_after();
-      if (tid == 0) mbar_arrive(emptyK);  // the S MMAs are done with K
       float x[G];
-      tmem_ld8(tbase + lane_base, x);
-      tmem_wait_ld();
+      tmem_ld8_sync(tbase + lane_base + 16 * b, x);
+#pragma unroll
+      for (int g = 0; g < G; ++g) x[g] = tid < rows ? x[g] * SCALE_LOG2 : -INFINITY;
+      trace.mark();  // tile: scores read
+      // does any row raise a head's max past its headroom?
+      uint32_t raise = 0;
+#pragma unroll
+      for (int g = 0; g < G; ++g) raise |= (x[g] > m_run[g] + C::TAU ? 1u : 0u) << g;
+      raise = __reduce_or_sync(0xffffffffu, raise);
+      // (two flag sets: a warp may write tile t+1's while another still reads tile t's)
+      uint32_t* flags = red_flag + 4 * b;
+      if (lane == 0) flags[warp] = raise;
+      consumers_sync(128);
+      raise = flags[0] | flags[1] | flags[2] | flags[3];
+      if (raise) {
+        // the tile's max of the raised heads, then O^T and the row sums
+        // rescaled to it (once the previous P.V has landed in O^T)
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float wm = warp_max(x[g]);
+          if (lane == 0) red[warp * G + g] = wm;
+        }
+        consumers_sync(128);
+        float alpha[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          alpha[g] = 1.0f;
+          if (raise & (1u << g)) {
+            const float tmax = fmaxf(fmaxf(red[g], red[G + g]), fmaxf(red[2 * G + g], red[3 * G + g]));
+            alpha[g] = m_run[g] == -INFINITY ? 0.0f : fast_exp2(m_run[g] - tmax);
+            m_run[g] = tmax;
+          }
+          l_part[g] *= alpha[g];
+        }
+        if (t > 0) {
+          ok &= mbar_wait_bounded(&pdone[(t - 1) & 1], (uint32_t)((t - 1) >> 1) & 1u, p.err);
+          __syncwarp();
+          tc_fence_after();
+          float o[G];
+          tmem_ld8_sync(tbase + lane_base + 32, o);  // thread tid = dim tid, 8 heads
+#pragma unroll
+          for (int g = 0; g < G; ++g) o[g] *= alpha[g];
+          tmem_st8(tbase + lane_base + 32, o);
+          tmem_wait_st();
+          tc_fence_before();
+        }
+        consumers_sync(128);  // red[] is rewritten by the next raise
+      }
+      // P^T buffer b was last read by P(t-2).V
+      if (t >= 2) ok &= mbar_wait_bounded(&pdone[b], (uint32_t)((t - 2) >> 1) & 1u, p.err);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        x[g] = tid < rows ? x[g] * SCALE_LOG2 : -INFINITY;
-        const float wm = warp_max(x[g]);
-        if (lane == 0) red_max[warp * G + g] = wm;
+        const KT pw = Elem<KT>::from_f32(fast_exp2(x[g] - m_run[g]));
+        l_part[g] += Elem<KT>::to_f32(pw);  // the sum of exactly the P the MMA sees
+        *reinterpret_cast<KT*>(sm + C::OFF_P + b * 4096 + pb * 2048 + g * 128 + ((pc ^ (g & 7)) << 4) + poff) = pw;
       }
-      consumers_sync(128);
-      float alpha[G];
-      const int pb = tid >> 6, pc = (tid & 63) >> 3, poff = (tid & 7) * 2;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float tmax = fmaxf(fmaxf(red_max[g], red_max[G + g]), fmaxf(red_max[2 * G + g], red_max[3 * G + g]));
-        const float mnew = fmaxf(m_run[g], tmax);
-        alpha[g] = (m_run[g] == -INFINITY) ? 0.0f : fast_exp2(m_run[g] - mnew);
-        const float pw = fast_exp2(x[g] - mnew);
-        m_run[g] = mnew;
-        // P^T row g (a head), column tid (a position): K-major, 128-byte swizzle
-        *reinterpret_cast<KT*>(sm + C::OFF_P + pb * 2048 + g * 128 + ((pc ^ (g & 7)) << 4) + poff) =
-            Elem<KT>::from_f32(pw);
-        const float ws = warp_sum(pw);
-        if (lane == 0) red_sum[warp * G + g] = ws;
+      if (last) {
+        // rows past the cache end carry zero probability; zero their values
+        // so the tensor core never multiplies 0 by a stale non-finite element
+        ok &= mbar_wait_bounded(&vfull[st], (uint32_t)(t / NS) & 1u, p.err);
+        unsigned char* vt = vring + st * C::STAGE;
+        if (has_new && tid < 16)
+          *reinterpret_cast<uint4*>(vt + swz<C::BLK>(rows - 1, tid * 16)) = reinterpret_cast<const uint4*>(newv)[tid];
+        for (int i = tid; i < (T - rows) * 16; i += 128) {
+          const int rr = rows + (i >> 4);
+          *reinterpret_cast<uint4*>(vt + swz<C::BLK>(rr, (i & 15) * 16)) = make_uint4(0u, 0u, 0u, 0u);
+        }
       }
-      if (ok) ok = mbar_wait_bounded(fullV, ph, p.err);
-      trace.mark();  // tile: softmax done, V landed
-      if (last && tid < 16)
-        *reinterpret_cast<uint4*>(vt + swz<C::BLK>(rows - 1, tid * 16)) = reinterpret_cast<const uint4*>(newv)[tid];
-      // rows past the cache end carry zero probability; zero their values so
-      // the tensor core never multiplies 0 by a stale non-finite element
-      for (int i = tid; i < (T - rows) * 16; i += 128) {
-        const int rr = rows + (i >> 4);
-        *reinterpret_cast<uint4*>(vt + swz<C::BLK>(rr, (i & 15) * 16)) = make_uint4(0u, 0u, 0u, 0u);
-      }
-      fence_proxy_async_shared();
-      tc_fence_before();
-      consumers_sync(128);
-      if (tid == 0) {
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          tc_mma_bf16(tbase + 16, umma_desc_sw128(sV + kk * 2048, C::BLK, 1024),
-                      umma_desc_sw128(sP + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), IDESC_PV, kk > 0);
-        tc_commit(mbarPV);
-      }
-#pragma unroll
-      for (int g = 0; g < G; ++g)
-        l_run[g] = fmaf(l_run[g], alpha[g],
-                        (red_sum[g] + red_sum[G + g]) + (red_sum[2 * G + g] + red_sum[3 * G + g]));
-      if (ok) ok = mbar_wait_bounded(mbarPV, ph, p.err);
-      trace.mark();  // tile: P.V MMA done
-      tc_fence_after();
-      if (tid == 0) mbar_arrive(emptyV);  // the P.V MMAs are done with V
-      float pv[G];
-      tmem_ld8(tbase + lane_base + 16, pv);
-      tmem_wait_ld();
-#pragma unroll
-      for (int g = 0; g < G; ++g) O[g] = fmaf(O[g], alpha[g], pv[g]);
-      tc_fence_before();
+      fence_proxy_async_shared();  // P^T (and the patched V) are read by tcgen05.mma
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pfull[b]);
+      trace.mark();  // tile: P written
     }
-    if (!ok) s_flag[1] = 1;
-    // thread tid = dim, k = head for finish_outputs
+    // O^T of the split (thread tid = dim tid, 8 heads) once the last P.V landed
+    ok &= mbar_wait_bounded(&pdone[(ntiles - 1) & 1], (uint32_t)((ntiles - 1) >> 1) & 1u, p.err);
+    __syncwarp();
+    tc_fence_after();
+    float O[G];
+    tmem_ld8_sync(tbase + lane_base + 32, O);
+    // the row-sum partials of the four warps
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float ws = warp_sum(l_part[g]);
+      if (lane == 0) red[warp * G + g] = ws;
+    }
+    consumers_sync(128);
     float Mg[G], Lg[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       Mg[g] = m_run[g] / 1.4426950408889634f;  // back to the natural-log domain of the partials
-      Lg[g] = l_run[g];
+      Lg[g] = (red[g] + red[G + g]) + (red[2 * G + g] + red[3 * G + g]);
     }
+    if (!ok) s_flag[1] = 1;
     tc_fence_before();
-    cta_sync();  // (A) with the producer warp
+    cta_sync();  // (A) with the TMA and MMA warps
     if (warp == 0) {
       tc_fence_after();
       tmem_dealloc(tbase, C::TMEM_COLS);
@@ -342,7 +416,8 @@ __global__ void __launch_bounds__(160) qx_decode_tc_kernel(const __grid_constant
     trace.mark();  // outputs (or partials) written
     return;
   }
-  cta_sync();  // (A) for the producer warp
+  tc_fence_before();
+  cta_sync();  // (A) for the TMA and MMA warps
 }
 
 }  // namespace qx

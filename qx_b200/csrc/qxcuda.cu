@@ -233,6 +233,24 @@ int auto_chunk(int slots, const int* attend, int n, int units_per_seq, int max_s
 
 using KernelFn = void (*)(DecodeParams);
 
+// Launch a DecodeParams kernel as a programmatic dependent of the stream's
+// previous kernel: its CTAs may become resident and set up (barriers, TMEM)
+// while that kernel drains, and wait for it in griddepcontrol.wait.
+cudaError_t launch_pdl(qxc_ctx* ctx, KernelFn fn, int grid, int threads, int smem, const DecodeParams& p) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, p);
+}
+
 // Diagnostics: with QXC_TRACE set in the environment, a launch gets a zeroed
 // stage-timeline buffer (kTraceSlots per CTA) and, once it completes, one
 // line per CTA goes to stderr: "<kernel> trace cta N: t0 t1 ..." in absolute
@@ -276,8 +294,7 @@ qxc_status launch_typed(qxc_ctx* ctx, const DecodeParams& p, int items) {
                                        C::SMEM));
     configured |= bit;
   }
-  qx_decode_kernel<M, KT, VT><<<items, C::NT, C::SMEM, ctx->stream>>>(p);
-  QXC_CUDA(ctx, cudaGetLastError());
+  QXC_CUDA(ctx, launch_pdl(ctx, qx_decode_kernel<M, KT, VT>, items, C::NT, C::SMEM, p));
   ctx->launches++;
   return QXC_OK;
 }
@@ -291,8 +308,7 @@ qxc_status launch_tc(qxc_ctx* ctx, const DecodeParams& p, int items) {
     QXC_CUDA(ctx, cudaFuncSetAttribute(qx_decode_tc_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured |= bit;
   }
-  qx_decode_tc_kernel<KT><<<items, C::NT, C::SMEM, ctx->stream>>>(p);
-  QXC_CUDA(ctx, cudaGetLastError());
+  QXC_CUDA(ctx, launch_pdl(ctx, qx_decode_tc_kernel<KT>, items, C::NT, C::SMEM, p));
   ctx->launches++;
   return QXC_OK;
 }
@@ -302,13 +318,14 @@ qxc_status launch_decode_kernel(qxc_ctx* ctx, const qxc_kv* kv, const DecodePara
 // Splits beyond which the merge runs as its own kernel.
 constexpr int kInKernelMergeMaxSplits = 8;
 
+// The merge grid is a programmatic dependent of the decode grid: it may be
+// launched while the decode runs and waits for it in griddepcontrol.wait.
 qxc_status launch_split_merge(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams& p) {
-  const int blocks = p.n_seq * p.layer_count * kv->hq;
+  const int grid = p.n_seq * p.layer_count * kv->hq * (kv->d / 32);
   if (kv->desc.model == QXC_MODEL_QWEN3)
-    qx_split_merge_kernel<8, 128, 4, 32><<<blocks, 256, 0, ctx->stream>>>(p);
+    QXC_CUDA(ctx, launch_pdl(ctx, qx_split_merge_kernel<8, 128, 4, 32>, grid, 128, 0, p));
   else
-    qx_split_merge_kernel<2, 64, 8, 16><<<blocks, 256, 0, ctx->stream>>>(p);
-  QXC_CUDA(ctx, cudaGetLastError());
+    QXC_CUDA(ctx, launch_pdl(ctx, qx_split_merge_kernel<2, 64, 8, 16>, grid, 128, 0, p));
   ctx->launches++;
   return QXC_OK;
 }
@@ -322,7 +339,7 @@ qxc_status launch_decode(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams& p0,
     st = launch_decode_kernel(ctx, kv, p, items);
   }
   if (st != QXC_OK || !p.external_merge) return st;
-  TraceRun tr(ctx, "merge", (size_t)p.n_seq * p.layer_count * kv->hq);
+  TraceRun tr(ctx, "merge", (size_t)p.n_seq * p.layer_count * kv->hq * (kv->d / 32));
   p.trace = tr.buf;
   return launch_split_merge(ctx, kv, p);
 }
@@ -452,6 +469,9 @@ qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer
   int max_split = 1;
   for (const SeqInfo& si : plan.tab) max_split = std::max(max_split, (si.attend + plan.chunk - 1) / plan.chunk);
   p->external_merge = max_split > kInKernelMergeMaxSplits ? 1 : 0;
+  // a one-wave grid lets the next grid (the merge, or the next call) get
+  // resident while it runs
+  p->early_trigger = plan.items <= decode_blocks_per_sm(kv) * ctx->sm_count ? 1 : 0;
   return QXC_OK;
 }
 
