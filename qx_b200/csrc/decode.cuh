@@ -86,7 +86,7 @@ struct DecodeParams {
   int pinned_exp;
   int emit_partials;  // write (O, m, l) per query head instead of O / l
   int external_merge;  // splits only store partials; qx_split_merge_kernel merges them
-  int early_trigger;   // one-wave grid: let the merge grid launch at once (griddepcontrol)
+  int early_trigger;   // one-wave grid: let the next grid launch at once (griddepcontrol)
   float* partials;    // scratch [items][G][D+2]
   int* tickets;       // scratch [n_seq][layer_count][HKV], zero between calls
   unsigned* err;

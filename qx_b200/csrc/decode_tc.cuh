@@ -51,7 +51,7 @@ struct TcCfg {
   static constexpr int OFF_RED = OFF_NEWV + D * 2;         // f32 [4 warps][G], then u32 [2][4] flags
   static constexpr int OFF_STAT = OFF_RED + 4 * G * 4 + 32;  // f32 [2 * G]; inv [G + 1]
   static constexpr int OFF_BAR = ((OFF_STAT + 4 * (3 * G + 1) + 15) / 16) * 16;
-  static constexpr int NBAR = 4 * NS + 2 + 2 + 2 + 3;
+  static constexpr int NBAR = 4 * NS + 2 + 2 + 2 + 4;
   static constexpr int SMEM = OFF_BAR + (NBAR + 2) * 8 + 1024;  // + TMEM slot and flags, + slack to align
   static constexpr int NT = 192;  // consumer warps 0-3, TMA warp 4, MMA warp 5
   static constexpr uint32_t TMEM_COLS = 64;  // S^T buffers [0,16) [16,32); O^T [32,48)
@@ -85,8 +85,9 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
   uint64_t* qready = pdone + 2;     // Q in shared memory
   uint64_t* kpatch = qready + 1;    // the appended key is in its K stage
   uint64_t* mdone = kpatch + 1;     // every MMA completed
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(mdone + 1);
-  int* s_flag = reinterpret_cast<int*>(mdone + 2);
+  uint64_t* loaded = mdone + 1;     // the prologue's global loads landed (the ring may start)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(loaded + 1);
+  int* s_flag = reinterpret_cast<int*>(loaded + 2);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
     mbar_init(qready, 1);
     mbar_init(kpatch, 1);
     mbar_init(mdone, 1);
+    mbar_init(loaded, 4);
     s_flag[1] = 0;
     fence_barrier_init();
   }
@@ -147,6 +149,9 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
       unsigned char* ring = sm + (lane == 0 ? C::OFF_K : C::OFF_V);
       prefetch_tmap(map);
       const int z0 = (int)(unit * p.capacity) + begin;
+      // the prologue's few loads go first: behind the ring's ~200 KB per SM
+      // they would wait for most of it
+      ok &= mbar_wait_bounded(loaded, 0, p.err);
       for (int t = 0; t < ntiles; ++t) {
         const int st = t % NS;
         if (t >= NS) ok &= mbar_wait_bounded(&empty[st], (uint32_t)(t / NS - 1) & 1u, p.err);
@@ -214,15 +219,28 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
     const long long qbase = (cu * HQ + (long long)h * G) * D;
     const long long kvbase = (cu * HKV + h) * D;
     const int pi = tid & 63;  // the rotation pair of every prologue item of this thread
-    for (int i = tid; i < (G + 1) * D; i += 128) {
-      const int g = i / D, e = i - g * D;
-      raw[i] = g < G ? load_any(p.q, qbase + g * D + e, p.q_dtype)
-                     : (has_new ? load_any(p.k, kvbase + e, p.in_dtype) : 0.0f);
+    // all of this thread's prologue inputs in flight at once: dim tid of the
+    // G query rows (and of the new key row), its RoPE pair, norm weights, new v
+    float qv[G], kn = 0.0f, vnew = 0.0f;
+    load_any_n<G>(p.q, qbase + tid, D, p.q_dtype, qv);
+    if (has_new) {
+      load_any_n<1>(p.k, kvbase + tid, 0, p.in_dtype, &kn);
+      load_any_n<1>(p.v, kvbase + tid, 0, p.in_dtype, &vnew);
     }
     const float2 cssn = p.rope_table[(long long)si.rope_pos * 64 + pi];
     const float wq0 = p.q_norm ? p.q_norm[pi] : 1.0f, wq1 = p.q_norm ? p.q_norm[64 + pi] : 1.0f;
     const float wk0 = p.k_norm ? p.k_norm[pi] : 1.0f, wk1 = p.k_norm ? p.k_norm[64 + pi] : 1.0f;
-    const float vnew = has_new ? load_any(p.v, kvbase + tid, p.in_dtype) : 0.0f;
+#pragma unroll
+    for (int g = 0; g < G; ++g) raw[g * D + tid] = qv[g];
+    raw[G * D + tid] = kn;
+    {
+      // every load above has landed once its value is used
+      const float sink = cssn.x + wq0 + wq1 + wk0 + wk1 + vnew;
+      asm volatile("" ::"f"(sink));
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(loaded);
+    trace.mark();  // prologue loads landed
     // zero the padding rows 8..15 of Q and of both P^T buffers (both column blocks)
     for (int i = tid; i < 6 * 128; i += 128) {
       const int blk = i >> 7, j = i & 127;  // blk 0,1: Q blocks; 2..5: P blocks
@@ -238,6 +256,7 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
       st_inv[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 128.0f), 1.0e-6f)));
     }
     consumers_sync(128);
+    trace.mark();  // RMS norms
     bool bad = false;
     for (int idx = tid; idx < (G + 1) * 64; idx += 128) {
       const int g = idx >> 6;

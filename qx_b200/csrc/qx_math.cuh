@@ -168,6 +168,33 @@ __device__ __forceinline__ float load_any(const void* base, long long i, int dty
   if (dtype == 2) return __half2float(reinterpret_cast<const __half*>(base)[i]);
   return reinterpret_cast<const float*>(base)[i];
 }
+// N elements base[i0 + stride * j] (j < N) of a runtime dtype, every load
+// issued before the first is used (a loop of load_any that stores each
+// value to shared memory would wait for each load in turn: the generic
+// source pointer might alias the shared destination).
+template <int N>
+__device__ __forceinline__ void load_any_n(const void* base, long long i0, int stride, int dtype, float* out) {
+  if (dtype == 1) {
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(base) + i0;
+    __nv_bfloat16 r[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) r[j] = b[(long long)stride * j];
+#pragma unroll
+    for (int j = 0; j < N; ++j) out[j] = __bfloat162float(r[j]);
+  } else if (dtype == 2) {
+    const __half* b = reinterpret_cast<const __half*>(base) + i0;
+    __half r[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) r[j] = b[(long long)stride * j];
+#pragma unroll
+    for (int j = 0; j < N; ++j) out[j] = __half2float(r[j]);
+  } else {
+    const float* b = reinterpret_cast<const float*>(base) + i0;
+#pragma unroll
+    for (int j = 0; j < N; ++j) out[j] = b[(long long)stride * j];
+  }
+}
+
 __device__ __forceinline__ void store_any(void* base, long long i, int dtype, float v) {
   if (dtype == 1) reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
   else if (dtype == 2) reinterpret_cast<__half*>(base)[i] = __float2half_rn(v);

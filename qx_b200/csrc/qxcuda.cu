@@ -468,10 +468,11 @@ qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer
   p->tickets = ctx->tickets;
   int max_split = 1;
   for (const SeqInfo& si : plan.tab) max_split = std::max(max_split, (si.attend + plan.chunk - 1) / plan.chunk);
+  const bool one_wave = plan.items <= decode_blocks_per_sm(kv) * ctx->sm_count;
   p->external_merge = max_split > kInKernelMergeMaxSplits ? 1 : 0;
   // a one-wave grid lets the next grid (the merge, or the next call) get
   // resident while it runs
-  p->early_trigger = plan.items <= decode_blocks_per_sm(kv) * ctx->sm_count ? 1 : 0;
+  p->early_trigger = one_wave ? 1 : 0;
   return QXC_OK;
 }
 
