@@ -378,12 +378,15 @@ def base_line(metric, value, unit, world, K, W, total_ms, higher, scaling, dtype
             "gpu_launches": int(launches)}
 
 
-def hbm_roofline(bytes_per_launch, per_ms, kernel):
+def hbm_roofline(bytes_per_launch, per_ms, kernel, workload=None):
+    """`traffic` is the ncu DRAM read+write of one launch of the same
+    workload (profiles/traffic.json), when one was captured."""
     peak, kind = hbm_peak()
     ach = bytes_per_launch / (float(np.mean(per_ms)) / 1e3) / 1e9
+    tr = profile_traffic(workload) if workload else None
     return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": kind,
-            "traffic": None, "kernel": kernel, "algorithmic_bytes_per_launch": bytes_per_launch,
-            "avg_launch_us": float(np.mean(per_ms)) * 1e3}
+            "traffic": (tr["dram_read"] + tr["dram_write"]) if tr else None, "kernel": kernel,
+            "algorithmic_bytes_per_launch": bytes_per_launch, "avg_launch_us": float(np.mean(per_ms)) * 1e3}
 
 
 def run_config0(args, world, rank, local):
@@ -524,7 +527,9 @@ def run_config2(args, world, rank, local):
                       "timing": "20 calls per CUDA graph replay",
                       "flops_per_step": flops}, clk, launches)
     line["roofline"] = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                        "peak_kind": kind, "traffic": None,
+                        "peak_kind": kind,
+                        "traffic": (lambda t: t["dram_read"] + t["dram_write"] if t else None)(
+                            profile_traffic(f"config2_l{L}")),
                         "kernel": "qx_prefill_rope_kernel + qx_prefill_attn_tc_kernel (timed together)",
                         "algorithmic_flops_per_launch": flops, "avg_launch_us": float(np.mean(per)) * 1e3}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -629,7 +634,8 @@ def run_config3(args, world, rank, local):
                      clk, launches)
     line["config"]["split"] = ctx.last_split
     line["roofline"] = hbm_roofline(B if world == 1 else per_rank_bytes, per,
-                                    "qx_decode_kernel<Qwen3,bf16,bf16>" + ("" if world == 1 else " + merge"))
+                                    "qx_decode_tc_kernel<bf16> + qx_split_merge_kernel (timed together)",
+                                    "config3" if world == 1 else None)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import py_oracle as o
