@@ -226,10 +226,11 @@ def run_config1(args, world, rank, local):
     # e2e through the public host-buffer API (qxc_decode_host)
     e2e = None
     if not args.no_e2e:
-        hq = q.cpu().numpy()
-        hk = k.cpu().numpy()
-        hv = v.cpu().numpy()
-        hout = np.zeros((LAYERS, 1024), np.float32)
+        # the step's inputs and output live in pinned host memory
+        hq = q.cpu().pin_memory().numpy()
+        hk = k.cpu().pin_memory().numpy()
+        hv = v.cpu().pin_memory().numpy()
+        hout = torch.zeros(LAYERS, 1024).pin_memory().numpy()
         hpos = [(C.c_int32 * 1)(P + i) for i in range(cycle)]
         hargs = [_lib.DecodeArgs(0, LAYERS, 1, None, hpos[i], hq[i].ctypes.data, hk[i].ctypes.data,
                                  hv[i].ctypes.data, hout.ctypes.data, None, None, None, F32, F32, F32, flags, args.split)
@@ -256,7 +257,7 @@ def run_config1(args, world, rank, local):
         e2e_s = allreduce_max(time.perf_counter() - t0, world, dev)
         e2e = {"value": world * E / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": LAYERS * (1024 + 512 + 512) * 4,
                "d2h_bytes_per_step": LAYERS * 1024 * 4, "steps": E,
-               "api": "qxc_decode_host (host q/k/v in, host out, synchronous)"}
+               "api": "qxc_decode_host (pinned host q/k/v in, pinned host out, synchronous)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -51,8 +51,6 @@ struct qxc_ctx {
   // device staging for host-pointer entry points
   char* stage_dev = nullptr;
   size_t stage_cap = 0;
-  char* stage_host = nullptr;
-  size_t stage_host_cap = 0;
   unsigned long long launches = 0;
   int last_split = 0;
   // Qwen RoPE (cos, sin) for every position 0..kQwenMaxPositions-1, shared
@@ -635,7 +633,6 @@ void qxc_destroy(qxc_ctx* ctx) {
   cudaFree(ctx->qwen_rope);
   cudaFree(ctx->granite_rope);
   cudaFree(ctx->prefill_q);
-  if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
@@ -917,13 +914,6 @@ static qxc_status stage_reserve(qxc_ctx* ctx, size_t bytes) {
     QXC_CUDA(ctx, cudaMalloc(&ctx->stage_dev, bytes));
     ctx->stage_cap = bytes;
   }
-  if (bytes > ctx->stage_host_cap) {
-    if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
-    ctx->stage_host = nullptr;
-    ctx->stage_host_cap = 0;
-    QXC_CUDA(ctx, cudaMallocHost(&ctx->stage_host, bytes));
-    ctx->stage_host_cap = bytes;
-  }
   return QXC_OK;
 }
 
@@ -940,11 +930,12 @@ qxc_status qxc_decode_host(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* a) {
   const size_t total = off_r + al(rb);
   qxc_status st = stage_reserve(ctx, total);
   if (st != QXC_OK) return st;
-  // one pinned staging buffer -> one host-to-device copy for q, k and v
-  memcpy(ctx->stage_host, a->q, qb);
-  memcpy(ctx->stage_host + off_k, a->k, kb);
-  memcpy(ctx->stage_host + off_v, a->v, kb);
-  QXC_CUDA(ctx, cudaMemcpyAsync(ctx->stage_dev, ctx->stage_host, off_o, cudaMemcpyHostToDevice, ctx->stream));
+  // Straight from the caller's buffers: pinned host memory goes by DMA with
+  // no host-side copy; pageable memory is staged by the driver (the copy
+  // still completes in stream order, so the result is the same).
+  QXC_CUDA(ctx, cudaMemcpyAsync(ctx->stage_dev, a->q, qb, cudaMemcpyHostToDevice, ctx->stream));
+  QXC_CUDA(ctx, cudaMemcpyAsync(ctx->stage_dev + off_k, a->k, kb, cudaMemcpyHostToDevice, ctx->stream));
+  QXC_CUDA(ctx, cudaMemcpyAsync(ctx->stage_dev + off_v, a->v, kb, cudaMemcpyHostToDevice, ctx->stream));
   qxc_decode_args d = *a;
   d.q = ctx->stage_dev;
   d.k = ctx->stage_dev + off_k;
@@ -953,13 +944,10 @@ qxc_status qxc_decode_host(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* a) {
   d.q_rot_out = a->q_rot_out ? reinterpret_cast<float*>(ctx->stage_dev + off_r) : nullptr;
   st = qxc_decode(ctx, kv, &d);
   if (st != QXC_OK) return st;
-  QXC_CUDA(ctx, cudaMemcpyAsync(ctx->stage_host + off_o, ctx->stage_dev + off_o, total - off_o,
-                                cudaMemcpyDeviceToHost, ctx->stream));
-  st = qxc_sync(ctx);
-  if (st != QXC_OK) return st;
-  memcpy(a->out, ctx->stage_host + off_o, ob);
-  if (a->q_rot_out) memcpy(a->q_rot_out, ctx->stage_host + off_r, rb);
-  return QXC_OK;
+  QXC_CUDA(ctx, cudaMemcpyAsync(a->out, ctx->stage_dev + off_o, ob, cudaMemcpyDeviceToHost, ctx->stream));
+  if (a->q_rot_out)
+    QXC_CUDA(ctx, cudaMemcpyAsync(a->q_rot_out, ctx->stage_dev + off_r, rb, cudaMemcpyDeviceToHost, ctx->stream));
+  return qxc_sync(ctx);
 }
 
 qxc_status qxc_granite_attention_decode(qxc_ctx* ctx, qxc_kv* kv, const float* q, const float* k, const float* v,
@@ -986,20 +974,15 @@ qxc_status qxc_apply_granite_rope(qxc_ctx* ctx, float* q, float* k, int32_t posi
   if (position < 0) return fail(ctx, QXC_ERR_INVALID_ARG, "negative position");
   qxc_status st = stage_reserve(ctx, 1536 * sizeof(float));
   if (st != QXC_OK) return st;
-  float* h = reinterpret_cast<float*>(ctx->stage_host);
-  memcpy(h, q, 1024 * sizeof(float));
-  memcpy(h + 1024, k, 512 * sizeof(float));
   float* dq = reinterpret_cast<float*>(ctx->stage_dev);
-  QXC_CUDA(ctx, cudaMemcpyAsync(dq, h, 1536 * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+  QXC_CUDA(ctx, cudaMemcpyAsync(dq, q, 1024 * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+  QXC_CUDA(ctx, cudaMemcpyAsync(dq + 1024, k, 512 * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
   qx_granite_rope_kernel<<<6, 128, 0, ctx->stream>>>(dq, dq + 1024, position, ctx->err_dev);
   QXC_CUDA(ctx, cudaGetLastError());
   ctx->launches++;
-  QXC_CUDA(ctx, cudaMemcpyAsync(h, dq, 1536 * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-  st = qxc_sync(ctx);
-  if (st != QXC_OK) return st;
-  memcpy(q, h, 1024 * sizeof(float));
-  memcpy(k, h + 1024, 512 * sizeof(float));
-  return QXC_OK;
+  QXC_CUDA(ctx, cudaMemcpyAsync(q, dq, 1024 * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+  QXC_CUDA(ctx, cudaMemcpyAsync(k, dq + 1024, 512 * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+  return qxc_sync(ctx);
 }
 
 // ---- KV-length split ---------------------------------------------------------
