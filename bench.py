@@ -603,26 +603,30 @@ def run_config3(args, world, rank, local):
         ctx.lse_merge(MODEL_QWEN3, world, allp, merged)
 
     K, W = args.steps, args.warmup
-    R = 1
-    if world == 1:
-        # one step is tens of microseconds of GPU work, comparable to the
-        # host's per-call path: capture R steps in a CUDA graph and replay it
-        R = 50
+    # one step is tens of microseconds of GPU work, comparable to the host's
+    # per-call path: capture R steps in a CUDA graph (the NCCL all-gather of
+    # the N>1 path included) and replay it
+    R = 50 if world == 1 else 20
+    with torch.cuda.stream(stream):
         for i in range(3):
             step(i)
-        stream.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(R):
-                step(i)
-        step = lambda i: graph.replay()  # noqa: E731
-        K, W = max(1, K // R), max(3, W // R)
+    stream.synchronize()
+    barrier(world)
+    graph = torch.cuda.CUDAGraph()
+    n0 = ctx.launch_count
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(R):
+            step(i)
+    per_replay = ctx.launch_count - n0  # our kernels in one replay
+    replay = lambda i: graph.replay()  # noqa: E731
+    K, W = max(1, K // R), max(3, W // R)
     with torch.cuda.stream(stream):
-        total, per, clk, launches = timed_steps(step, K, W, stream, world, dev, local, ctx)
-    if R > 1:
-        per = [x / R for x in per]  # per call
-        launches = K * R
-        K *= R                      # total covers all K * R calls
+        total, per, clk, launches = timed_steps(replay, K, W, stream, world, dev, local, ctx)
+    stream.synchronize()
+    del graph  # a graph holding NCCL work must go before the process group
+    per = [x / R for x in per]  # per call
+    launches = K * per_replay
+    K *= R                          # total covers all K * R calls
     B = 2 * L * 4 * 128 * 2 + 4 * 128 * (2 * 32 + 2 * 4)
     per_rank_bytes = 2 * (e - b) * 4 * 128 * 2
     line = base_line("Qwen3-30B-A3B attention decode tok/s (KV 32768, bf16)", K / (total / 1e3), "tok/s", world, K,
@@ -631,7 +635,7 @@ def run_config3(args, world, rank, local):
                       "l2": f"calls rotate over {NSET} cache copies ({NSET * per_rank_bytes / 2**20:.0f} MB > 126 MB L2)",
                       "parallelism": "single GPU" if world == 1 else
                       f"KV length split x{world}, NCCL all-gather of (m,l,O) partials + LSE merge",
-                      "timing": "50 steps per CUDA graph replay" if world == 1 else "eager launches"},
+                      "timing": f"{R} steps per CUDA graph replay"},
                      clk, launches)
     line["config"]["split"] = ctx.last_split
     line["roofline"] = hbm_roofline(B if world == 1 else per_rank_bytes, per,
