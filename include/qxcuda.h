@@ -166,6 +166,39 @@ qxc_status qxc_granite_attention_decode(qxc_ctx* ctx, qxc_kv* kv, const float* q
  * q[1024], k[512], computed on the device with qx's pinned sin/cos. */
 qxc_status qxc_apply_granite_rope(qxc_ctx* ctx, float* q, float* k, int32_t position);
 
+/* ---- speculative verify (K candidate tokens of one sequence) -------------- */
+/* Replaces the reference's batched verifier attention stage:
+ * GpuRuntimeBuffers encode_rope_kv_batch + encode_attention_batch_with_plan
+ * (qx-runtime-v2 lib.rs:3722-3760; qx-metal lib.rs:8105-8260). Appends the
+ * RoPE'd keys and the values of positions start..start+tokens-1 (start must
+ * equal the sequence's length, start+tokens <= capacity, else
+ * QXC_ERR_POSITION), then token t attends positions [0, start+t]: the same
+ * rows and the same outputs as `tokens` successive qxc_decode calls. The
+ * length advances by `tokens` (unless QXC_DECODE_NO_ADVANCE); take a
+ * qxc_kv_checkpoint before and qxc_kv_commit the accepted prefix after.
+ * Layouts: q/out [tokens][layer_count][Hq*D], k/v [tokens][layer_count][Hkv*D],
+ * device pointers; asynchronous on the context's stream. */
+typedef struct {
+  int32_t seq;
+  int32_t layer_begin;
+  int32_t layer_count;
+  int32_t start;
+  int32_t tokens;
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  const float* q_norm; /* Qwen RMSNorm weights [128] (null: 1.0) */
+  const float* k_norm;
+  int32_t q_dtype;
+  int32_t in_dtype;
+  int32_t out_dtype;
+  int32_t flags;
+  int32_t split; /* 0: automatic */
+} qxc_verify_args;
+
+qxc_status qxc_decode_verify(qxc_ctx* ctx, qxc_kv* kv, const qxc_verify_args* args);
+
 /* ---- causal prefill ------------------------------------------------------ */
 /* Prompt prefill of `length` tokens into an EMPTY (sequence, layer) of a
  * Granite arena (cursor must be 0): RoPE on q and k at positions

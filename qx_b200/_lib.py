@@ -47,6 +47,14 @@ class PartialArgs(C.Structure):
                 ("in_dtype", C.c_int32), ("flags", C.c_int32), ("split", C.c_int32)]
 
 
+class VerifyArgs(C.Structure):
+    """qxc_verify_args (K speculative tokens of one sequence)."""
+    _fields_ = [("seq", C.c_int32), ("layer_begin", C.c_int32), ("layer_count", C.c_int32), ("start", C.c_int32),
+                ("tokens", C.c_int32), ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("out", C.c_void_p),
+                ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("q_dtype", C.c_int32), ("in_dtype", C.c_int32),
+                ("out_dtype", C.c_int32), ("flags", C.c_int32), ("split", C.c_int32)]
+
+
 class StaticDecodeArgs(C.Structure):
     """qxc_static_decode_args (allocation-free Granite decode)."""
     _fields_ = [("key_cache", C.c_void_p), ("value_cache", C.c_void_p), ("capacity", C.c_int32),
@@ -99,6 +107,7 @@ def load() -> C.CDLL:
         "qxc_apply_granite_rope": (C.c_int, [vp, vp, vp, i32]),
         "qxc_prefill": (C.c_int, [vp, vp, C.POINTER(PrefillArgs)]),
         "qxc_decode_partials": (C.c_int, [vp, vp, C.POINTER(PartialArgs)]),
+        "qxc_decode_verify": (C.c_int, [vp, vp, C.POINTER(VerifyArgs)]),
         "qxc_lse_merge": (C.c_int, [vp, i32, i32, vp, vp, i32]),
         "qxc_granite_decode_static_scratch": (C.c_int, [C.POINTER(StaticDecodeArgs), vp, C.c_char_p, C.c_size_t]),
     }

@@ -24,6 +24,7 @@
 #include "../../include/qxcuda.h"
 #include "decode.cuh"
 #include "decode_tc.cuh"
+#include "append.cuh"
 #include "prefill.cuh"
 
 using namespace qx;
@@ -574,6 +575,24 @@ qxc_status ensure_qwen_rope(qxc_ctx* ctx) {
 }  // namespace
 
 // ============================================================================
+// Append kernel of qxc_decode_verify, a programmatic dependent like the decode.
+template <class M, typename KT, typename VT>
+qxc_status launch_append(qxc_ctx* ctx, const AppendParams& a, int grid) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(128);
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QXC_CUDA(ctx, cudaLaunchKernelEx(&cfg, qx_append_rows_kernel<M, KT, VT>, a));
+  ctx->launches++;
+  return QXC_OK;
+}
+
 extern "C" {
 
 int qxc_abi_version(void) { return QXC_ABI_VERSION; }
@@ -902,6 +921,89 @@ qxc_status qxc_decode(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* a) {
   if (st != QXC_OK) return st;
   if (!(a->flags & QXC_DECODE_NO_ADVANCE))
     for (int i = 0; i < a->seq_count; ++i) kv->len[a->seq_ids ? a->seq_ids[i] : i] += 1;
+  return QXC_OK;
+}
+
+// ---- speculative verify ----------------------------------------------------
+qxc_status qxc_decode_verify(qxc_ctx* ctx, qxc_kv* kv, const qxc_verify_args* a) {
+  if (!ctx || !kv || !a) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (kv->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "KV arena belongs to another context");
+  qxc_status st = check_seq(ctx, kv, a->seq);
+  if (st != QXC_OK) return st;
+  if (a->tokens < 1) return fail(ctx, QXC_ERR_INVALID_ARG, "batched attention requires at least one token");
+  if (a->layer_count < 1 || a->layer_begin < 0 || a->layer_begin + a->layer_count > kv->desc.layers)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "layers [%d, %d) outside the arena's %d layers", a->layer_begin,
+                a->layer_begin + a->layer_count, kv->desc.layers);
+  if (!a->q || !a->k || !a->v || !a->out) return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
+  if (!valid_dtype(a->q_dtype) || !valid_dtype(a->in_dtype) || !valid_dtype(a->out_dtype))
+    return fail(ctx, QXC_ERR_INVALID_ARG, "unknown tensor dtype");
+  if (kv->desc.model == QXC_MODEL_QWEN3 && (a->q_dtype != kv->desc.key_dtype || a->in_dtype != kv->desc.key_dtype))
+    return fail(ctx, QXC_ERR_INVALID_ARG, "Qwen q/k/v must use the KV cache's 16-bit type");
+  if (kv->desc.first_position != 0)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "a KV-length shard decodes through qxc_decode_partials");
+  // KvCache::append for every candidate (qx-runtime lib.rs:385-398)
+  if (a->start != kv->len[a->seq])
+    return fail(ctx, QXC_ERR_POSITION, "KV position %d does not follow cache length %d", a->start, kv->len[a->seq]);
+  if (a->start + a->tokens > kv->desc.capacity)
+    return fail(ctx, QXC_ERR_POSITION, "KV position %d exceeds context %d", a->start + a->tokens - 1,
+                kv->desc.capacity);
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  // 1. the candidates' rows
+  AppendParams ap;
+  memset(&ap, 0, sizeof(ap));
+  ap.k_region = kv->k_region;
+  ap.v_region = kv->v_region;
+  ap.k_unit_bytes = (long long)kv->k_unit;
+  ap.v_unit_bytes = (long long)kv->v_unit;
+  ap.layers = kv->desc.layers;
+  ap.layer_begin = a->layer_begin;
+  ap.layer_count = a->layer_count;
+  ap.seq = a->seq;
+  ap.start = a->start;
+  ap.tokens = a->tokens;
+  ap.k = a->k;
+  ap.v = a->v;
+  ap.k_norm = a->k_norm;
+  ap.rope_table = kv->rope_table;
+  ap.in_dtype = a->in_dtype;
+  ap.err = ctx->err_dev;
+  const int grid = a->tokens * a->layer_count;
+  const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
+  if (kv->desc.model == QXC_MODEL_QWEN3)
+    st = kd == QXC_BF16 ? launch_append<Qwen3, __nv_bfloat16, __nv_bfloat16>(ctx, ap, grid)
+                        : launch_append<Qwen3, __half, __half>(ctx, ap, grid);
+  else if (kd == QXC_F32 && vd == QXC_F32) st = launch_append<Granite, float, float>(ctx, ap, grid);
+  else if (kd == QXC_F32 && vd == QXC_F16) st = launch_append<Granite, float, __half>(ctx, ap, grid);
+  else if (kd == QXC_F16 && vd == QXC_F32) st = launch_append<Granite, __half, float>(ctx, ap, grid);
+  else if (kd == QXC_F16 && vd == QXC_F16) st = launch_append<Granite, __half, __half>(ctx, ap, grid);
+  else st = launch_append<Granite, __nv_bfloat16, __nv_bfloat16>(ctx, ap, grid);
+  if (st != QXC_OK) return st;
+  // 2. token t attends [0, start + t]: one decode launch, one causal entry per token
+  std::vector<int> ids(a->tokens, a->seq), attend(a->tokens), none(a->tokens, -1), rope(a->tokens);
+  for (int t = 0; t < a->tokens; ++t) {
+    attend[t] = a->start + t + 1;
+    rope[t] = a->start + t;
+  }
+  CallPlan plan;
+  st = plan_call(ctx, kv, a->tokens, ids.data(), attend.data(), none.data(), rope.data(), a->layer_count, a->split,
+                 &plan);
+  if (st != QXC_OK) return st;
+  DecodeParams p;
+  st = fill_params(ctx, kv, plan, a->layer_begin, a->layer_count, &p);
+  if (st != QXC_OK) return st;
+  p.q = a->q;
+  p.k = a->k;
+  p.v = a->v;
+  p.out = a->out;
+  p.q_norm = a->q_norm;
+  p.k_norm = a->k_norm;
+  p.q_dtype = a->q_dtype;
+  p.in_dtype = a->in_dtype;
+  p.out_dtype = a->out_dtype;
+  p.pinned_exp = default_pinned(kv, a->flags) ? 1 : 0;
+  st = launch_decode(ctx, kv, p, plan.items);
+  if (st != QXC_OK) return st;
+  if (!(a->flags & QXC_DECODE_NO_ADVANCE)) kv->len[a->seq] += a->tokens;
   return QXC_OK;
 }
 

@@ -251,6 +251,20 @@ class KvArena:
                               out_dtype, flags, split, q_rot_out, q_norm, k_norm)
         self.ctx.check(self.lib.qxc_decode(self.ctx.handle, self.handle, C.byref(a)))
 
+    def decode_verify(self, q, k, v, out, start: int, tokens: int, seq: int = 0, layer_begin: int = 0,
+                      layer_count: int | None = None, q_dtype: int | None = None, in_dtype: int | None = None,
+                      out_dtype: int = F32, flags: int = 0, split: int = 0, q_norm=None, k_norm=None) -> None:
+        """K speculative tokens of one sequence in one call (qxc_decode_verify):
+        rows start..start+tokens-1 appended, token t attending [0, start + t].
+        q/out [tokens][layer_count][Hq*D], k/v [tokens][layer_count][Hkv*D] on
+        the device; the reference's batched verifier attention stage."""
+        layer_count = self.layers - layer_begin if layer_count is None else layer_count
+        dflt = self.key_dtype if self.model == MODEL_QWEN3 else F32
+        a = _lib.VerifyArgs(seq, layer_begin, layer_count, start, tokens, _ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                            _ptr(q_norm), _ptr(k_norm), dflt if q_dtype is None else q_dtype,
+                            dflt if in_dtype is None else in_dtype, out_dtype, flags, split)
+        self.ctx.check(self.lib.qxc_decode_verify(self.ctx.handle, self.handle, C.byref(a)))
+
     def decode_host(self, q: np.ndarray, k: np.ndarray, v: np.ndarray, positions, layer_begin: int = 0,
                     layer_count: int | None = None, seq_ids=None, q_dtype: int | None = None,
                     in_dtype: int | None = None, out_dtype: int = F32, flags: int = 0, split: int = 0,
