@@ -199,6 +199,48 @@ typedef struct {
 
 qxc_status qxc_decode_verify(qxc_ctx* ctx, qxc_kv* kv, const qxc_verify_args* args);
 
+/* ---- Q4 projections around attention (Granite layer) --------------------- */
+/* A Q4 matrix in the reference's row-major layout with group 32
+ * (qx-quant QuantizedTensor, layout RowMajor): per row and group, an FP16
+ * scale and 16 bytes of codes, low nibble first; value = (code - 7) * scale. */
+typedef struct {
+  int32_t rows;
+  int32_t cols;            /* a multiple of 32, at most 4096 */
+  const uint8_t* codes;    /* device [rows][cols/32][16] */
+  const uint16_t* scales;  /* device [rows][cols/32] FP16 bit patterns */
+} qxc_q4_matrix;
+
+/* y = W x (QuantizedTensor::mat_vec_simd32, qx-quant lib.rs:892-933), or
+ * with rms_weight != NULL y = W (cpu_rms_norm_simd(x, rms_weight),
+ * qx-runtime-v2 lib.rs:4924-4946; then cols must be 1024). Bit-identical
+ * to the reference's CPU routines. Device pointers, asynchronous. */
+qxc_status qxc_q4_mat_vec(qxc_ctx* ctx, const qxc_q4_matrix* w, const float* x, const float* rms_weight,
+                          float* y);
+
+/* The attention sub-layer of a Granite layer with Q4 weights, for one token
+ * (GpuRuntimeBuffers::encode_attention_layer, qx-runtime-v2 lib.rs:6916-6994;
+ * CPU twin CpuQ4Reference::step :4680-4706): RMSNorm(hidden_in, input_norm)
+ * -> Q4 q/k/v projections -> RoPE, KV append at `position` and GQA attention
+ * (qxc_decode) -> Q4 o-projection -> hidden_out = fma(0.22, o, hidden_in).
+ * Same position rules as qxc_decode. Device pointers, asynchronous. */
+typedef struct {
+  int32_t seq;
+  int32_t layer;
+  int32_t position;
+  const float* hidden_in;   /* [1024] */
+  float* hidden_out;        /* [1024] */
+  const float* input_norm;  /* [1024] */
+  qxc_q4_matrix q_proj;     /* 1024 x 1024 */
+  qxc_q4_matrix k_proj;     /* 512 x 1024 */
+  qxc_q4_matrix v_proj;     /* 512 x 1024 */
+  qxc_q4_matrix o_proj;     /* 1024 x 1024 */
+  float* attention_out;     /* optional [1024]: attention before the o-projection */
+  int32_t flags;
+  int32_t split;
+} qxc_layer_args;
+
+qxc_status qxc_attention_layer(qxc_ctx* ctx, qxc_kv* kv, const qxc_layer_args* args);
+
 /* ---- causal prefill ------------------------------------------------------ */
 /* Prompt prefill of `length` tokens into an EMPTY (sequence, layer) of a
  * Granite arena (cursor must be 0): RoPE on q and k at positions

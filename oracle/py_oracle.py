@@ -62,6 +62,12 @@ def lib():
         _lib.qxo_qwen_gqa_attention.argtypes = [u16p, u16p, u16p, C.c_int, C.c_int, fp, u16p, C.c_int]
         _lib.qxo_f32_to_bf16.argtypes = [C.c_float]
         _lib.qxo_f32_to_bf16.restype = C.c_uint16
+        u8p = C.POINTER(C.c_uint8)
+        _lib.qxo_rms_norm_simd.argtypes = [fp, fp, fp]
+        _lib.qxo_q4_quantize.argtypes = [fp, C.c_int, C.c_int, u8p, u16p]
+        _lib.qxo_q4_mat_vec_simd32.argtypes = [u8p, u16p, C.c_int, C.c_int, fp, fp]
+        _lib.qxo_granite_attention_layer.argtypes = [fp, fp, u8p, u16p, u8p, u16p, u8p, u16p, u8p, u16p, C.c_int,
+                                                     fp, fp, ip, C.c_int, fp, fp]
     return _lib
 
 
@@ -203,3 +209,49 @@ def qwen_decode(q_bits, k_bits, v_bits, q_norm, k_norm, key_cache, value_cache, 
     out, bits = qwen_gqa_attention(qr, key_cache[: position + 1], value_cache[: position + 1], position + 1, dtype,
                                    threads)
     return qr, kr, out, bits
+
+
+# ---- attention sub-layer with Q4 projections (qx-runtime-v2 CpuQ4Reference::step) ----
+def _u8(a):
+    return a.ctypes.data_as(C.POINTER(C.c_uint8))
+
+
+def rms_norm_simd(x, weight):
+    """cpu_rms_norm_simd over HIDDEN = 1024 -> (status 1 ok, normalized)."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(weight, np.float32)
+    out = np.zeros(1024, np.float32)
+    st = lib().qxo_rms_norm_simd(_fp(x), _fp(w), _fp(out))
+    return st, out
+
+
+class Q4Matrix:
+    """Q4, group 32, row-major: codes [rows][cols/32][16] u8, scales
+    [rows][cols/32] FP16 bits (QuantizedTensor::quantize)."""
+
+    def __init__(self, weights: np.ndarray):
+        w = np.ascontiguousarray(weights, np.float32)
+        self.rows, self.cols = w.shape
+        self.codes = np.zeros((self.rows, self.cols // 32, 16), np.uint8)
+        self.scales = np.zeros((self.rows, self.cols // 32), np.uint16)
+        lib().qxo_q4_quantize(_fp(w), self.rows, self.cols, _u8(self.codes), _u16(self.scales))
+
+    def mat_vec(self, x) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros(self.rows, np.float32)
+        lib().qxo_q4_mat_vec_simd32(_u8(self.codes), _u16(self.scales), self.rows, self.cols, _fp(x), _fp(out))
+        return out
+
+
+def granite_attention_layer(hidden, input_norm, qp: Q4Matrix, kp: Q4Matrix, vp: Q4Matrix, op: Q4Matrix,
+                            position: int, cache: KvCache):
+    """(status 0 ok, hidden out [1024], attention [1024]) for one layer at `position`."""
+    h = np.ascontiguousarray(hidden, np.float32)
+    w = np.ascontiguousarray(input_norm, np.float32)
+    out = np.zeros(1024, np.float32)
+    att = np.zeros(1024, np.float32)
+    st = lib().qxo_granite_attention_layer(_fp(h), _fp(w), _u8(qp.codes), _u16(qp.scales), _u8(kp.codes),
+                                           _u16(kp.scales), _u8(vp.codes), _u16(vp.scales), _u8(op.codes),
+                                           _u16(op.scales), position, _fp(cache.keys), _fp(cache.values),
+                                           C.byref(cache.length), cache.max_context, _fp(out), _fp(att))
+    return st, out, att

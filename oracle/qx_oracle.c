@@ -639,3 +639,94 @@ void qxo_qwen_gqa_attention(const uint16_t* query, const uint16_t* key_cache,
   qwen_ctx c = {query, key_cache, value_cache, context, dtype, out_f32, out_bits};
   qxo_parallel_for(Q_HEADS, threads, qwen_head_body, &c);
 }
+
+/* ===================================================================== */
+/* Attention sub-layer with Q4 projections                               */
+/* (qx-runtime-v2 CpuQ4Reference::step, lib.rs:4680-4706)                */
+/* ===================================================================== */
+
+/* cpu_rms_norm_simd, qx-runtime-v2 lib.rs:4924-4946. */
+int qxo_rms_norm_simd(const float* input, const float* weight, float* out) {
+  float threads[256];
+  for (int tid = 0; tid < 256; ++tid) {
+    float sum = 0.0f;
+    for (int index = tid; index < G_HIDDEN; index += 256) sum = fmaf(input[index], input[index], sum);
+    threads[tid] = sum;
+  }
+  float groups[32] = {0};
+  for (int group = 0; group < 8; ++group) groups[group] = qxo_reduce_simd32(threads + group * 32);
+  const float mean_square = qxo_reduce_simd32(groups) / (float)G_HIDDEN;
+  float scale;
+  if (!qxo_rsqrt_f32(mean_square + 1e-6f, &scale)) return 0; /* RMS_EPSILON, qx-model lib.rs:24 */
+  for (int i = 0; i < G_HIDDEN; ++i) out[i] = input[i] * scale * weight[i];
+  return 1;
+}
+
+/* QuantizedTensor::quantize (qx-quant lib.rs:313-360) for Q4, group 32:
+ * scale = max|x| / 7 rounded to FP16 (1.0 for an all-zero group), code =
+ * clamp(round(x / scale), -7, 7) + 7 packed low nibble first (pack_scaled,
+ * :1383-1404). */
+void qxo_q4_quantize(const float* src, int rows, int cols, uint8_t* codes, uint16_t* scales) {
+  const int groups = cols / 32;
+  for (int r = 0; r < rows; ++r)
+    for (int g = 0; g < groups; ++g) {
+      const float* x = src + (size_t)r * cols + g * 32;
+      float max_abs = 0.0f;
+      for (int i = 0; i < 32; ++i) max_abs = fmaxf(max_abs, fabsf(x[i]));
+      const float scale = max_abs == 0.0f ? 1.0f : max_abs / 7.0f;
+      const uint16_t bits = qxo_f32_to_f16(scale);
+      const float stored = qxo_f16_to_f32(bits);
+      scales[(size_t)r * groups + g] = bits;
+      uint8_t* dst = codes + ((size_t)r * groups + g) * 16;
+      memset(dst, 0, 16);
+      for (int i = 0; i < 32; ++i) {
+        float q = roundf(x[i] / stored); /* Rust round: half away from zero */
+        q = q < -7.0f ? -7.0f : (q > 7.0f ? 7.0f : q);
+        const uint8_t code = (uint8_t)((int)q + 7);
+        dst[i / 2] |= (uint8_t)((code & 0xF) << ((i & 1) * 4));
+      }
+    }
+}
+
+/* QuantizedTensor::mat_vec_simd32 (qx-quant lib.rs:892-933) with
+ * decode_scaled (:1472-1485): value = (code - 7) * scale. */
+void qxo_q4_mat_vec_simd32(const uint8_t* codes, const uint16_t* scales, int rows, int cols,
+                           const float* input, float* out) {
+  const int groups = cols / 32;
+  for (int r = 0; r < rows; ++r) {
+    float lanes[32] = {0};
+    for (int g = 0; g < groups; ++g) {
+      const float scale = qxo_f16_to_f32(scales[(size_t)r * groups + g]);
+      const uint8_t* packed = codes + ((size_t)r * groups + g) * 16;
+      for (int i = 0; i < 32; ++i) {
+        const int column = g * 32 + i;
+        const uint8_t code = (packed[i / 2] >> ((i & 1) * 4)) & 0xF;
+        const float value = (float)((int)code - 7) * scale;
+        lanes[column % 32] = fmaf(value, input[column], lanes[column % 32]);
+      }
+    }
+    out[r] = qxo_reduce_simd32(lanes);
+  }
+}
+
+int qxo_granite_attention_layer(const float* hidden, const float* input_norm,
+                                const uint8_t* q_codes, const uint16_t* q_scales,
+                                const uint8_t* k_codes, const uint16_t* k_scales,
+                                const uint8_t* v_codes, const uint16_t* v_scales,
+                                const uint8_t* o_codes, const uint16_t* o_scales,
+                                int position, float* keys, float* values, int* length,
+                                int capacity, float* out, float* attention_out) {
+  float normalized[G_HIDDEN], q[G_HIDDEN], k[G_KV_HEADS * G_HEAD_DIM], v[G_KV_HEADS * G_HEAD_DIM];
+  float attention[G_HIDDEN], projection[G_HIDDEN];
+  if (!qxo_rms_norm_simd(hidden, input_norm, normalized)) return QXO_ERR_NONFINITE;
+  qxo_q4_mat_vec_simd32(q_codes, q_scales, G_HIDDEN, G_HIDDEN, normalized, q);
+  qxo_q4_mat_vec_simd32(k_codes, k_scales, G_KV_HEADS * G_HEAD_DIM, G_HIDDEN, normalized, k);
+  qxo_q4_mat_vec_simd32(v_codes, v_scales, G_KV_HEADS * G_HEAD_DIM, G_HIDDEN, normalized, v);
+  const int st = qxo_granite_attention_decode(q, k, v, position, keys, values, QXO_F32, QXO_F32, length,
+                                              capacity, 0, attention);
+  if (st != QXO_OK) return st;
+  if (attention_out) memcpy(attention_out, attention, sizeof(attention));
+  qxo_q4_mat_vec_simd32(o_codes, o_scales, G_HIDDEN, G_HIDDEN, attention, projection);
+  for (int i = 0; i < G_HIDDEN; ++i) out[i] = fmaf(0.22f, projection[i], hidden[i]); /* RESIDUAL_MULTIPLIER */
+  return QXO_OK;
+}

@@ -113,6 +113,35 @@ void qxo_qwen_gqa_attention(const uint16_t* query, const uint16_t* key_cache,
                             int dtype, float* out_f32, uint16_t* out_bits,
                             int threads);
 
+/* ---- the attention half of a Granite layer with Q4 projections
+ *      (qx-runtime-v2 CpuQ4Reference::step, lib.rs:4680-4706) ---- */
+/* cpu_rms_norm_simd (qx-runtime-v2 lib.rs:4924-4946): HIDDEN = 1024,
+ * 256 fma partials, two reduce_simd32 levels, consensus rsqrt, then
+ * (x * scale) * weight. Returns 0 when the RMS is not positive finite. */
+int qxo_rms_norm_simd(const float* input, const float* weight, float* out);
+/* QuantizedTensor::quantize for Q4, group 32, row-major layout
+ * (qx-quant lib.rs:313-360 and pack_scaled :1383-1404): scales[row][group]
+ * as FP16 bits, codes[row][group][16 bytes], low nibble first. */
+void qxo_q4_quantize(const float* src, int rows, int cols, uint8_t* codes, uint16_t* scales);
+/* QuantizedTensor::mat_vec_simd32 for that layout (qx-quant lib.rs:892-933,
+ * decode_scaled :1472-1485): column c accumulates into lane c % 32 by fma,
+ * then the (16, 8, 4, 2, 1) lane tree. */
+void qxo_q4_mat_vec_simd32(const uint8_t* codes, const uint16_t* scales, int rows, int cols,
+                           const float* input, float* out);
+/* One attention sub-layer: normalized = rms_norm(hidden, input_norm);
+ * q/k/v = Q4 mat-vecs; attention = granite_attention_decode at `position`
+ * on `cache`; out[i] = fma(RESIDUAL_MULTIPLIER = 0.22, o_proj(attention)[i],
+ * hidden[i]). Weights as qxo_q4_quantize writes them; attention_out
+ * (optional, [1024]) receives the attention output. Returns QXO_OK or
+ * the decode's error status. */
+int qxo_granite_attention_layer(const float* hidden, const float* input_norm,
+                                const uint8_t* q_codes, const uint16_t* q_scales,
+                                const uint8_t* k_codes, const uint16_t* k_scales,
+                                const uint8_t* v_codes, const uint16_t* v_scales,
+                                const uint8_t* o_codes, const uint16_t* o_scales,
+                                int position, float* keys, float* values, int* length,
+                                int capacity, float* out, float* attention_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,19 @@ class VerifyArgs(C.Structure):
                 ("out_dtype", C.c_int32), ("flags", C.c_int32), ("split", C.c_int32)]
 
 
+class Q4Matrix(C.Structure):
+    """qxc_q4_matrix: row-major Q4, group 32 (device codes and FP16 scales)."""
+    _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("codes", C.c_void_p), ("scales", C.c_void_p)]
+
+
+class LayerArgs(C.Structure):
+    """qxc_layer_args (the attention sub-layer of a Granite layer with Q4 weights)."""
+    _fields_ = [("seq", C.c_int32), ("layer", C.c_int32), ("position", C.c_int32), ("hidden_in", C.c_void_p),
+                ("hidden_out", C.c_void_p), ("input_norm", C.c_void_p), ("q_proj", Q4Matrix), ("k_proj", Q4Matrix),
+                ("v_proj", Q4Matrix), ("o_proj", Q4Matrix), ("attention_out", C.c_void_p), ("flags", C.c_int32),
+                ("split", C.c_int32)]
+
+
 class StaticDecodeArgs(C.Structure):
     """qxc_static_decode_args (allocation-free Granite decode)."""
     _fields_ = [("key_cache", C.c_void_p), ("value_cache", C.c_void_p), ("capacity", C.c_int32),
@@ -108,6 +121,8 @@ def load() -> C.CDLL:
         "qxc_prefill": (C.c_int, [vp, vp, C.POINTER(PrefillArgs)]),
         "qxc_decode_partials": (C.c_int, [vp, vp, C.POINTER(PartialArgs)]),
         "qxc_decode_verify": (C.c_int, [vp, vp, C.POINTER(VerifyArgs)]),
+        "qxc_q4_mat_vec": (C.c_int, [vp, C.POINTER(Q4Matrix), vp, vp, vp]),
+        "qxc_attention_layer": (C.c_int, [vp, vp, C.POINTER(LayerArgs)]),
         "qxc_lse_merge": (C.c_int, [vp, i32, i32, vp, vp, i32]),
         "qxc_granite_decode_static_scratch": (C.c_int, [C.POINTER(StaticDecodeArgs), vp, C.c_char_p, C.c_size_t]),
     }

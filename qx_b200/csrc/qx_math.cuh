@@ -130,6 +130,22 @@ __device__ __forceinline__ bool pinned_sin_cos(float angle, float* s, float* c) 
   return true;
 }
 
+// rsqrt_f32 (qx-consensus-math lib.rs:114-128): integer seed and four fixed
+// Newton steps; false for a non-positive or non-finite input or result.
+__device__ __forceinline__ bool pinned_rsqrt(float x, float* out) {
+  if (!isfinite(x) || x <= 0.0f) return false;
+  const float half = __fmul_rn(x, 0.5f);
+  float e = __uint_as_float(0x5f375a86u - (__float_as_uint(x) >> 1));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float square = __fmul_rn(e, e);
+    const float correction = __fmaf_rn(-half, square, 1.5f);
+    e = __fmul_rn(e, correction);
+  }
+  *out = e;
+  return isfinite(e);
+}
+
 // granite_rope_sin_cos (lib.rs:192-195).
 __device__ __forceinline__ bool granite_sin_cos(uint32_t position, int pair, float* s, float* c) {
   float angle = __fmul_rn(__uint2float_rn(position), fbits(kGraniteInvFreqBits[pair]));

@@ -25,6 +25,7 @@
 #include "decode.cuh"
 #include "decode_tc.cuh"
 #include "append.cuh"
+#include "layer.cuh"
 #include "prefill.cuh"
 
 using namespace qx;
@@ -58,6 +59,7 @@ struct qxc_ctx {
   // by all Qwen arenas of this context (created with the first one).
   float2* qwen_rope = nullptr;
   float2* granite_rope = nullptr;  // pinned (sin, cos) [4096][32], built on first prefill
+  float* layer_scratch = nullptr;   // attention layer: q[1024] k[512] v[512] attention[1024]
   // prefill's rotated-query scratch (bf16 elements)
   unsigned short* prefill_q = nullptr;
   size_t prefill_q_cap = 0;
@@ -575,6 +577,44 @@ qxc_status ensure_qwen_rope(qxc_ctx* ctx) {
 }  // namespace
 
 // ============================================================================
+// Q4 mat-vec kernel, a programmatic dependent like the decode.
+qxc_status launch_matvec(qxc_ctx* ctx, const LayerParams& p) {
+  int rows = 0;
+  for (int m = 0; m < p.nmat; ++m) rows += p.w[m].rows;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(std::min(1024, (rows + 7) / 8));
+  cfg.blockDim = dim3(256);
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QXC_CUDA(ctx, cudaLaunchKernelEx(&cfg, qx_q4_matvec_kernel, p));
+  ctx->launches++;
+  return QXC_OK;
+}
+
+qxc_status check_q4(qxc_ctx* ctx, const qxc_q4_matrix* w, int rows, int cols, const char* name) {
+  if (!w->codes || !w->scales) return fail(ctx, QXC_ERR_INVALID_ARG, "%s: null Q4 data", name);
+  if ((rows && w->rows != rows) || (cols && w->cols != cols))
+    return fail(ctx, QXC_ERR_INVALID_ARG, "%s must be %d x %d, got %d x %d", name, rows, cols, w->rows, w->cols);
+  if (w->rows < 1 || w->cols < 32 || w->cols % 32 != 0 || w->cols > 4 * kHidden)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "%s: %d x %d is not a Q4 shape (cols a multiple of 32, at most %d)", name,
+                w->rows, w->cols, 4 * kHidden);
+  return QXC_OK;
+}
+
+Q4Ref q4ref(const qxc_q4_matrix& w) {
+  Q4Ref r;
+  r.codes = w.codes;
+  r.scales = w.scales;
+  r.rows = w.rows;
+  r.cols = w.cols;
+  return r;
+}
+
 // Append kernel of qxc_decode_verify, a programmatic dependent like the decode.
 template <class M, typename KT, typename VT>
 qxc_status launch_append(qxc_ctx* ctx, const AppendParams& a, int grid) {
@@ -651,6 +691,7 @@ void qxc_destroy(qxc_ctx* ctx) {
   cudaFree(ctx->stage_dev);
   cudaFree(ctx->qwen_rope);
   cudaFree(ctx->granite_rope);
+  cudaFree(ctx->layer_scratch);
   cudaFree(ctx->prefill_q);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -922,6 +963,95 @@ qxc_status qxc_decode(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* a) {
   if (!(a->flags & QXC_DECODE_NO_ADVANCE))
     for (int i = 0; i < a->seq_count; ++i) kv->len[a->seq_ids ? a->seq_ids[i] : i] += 1;
   return QXC_OK;
+}
+
+// ---- Q4 projections around attention ------------------------------------------
+qxc_status qxc_q4_mat_vec(qxc_ctx* ctx, const qxc_q4_matrix* w, const float* x, const float* rms_weight,
+                          float* y) {
+  if (!ctx || !w || !x || !y) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  qxc_status st = check_q4(ctx, w, 0, rms_weight ? kHidden : 0, "matrix");
+  if (st != QXC_OK) return st;
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  LayerParams p;
+  memset(&p, 0, sizeof(p));
+  p.hidden = x;
+  p.norm = rms_weight;
+  p.normalize = rms_weight ? 1 : 0;
+  p.w[0] = q4ref(*w);
+  p.y[0] = y;
+  p.nmat = 1;
+  p.err = ctx->err_dev;
+  return launch_matvec(ctx, p);
+}
+
+qxc_status qxc_attention_layer(qxc_ctx* ctx, qxc_kv* kv, const qxc_layer_args* a) {
+  if (!ctx || !kv || !a) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (kv->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "KV arena belongs to another context");
+  if (kv->desc.model != QXC_MODEL_GRANITE) return fail(ctx, QXC_ERR_UNSUPPORTED, "the Q4 layer is Granite's");
+  if (!a->hidden_in || !a->hidden_out || !a->input_norm) return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
+  qxc_status st = check_q4(ctx, &a->q_proj, kHidden, kHidden, "q_proj");
+  if (st == QXC_OK) st = check_q4(ctx, &a->k_proj, 512, kHidden, "k_proj");
+  if (st == QXC_OK) st = check_q4(ctx, &a->v_proj, 512, kHidden, "v_proj");
+  if (st == QXC_OK) st = check_q4(ctx, &a->o_proj, kHidden, kHidden, "o_proj");
+  if (st == QXC_OK) st = check_seq(ctx, kv, a->seq);
+  if (st != QXC_OK) return st;
+  if (a->layer < 0 || a->layer >= kv->desc.layers) return fail(ctx, QXC_ERR_INVALID_ARG, "layer %d out of range", a->layer);
+  // KvCache::append (qx-runtime lib.rs:385-398), checked before any launch
+  if (a->position != kv->len[a->seq])
+    return fail(ctx, QXC_ERR_POSITION, "KV position %d does not follow cache length %d", a->position,
+                kv->len[a->seq]);
+  if (a->position >= kv->desc.capacity)
+    return fail(ctx, QXC_ERR_POSITION, "KV position %d exceeds context %d", a->position, kv->desc.capacity);
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  if (!ctx->layer_scratch) QXC_CUDA(ctx, cudaMalloc(&ctx->layer_scratch, 3072 * sizeof(float)));
+  float* q = ctx->layer_scratch;
+  float* k = q + 1024;
+  float* v = k + 512;
+  float* att = a->attention_out ? a->attention_out : v + 512;
+  // 1. RMSNorm + q/k/v projections
+  LayerParams p;
+  memset(&p, 0, sizeof(p));
+  p.hidden = a->hidden_in;
+  p.norm = a->input_norm;
+  p.normalize = 1;
+  p.w[0] = q4ref(a->q_proj);
+  p.w[1] = q4ref(a->k_proj);
+  p.w[2] = q4ref(a->v_proj);
+  p.y[0] = q;
+  p.y[1] = k;
+  p.y[2] = v;
+  p.nmat = 3;
+  p.err = ctx->err_dev;
+  st = launch_matvec(ctx, p);
+  if (st != QXC_OK) return st;
+  // 2. RoPE, append, attention
+  qxc_decode_args d;
+  memset(&d, 0, sizeof(d));
+  const int32_t seq = a->seq, pos = a->position;
+  d.layer_begin = a->layer;
+  d.layer_count = 1;
+  d.seq_count = 1;
+  d.seq_ids = &seq;
+  d.positions = &pos;
+  d.q = q;
+  d.k = k;
+  d.v = v;
+  d.out = att;
+  d.q_dtype = d.in_dtype = d.out_dtype = QXC_F32;
+  d.flags = a->flags;
+  d.split = a->split;
+  st = qxc_decode(ctx, kv, &d);
+  if (st != QXC_OK) return st;
+  // 3. o-projection and residual
+  LayerParams o;
+  memset(&o, 0, sizeof(o));
+  o.hidden = att;
+  o.w[0] = q4ref(a->o_proj);
+  o.y[0] = a->hidden_out;
+  o.nmat = 1;
+  o.residual = a->hidden_in;
+  o.err = ctx->err_dev;
+  return launch_matvec(ctx, o);
 }
 
 // ---- speculative verify ----------------------------------------------------

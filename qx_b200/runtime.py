@@ -265,6 +265,16 @@ class KvArena:
                             dflt if in_dtype is None else in_dtype, out_dtype, flags, split)
         self.ctx.check(self.lib.qxc_decode_verify(self.ctx.handle, self.handle, C.byref(a)))
 
+    def attention_layer(self, hidden_in, hidden_out, input_norm, q_proj: "Q4Weights", k_proj: "Q4Weights",
+                        v_proj: "Q4Weights", o_proj: "Q4Weights", position: int, seq: int = 0, layer: int = 0,
+                        attention_out=None, flags: int = 0, split: int = 0) -> None:
+        """The attention sub-layer of a Granite layer with Q4 weights for one
+        token (qxc_attention_layer): RMSNorm, Q4 q/k/v, RoPE + append +
+        attention, Q4 o-projection, residual; device tensors."""
+        a = _lib.LayerArgs(seq, layer, position, _ptr(hidden_in), _ptr(hidden_out), _ptr(input_norm),
+                           q_proj.ref(), k_proj.ref(), v_proj.ref(), o_proj.ref(), _ptr(attention_out), flags, split)
+        self.ctx.check(self.lib.qxc_attention_layer(self.ctx.handle, self.handle, C.byref(a)))
+
     def decode_host(self, q: np.ndarray, k: np.ndarray, v: np.ndarray, positions, layer_begin: int = 0,
                     layer_count: int | None = None, seq_ids=None, q_dtype: int | None = None,
                     in_dtype: int | None = None, out_dtype: int = F32, flags: int = 0, split: int = 0,
@@ -402,3 +412,22 @@ class ExecutionPlan:
         """GpuRuntimeBuffers::new's KV allocation (qx-runtime-v2 lib.rs:6774-6811)."""
         kd, vd = self.kv_precision.value
         return KvArena(ctx, MODEL_GRANITE, self.layers, sequences, self.context, kd, vd)
+
+
+class Q4Weights:
+    """A Q4 matrix on the device in the reference's row-major group-32 layout
+    (qx-quant QuantizedTensor): `codes` [rows][cols/32][16] uint8 and
+    `scales` [rows][cols/32] FP16 bits, as torch tensors (or anything with
+    __cuda_array_interface__ / data_ptr())."""
+
+    def __init__(self, codes, scales, rows: int, cols: int):
+        self.codes, self.scales, self.rows, self.cols = codes, scales, rows, cols
+
+    def ref(self) -> "_lib.Q4Matrix":
+        return _lib.Q4Matrix(self.rows, self.cols, _ptr(self.codes), _ptr(self.scales))
+
+
+def q4_mat_vec(ctx: "Context", w: Q4Weights, x, y, rms_weight=None) -> None:
+    """y = W x, or W rms_norm(x, rms_weight) (qxc_q4_mat_vec); device tensors."""
+    m = w.ref()
+    ctx.check(ctx.lib.qxc_q4_mat_vec(ctx.handle, C.byref(m), _ptr(x), _ptr(rms_weight), _ptr(y)))

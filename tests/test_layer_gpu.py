@@ -1,0 +1,129 @@
+"""The attention sub-layer with Q4 projections (qxc_q4_mat_vec,
+qxc_attention_layer) against the oracle's restatement of the reference's CPU
+layer (qx-runtime-v2 CpuQ4Reference::step, lib.rs:4680-4706).
+
+The RMSNorm and Q4 mat-vec keep the reference's lane order, so q/k/v, the
+appended key row and the projections are bit-exact; the layer output, which
+passes through the attention, is within the fp32 gate (1e-5 normwise).
+"""
+import sys
+import os
+
+import numpy as np
+import pytest
+
+from helpers import normwise
+from qx_b200 import F32, MODEL_GRANITE, KvArena, Q4Weights, q4_mat_vec
+from qx_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+
+def q4(oracle, rows, cols, seed, scale=0.05):
+    m = oracle.Q4Matrix((syn.normal(seed, (rows, cols)) * scale).astype(np.float32))
+    return m
+
+
+def dev_q4(m):
+    import torch
+    return Q4Weights(torch.from_numpy(m.codes).cuda(), torch.from_numpy(m.scales.view(np.int16)).cuda(), m.rows,
+                     m.cols)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 32), (7, 96), (512, 1024), (1024, 1024), (33, 4096)])
+def test_q4_mat_vec_bit_exact(gpu_ctx, oracle, rows, cols):
+    import torch
+    m = q4(oracle, rows, cols, 0x8100 + rows + cols)
+    x = syn.normal(0x8200 + cols, (cols,))
+    y = torch.zeros(rows, device="cuda")
+    q4_mat_vec(gpu_ctx, dev_q4(m), torch.from_numpy(x).cuda(), y)
+    gpu_ctx.sync()
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), m.mat_vec(x).view(np.uint32))
+
+
+def test_rms_then_q4_bit_exact(gpu_ctx, oracle):
+    import torch
+    m = q4(oracle, 512, 1024, 0x8300)
+    x = syn.normal(0x8301, (1024,)) * 3.0
+    w = (1.0 + 0.1 * syn.normal(0x8302, (1024,))).astype(np.float32)
+    st, xn = oracle.rms_norm_simd(x, w)
+    assert st == 1
+    y = torch.zeros(512, device="cuda")
+    q4_mat_vec(gpu_ctx, dev_q4(m), torch.from_numpy(x).cuda(), y, rms_weight=torch.from_numpy(w).cuda())
+    gpu_ctx.sync()
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), m.mat_vec(xn).view(np.uint32))
+
+
+def layer_setup(gpu_ctx, oracle, layers, prefix, cap):
+    import torch
+    W = []
+    for l in range(layers):
+        W.append(dict(norm=(1.0 + 0.1 * syn.normal(0x8400 + l, (1024,))).astype(np.float32),
+                      q=q4(oracle, 1024, 1024, 0x8410 + l), k=q4(oracle, 512, 1024, 0x8420 + l),
+                      v=q4(oracle, 512, 1024, 0x8430 + l), o=q4(oracle, 1024, 1024, 0x8440 + l)))
+    kc = syn.normal(0x8450, (layers, prefix, 8, 64))
+    vc = syn.normal(0x8451, (layers, prefix, 8, 64))
+    arena = KvArena(gpu_ctx, MODEL_GRANITE, layers, 1, cap, F32, F32)
+    caches = []
+    for l in range(layers):
+        c = oracle.KvCache(cap)
+        if prefix:
+            arena.write(0, l, 0, kc[l], vc[l])
+            c.keys[:prefix], c.values[:prefix] = kc[l], vc[l]
+            c.length.value = prefix
+        caches.append(c)
+    arena.set_len(0, prefix)
+    dW = [dict(norm=torch.from_numpy(w["norm"]).cuda(), q=dev_q4(w["q"]), k=dev_q4(w["k"]), v=dev_q4(w["v"]),
+               o=dev_q4(w["o"])) for w in W]
+    return W, dW, arena, caches
+
+
+@pytest.mark.parametrize("prefix", [0, 1, 300])
+def test_attention_layer_matches_oracle(gpu_ctx, oracle, prefix):
+    """Every layer fed the oracle's input for that layer: q/k/v and so every
+    cache row bit-exact; each layer's output within 1e-5."""
+    import torch
+    layers, tokens, cap = 2, 3, 320
+    W, dW, arena, caches = layer_setup(gpu_ctx, oracle, layers, prefix, cap)
+    for t in range(tokens):
+        ref = syn.normal(0x8460 + t, (1024,))
+        for l in range(layers):
+            inp = ref
+            st, ref, att_ref = oracle.granite_attention_layer(inp, W[l]["norm"], W[l]["q"], W[l]["k"], W[l]["v"],
+                                                              W[l]["o"], prefix + t, caches[l])
+            assert st == 0
+            out = torch.zeros(1024, device="cuda")
+            att = torch.zeros(1024, device="cuda")
+            arena.attention_layer(torch.from_numpy(inp).cuda(), out, dW[l]["norm"], dW[l]["q"], dW[l]["k"],
+                                  dW[l]["v"], dW[l]["o"], prefix + t, layer=l, attention_out=att,
+                                  flags=1 if l + 1 < layers else 0)
+            gpu_ctx.sync()
+            assert normwise(att.cpu().numpy(), att_ref) <= 1e-5
+            assert normwise(out.cpu().numpy(), ref) <= 1e-5
+    assert arena.len(0) == prefix + tokens
+    for l in range(layers):
+        gk, gv = arena.read(0, l, 0, prefix + tokens)
+        assert np.array_equal(gk.view(np.uint32), caches[l].keys[:prefix + tokens].view(np.uint32))
+        assert np.array_equal(gv.view(np.uint32), caches[l].values[:prefix + tokens].view(np.uint32))
+
+
+def test_attention_layers_chained(gpu_ctx, oracle):
+    """The GPU's own hidden states through a 4-layer stack for 4 tokens:
+    within 1e-5 of the oracle's stack."""
+    import torch
+    layers, tokens, prefix, cap = 4, 4, 200, 256
+    W, dW, arena, caches = layer_setup(gpu_ctx, oracle, layers, prefix, cap)
+    for t in range(tokens):
+        h = syn.normal(0x8470 + t, (1024,))
+        ref, cur = h.copy(), torch.from_numpy(h).cuda()
+        for l in range(layers):
+            st, ref, _ = oracle.granite_attention_layer(ref, W[l]["norm"], W[l]["q"], W[l]["k"], W[l]["v"],
+                                                        W[l]["o"], prefix + t, caches[l])
+            assert st == 0
+            nxt = torch.zeros(1024, device="cuda")
+            arena.attention_layer(cur, nxt, dW[l]["norm"], dW[l]["q"], dW[l]["k"], dW[l]["v"], dW[l]["o"],
+                                  prefix + t, layer=l, flags=1 if l + 1 < layers else 0)
+            cur = nxt
+        gpu_ctx.sync()
+        assert normwise(cur.cpu().numpy(), ref) <= 1e-5
+    assert arena.len(0) == prefix + tokens
