@@ -661,6 +661,90 @@ def run_config3(args, world, rank, local):
     return line
 
 
+def run_layer(args, world, rank, local):
+    """The attention sub-layers of the Granite stack with Q4 weights (the
+    reference's encode_attention_layer: RMSNorm, Q4 q/k/v, RoPE + append +
+    attention, Q4 o-projection, residual), 24 layers per token, fp32 KV at
+    context --context, positions cycled over the last 64 like config 1.
+    Random Q4 codes and FP16 scales stand in for the .qx weights."""
+    import torch
+    from qx_b200 import F32, MODEL_GRANITE, Context, KvArena, Q4Weights
+    from qx_b200 import _lib
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L = args.context
+    cycle = 64
+    P = L - cycle
+    ctx = Context(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    arena = KvArena(ctx, MODEL_GRANITE, LAYERS, 1, L, F32, F32)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0x51580500 + rank)
+
+    def q4w(rows, cols):
+        codes = torch.randint(0, 255, (rows, cols // 32, 16), dtype=torch.uint8, device=dev, generator=g)
+        scales = (torch.rand(rows, cols // 32, device=dev, generator=g) * 0.004 + 0.001).to(torch.float16)
+        return Q4Weights(codes, scales.view(torch.int16), rows, cols)
+
+    with torch.cuda.stream(stream):
+        for l in range(LAYERS):
+            arena.tensor(0, l, True)[:P].normal_(generator=g)
+            arena.tensor(0, l, False)[:P].normal_(generator=g)
+        weights = [dict(norm=1.0 + 0.1 * torch.randn(1024, device=dev, generator=g), q=q4w(1024, 1024),
+                        k=q4w(512, 1024), v=q4w(512, 1024), o=q4w(1024, 1024)) for _ in range(LAYERS)]
+        hidden = [torch.randn(1024, device=dev, generator=g) for _ in range(2)]
+    stream.synchronize()
+    arena.set_len(0, P)
+
+    def one(i):
+        pos = P + i % cycle
+        for l in range(LAYERS):
+            w = weights[l]
+            arena.attention_layer(hidden[l % 2], hidden[(l + 1) % 2], w["norm"], w["q"], w["k"], w["v"], w["o"],
+                                  pos, layer=l, flags=_lib.DECODE_NO_ADVANCE if l + 1 < LAYERS else 0)
+
+    # one step is 72 launches of a few microseconds each: capture a whole
+    # cycle of 64 tokens in a CUDA graph and replay it (the host cursor is
+    # rewound before each replay; the graph's kernels carry their positions)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            one(i)
+    stream.synchronize()
+    arena.rollback(0, P)
+    graph = torch.cuda.CUDAGraph()
+    n0 = ctx.launch_count
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(cycle):
+            one(i)
+    per_replay = ctx.launch_count - n0
+
+    def replay(i):
+        arena.rollback(0, P)
+        graph.replay()
+
+    K, W = max(1, args.steps // cycle), max(3, args.warmup // cycle)
+    with torch.cuda.stream(stream):
+        total, per, clk, _ = timed_steps(replay, K, W, stream, world, dev, local, ctx)
+    stream.synchronize()
+    per = [x / cycle for x in per]  # per token
+    steps = K * cycle
+    kv = sum(granite_stack_bytes(P + j + 1) for j in range(cycle)) / cycle
+    wbytes = LAYERS * (1024 + 512 + 512 + 1024) * (1024 // 2 + 1024 // 32 * 2)
+    B = kv + wbytes + LAYERS * 2 * 1024 * 4 * 2
+    line = base_line("attention sub-layer stack tok/s (Granite 24 layers, Q4 projections, fp32 KV)",
+                     world * steps / (total / 1e3), "tok/s", world, steps, W, total, True, "weak", "f32",
+                     {"workload": f"Granite 24-layer attention sub-layers with Q4 q/k/v/o (random codes), fp32 KV, "
+                                  f"context {L}, positions {P}..{L - 1} cycled, batch 1",
+                      "l2": "inputs larger than L2: ~400 MB of KV and 42 MB of Q4 weights per token",
+                      "timing": "64 tokens per CUDA graph replay", "bytes_per_token": int(B)},
+                     clk, K * per_replay)
+    line["roofline"] = hbm_roofline(B, per, "qx_q4_matvec_kernel + qx_decode_kernel<Granite,float,float>")
+    arena.close()
+    ctx.close()
+    return line
+
+
 def run_config4(args, world, rank, local):
     """Config 4: 256 independent Granite sequences, lengths U{128..4096}, bf16 KV,
     one decode step through 24 layers; sequences sharded over ranks by LPT on KV bytes."""
@@ -792,7 +876,8 @@ def main():
     ap.add_argument("--steps", type=int, default=3200)
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config1", choices=["config0", "config1", "config2", "config3", "config4"])
+    ap.add_argument("--workload", default="config1",
+                    choices=["config0", "config1", "config2", "config3", "config4", "layer"])
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--prefill-len", type=int, default=2048, help="config2 prompt length (512 or 2048)")
@@ -823,7 +908,7 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         run = {"config0": run_config0, "config1": run_config1, "config2": run_config2, "config3": run_config3,
-               "config4": run_config4}[args.workload]
+               "config4": run_config4, "layer": run_layer}[args.workload]
         line = run(args, world, rank, local)
         if rank == 0:
             print(json.dumps(line), flush=True)

@@ -47,18 +47,25 @@ struct LayerParams {
 };
 
 // One row of a Q4 matrix against x (shared memory), by the warp; the sum is
-// returned in lane 0. Lane l owns columns l, l + 32, ...: the nibble `l` of
-// every group, whose scale it gets from the lane that loaded it.
+// returned in lane 0. Lane l owns columns l, l + 32, ... — nibble l of every
+// group. The row's codes arrive as one 16-byte load per lane (group l) and
+// pass through the warp's shared staging slice, from which lane l reads byte
+// l / 2 of each group; group j's scale comes from lane j by a shuffle.
 __device__ __forceinline__ float q4_row_dot(const uint8_t* __restrict__ codes, const uint16_t* __restrict__ scales,
-                                            int groups, const float* x, int lane) {
+                                            int groups, const float* x, uint8_t* stage, int lane) {
   float acc = 0.0f;
   for (int g0 = 0; g0 < groups; g0 += 32) {
-    const float sc_l = g0 + lane < groups ? __half2float(__ushort_as_half(__ldg(scales + g0 + lane))) : 0.0f;
+    const bool mine = g0 + lane < groups;
+    const uint4 c = mine ? __ldg(reinterpret_cast<const uint4*>(codes) + g0 + lane) : make_uint4(0u, 0u, 0u, 0u);
+    const float sc_l = mine ? __half2float(__ushort_as_half(__ldg(scales + g0 + lane))) : 0.0f;
+    __syncwarp();
+    reinterpret_cast<uint4*>(stage)[lane] = c;
+    __syncwarp();
+    const int n = min(32, groups - g0);
 #pragma unroll 8
-    for (int j = 0; j < 32 && g0 + j < groups; ++j) {
+    for (int j = 0; j < n; ++j) {
       const float sc = __shfl_sync(0xffffffffu, sc_l, j);
-      const uint8_t byte = __ldg(codes + (g0 + j) * 16 + (lane >> 1));
-      const int code = (byte >> ((lane & 1) * 4)) & 0xF;
+      const int code = (stage[j * 16 + (lane >> 1)] >> ((lane & 1) * 4)) & 0xF;
       const float value = __fmul_rn((float)(code - 7), sc);
       acc = __fmaf_rn(value, x[(g0 + j) * 32 + lane], acc);
     }
@@ -72,16 +79,26 @@ __device__ __forceinline__ float q4_row_dot(const uint8_t* __restrict__ codes, c
 // 256 threads. With `residual`, row r's output is fma(0.22, dot, residual[r]).
 __global__ void __launch_bounds__(256) qx_q4_matvec_kernel(const __grid_constant__ LayerParams p) {
   __shared__ float xs[kHidden * 4];  // the input vector (up to 4096 columns)
+  __shared__ __align__(16) uint8_t stage[8][512];
   __shared__ float part[8];
   __shared__ float s_scale;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_launch_dependents();  // the next kernel may get resident and wait for this one
   pdl_wait();
   const int cols = p.w[0].cols;
   if (p.normalize) {
+    // every input and weight element of this thread in flight at once
+    float hv[kHidden / 256], wv[kHidden / 256];
+#pragma unroll
+    for (int k = 0; k < kHidden / 256; ++k) {
+      hv[k] = p.hidden[tid + 256 * k];
+      wv[k] = p.norm[tid + 256 * k];
+    }
     // cpu_rms_norm_simd: thread t sums x[t], x[t + 256], ... by fma; warps
     // and then the 8 warp sums reduce as reduce_simd32
     float sum = 0.0f;
-    for (int i = tid; i < kHidden; i += 256) sum = __fmaf_rn(p.hidden[i], p.hidden[i], sum);
+#pragma unroll
+    for (int k = 0; k < kHidden / 256; ++k) sum = __fmaf_rn(hv[k], hv[k], sum);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) sum = __fadd_rn(sum, __shfl_down_sync(0xffffffffu, sum, off));
     if (lane == 0) part[warp] = sum;
@@ -98,7 +115,8 @@ __global__ void __launch_bounds__(256) qx_q4_matvec_kernel(const __grid_constant
       }
     }
     __syncthreads();
-    for (int i = tid; i < kHidden; i += 256) xs[i] = __fmul_rn(__fmul_rn(p.hidden[i], s_scale), p.norm[i]);
+#pragma unroll
+    for (int k = 0; k < kHidden / 256; ++k) xs[tid + 256 * k] = __fmul_rn(__fmul_rn(hv[k], s_scale), wv[k]);
   } else {
     for (int i = tid; i < cols; i += 256) xs[i] = p.hidden[i];
   }
@@ -111,7 +129,7 @@ __global__ void __launch_bounds__(256) qx_q4_matvec_kernel(const __grid_constant
     const Q4Ref w = p.w[m];
     const int groups = w.cols / 32;
     const float y = q4_row_dot(w.codes + (long long)r * groups * 16, w.scales + (long long)r * groups, groups, xs,
-                               lane);
+                               stage[warp], lane);
     if (lane == 0) {
       float v = p.residual ? __fmaf_rn(kResidualMultiplier, y, p.residual[r]) : y;
       if (!isfinite(v)) flag_error(p.err, QX_ERR_BIT_NONFINITE);

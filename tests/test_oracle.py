@@ -164,3 +164,65 @@ def test_decode_many_threads_identical(oracle, threads):
         c.length.value = 40 + u
         st, o = oracle.granite_attention_decode(qs[u], ks[u], vs[u], 40 + u, c)
         assert np.array_equal(o, outs[u])
+
+
+# ---- the Q4 attention sub-layer (qx-runtime-v2 CpuQ4Reference::step) ----------------
+def test_q4_quantizer_follows_pack_scaled(oracle):
+    """qx-quant QuantizedTensor::quantize / pack_scaled: scale = max|x|/7
+    as FP16, codes round-half-away(x / scale) clamped to [-7, 7] + 7."""
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal((6, 96)) * 0.1).astype(np.float32)
+    w[2, 32:64] = 0.0  # an all-zero group takes scale 1.0
+    m = oracle.Q4Matrix(w)
+    scales = m.scales.view(np.float16).astype(np.float32)
+    for r in range(6):
+        for g in range(3):
+            grp = w[r, g * 32:(g + 1) * 32]
+            mx = np.abs(grp).max()
+            expect = np.float32(np.float16(mx / np.float32(7.0))) if mx > 0 else np.float32(1.0)
+            assert scales[r, g] == expect
+            lo = m.codes[r, g] & 0xF
+            hi = m.codes[r, g] >> 4
+            codes = np.empty(32, np.int32)
+            codes[0::2], codes[1::2] = lo, hi
+            q = grp / scales[r, g]
+            ref = np.clip(np.sign(q) * np.floor(np.abs(q) + 0.5), -7, 7).astype(np.int32) + 7
+            assert np.array_equal(codes, ref)
+
+
+def test_q4_mat_vec_and_rms_against_float64(oracle):
+    rng = np.random.default_rng(6)
+    m = oracle.Q4Matrix((rng.standard_normal((40, 1024)) * 0.05).astype(np.float32))
+    x = rng.standard_normal(1024).astype(np.float32)
+    scales = m.scales.view(np.float16).astype(np.float64)
+    codes = np.empty((40, 1024), np.float64)
+    for g in range(32):
+        for i in range(32):
+            c = (m.codes[:, g, i // 2] >> ((i & 1) * 4)) & 0xF
+            codes[:, g * 32 + i] = (c.astype(np.float64) - 7.0) * scales[:, g]
+    y = m.mat_vec(x)
+    assert np.abs(y - codes @ x.astype(np.float64)).max() <= 1e-5 * np.abs(codes @ x).max()
+    w = (1.0 + 0.1 * rng.standard_normal(1024)).astype(np.float32)
+    st, xn = oracle.rms_norm_simd(x, w)
+    assert st == 1
+    ref = x.astype(np.float64) / np.sqrt((x.astype(np.float64) ** 2).mean() + 1e-6) * w
+    assert np.abs(xn - ref).max() <= 2e-6 * np.abs(ref).max()
+
+
+def test_attention_layer_oracle_composes_its_parts(oracle):
+    """granite_attention_layer = rms -> q/k/v -> decode -> o -> fma residual."""
+    rng = np.random.default_rng(7)
+    W = [oracle.Q4Matrix((rng.standard_normal(s) * 0.05).astype(np.float32))
+         for s in ((1024, 1024), (512, 1024), (512, 1024), (1024, 1024))]
+    norm = (1.0 + 0.1 * rng.standard_normal(1024)).astype(np.float32)
+    h = rng.standard_normal(1024).astype(np.float32)
+    c1, c2 = oracle.KvCache(8), oracle.KvCache(8)
+    st, out, att = oracle.granite_attention_layer(h, norm, *W, 0, c1)
+    assert st == 0
+    _, xn = oracle.rms_norm_simd(h, norm)
+    q, k, v = W[0].mat_vec(xn), W[1].mat_vec(xn), W[2].mat_vec(xn)
+    st2, att2 = oracle.granite_attention_decode(q, k, v, 0, c2)
+    assert st2 == 0 and np.array_equal(att, att2)
+    o = W[3].mat_vec(att2)
+    assert np.array_equal(out, (np.float32(0.22) * o.astype(np.float64) + h).astype(np.float32)) or \
+        np.abs(out - (0.22 * o.astype(np.float64) + h)).max() <= 1e-6
