@@ -10,7 +10,7 @@ reference's speculative rollback does), so every step reads ~400 MB of KV,
 far more than the 126 MB L2.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload config1|config3|config4|config0]
+                    [--workload config1|config0|config2|config3|config4|layer|commit]
 
 Prints one JSON line on rank 0. N>1 runs under torchrun: one independent
 sequence (replica) per GPU, no collective on the data path ("weak" scaling),
@@ -745,6 +745,121 @@ def run_layer(args, world, rank, local):
     return line
 
 
+def run_commit(args, world, rank, local):
+    """KV-slot commitments (the reference's verification-hash stage): every
+    step hashes all 24 x 4096 slots of an fp32 Granite cache (402 MB, more
+    than the 126 MB L2) into 98,304 kv_leaf_hash_v1 digests with one
+    qxc_kv_slot_hashes launch; the per-token call of the reference
+    (qxc_verification_hashes: 25 positions, state roots + slot leaves) is
+    timed beside it. BLAKE3 is integer-ALU work: the roofline is the
+    measured compress-only rate of the same compression function."""
+    import torch
+    from qx_b200 import F32, MODEL_GRANITE, Context, KvArena
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L = args.context
+    ctx = Context(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    arena = KvArena(ctx, MODEL_GRANITE, LAYERS, 1, L, F32, F32)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0x51580600 + rank)
+    slots = LAYERS * L
+    with torch.cuda.stream(stream):
+        for l in range(LAYERS):
+            arena.tensor(0, l, True).normal_(generator=g)
+            arena.tensor(0, l, False).normal_(generator=g)
+        digests = torch.zeros(LAYERS, L, 32, dtype=torch.uint8, device=dev)
+        residuals = torch.randn(LAYERS + 1, 1024, device=dev, generator=g)
+        vdig = torch.zeros(LAYERS + 1, 64, dtype=torch.uint8, device=dev)
+    stream.synchronize()
+    arena.set_len(0, L)
+
+    def step(i):
+        arena.slot_hashes(digests, 0, LAYERS, 0, L)
+
+    with torch.cuda.stream(stream):
+        total, per, clk, launches = timed_steps(step, args.steps, args.warmup, stream, world, dev, local, ctx)
+    stream.synchronize()
+    K = args.steps
+    rate = ctx.blake3_compress_rate()
+    per_slot = 5 * 16 + 7 + 7 + 2  # leaves of 8 key + 8 value chunks, two 8-leaf trees, the 2-block slot leaf
+    avg_s = float(np.mean(per)) / 1e3
+    ach = slots * per_slot / avg_s
+    line = base_line("KV slot commitments/s (BLAKE3 kv_leaf_hash_v1, Granite 24 layers x 4096 tokens, fp32 KV)",
+                     world * K * slots / (total / 1e3), "slots/s", world, K, args.warmup, total, True, "weak", "u32",
+                     {"workload": f"all {LAYERS} x {L} (layer, token) slots of one fp32 Granite KV cache per step "
+                                  "(2 KB key + 2 KB value rows), one launch",
+                      "l2": f"inputs larger than L2: {slots * 4096 / 1e6:.0f} MB of KV hashed per step",
+                      "bytes_per_slot": 4096, "compressions_per_slot": per_slot},
+                     clk, launches)
+    # ncu DRAM bytes of a 24 x 2048-slot launch, scaled by the slots hashed
+    tr = profile_traffic("commit_ctx2048")
+    traffic = (tr["dram_read"] + tr["dram_write"]) * slots / tr["slots_per_launch"] if tr else None
+    line["roofline"] = {"bound": "alu", "achieved": ach / 1e9, "peak": rate / 1e9, "unit": "Gcompress/s",
+                        "frac": ach / rate, "peak_kind": "measured (qxc_blake3_compress_rate: the same BLAKE3 "
+                                                         "compression, registers only, every SM)",
+                        "traffic": traffic, "kernel": "qx_kv_hash_serial_kernel",
+                        "hbm_GBps": slots * 4096 / avg_s / 1e9, "avg_launch_us": avg_s * 1e6}
+    # the reference's per-token call: 25 positions (genesis + 24 layers),
+    # 4 KB residual snapshots, checkpoint interval 1 (its default)
+    with torch.cuda.stream(stream):
+        for _ in range(5):
+            arena.verification_hashes(L - 1, residuals, 4096, 1, vdig)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(200):
+            arena.verification_hashes(L - 1, residuals, 4096, 1, vdig)
+        e1.record(stream)
+    stream.synchronize()
+    line["per_token_call_us"] = e0.elapsed_time(e1) / 200 * 1e3
+    # the lane-per-chunk layout on the same range (the small-range default)
+    from qx_b200 import HASH_PER_CHUNK
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            arena.slot_hashes(digests, 0, LAYERS, 0, L, layout=HASH_PER_CHUNK)
+        e0.record(stream)
+        for _ in range(10):
+            arena.slot_hashes(digests, 0, LAYERS, 0, L, layout=HASH_PER_CHUNK)
+        e1.record(stream)
+    stream.synchronize()
+    line["per_chunk_layout_slots_per_s"] = slots * 10 / (e0.elapsed_time(e1) / 1e3)
+    # e2e: the public call plus the digests read back to pinned host memory
+    # (the hashed rows are the resident cache itself, nothing is uploaded)
+    if not args.no_e2e:
+        host = torch.empty(digests.shape, dtype=torch.uint8).pin_memory()
+        E = max(3, K // 4)
+
+        def estep(i):
+            arena.slot_hashes(digests, 0, LAYERS, 0, L)
+            host.copy_(digests, non_blocking=True)
+
+        with torch.cuda.stream(stream):
+            et, _, _, _ = timed_steps(estep, E, args.warmup, stream, world, dev, local, ctx)
+        line["e2e"] = {"value": world * E * slots / (et / 1e3), "unit": "slots/s", "h2d_bytes_per_step": 0,
+                       "d2h_bytes_per_step": int(digests.numel())}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import py_oracle as o
+        o.build()
+        rows = [(arena.read(0, l, t, 1)) for l, t in ((l, t) for l in range(2) for t in range(64))]
+        kb = [k.tobytes() for k, _ in rows]
+        vb = [v.tobytes() for _, v in rows]
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0:
+            for j in range(len(kb)):
+                o.kv_leaf_hash(j // 64, j % 64, kb[j], vb[j])
+            n += len(kb)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": n / dt, "unit": "slots/s", "cores": 1, "kind": "port",
+                                "sample": f"{n} kv_leaf_hash_v1 slots of the same cache (fp32 rows), one thread, "
+                                          "oracle/qx_oracle.c (restatement of qx-commit state.rs with the "
+                                          "published BLAKE3)", "seconds": dt}
+    arena.close()
+    ctx.close()
+    return line
+
+
 def run_config4(args, world, rank, local):
     """Config 4: 256 independent Granite sequences, lengths U{128..4096}, bf16 KV,
     one decode step through 24 layers; sequences sharded over ranks by LPT on KV bytes."""
@@ -877,7 +992,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config1",
-                    choices=["config0", "config1", "config2", "config3", "config4", "layer"])
+                    choices=["config0", "config1", "config2", "config3", "config4", "layer", "commit"])
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--prefill-len", type=int, default=2048, help="config2 prompt length (512 or 2048)")
@@ -908,7 +1023,7 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         run = {"config0": run_config0, "config1": run_config1, "config2": run_config2, "config3": run_config3,
-               "config4": run_config4, "layer": run_layer}[args.workload]
+               "config4": run_config4, "layer": run_layer, "commit": run_commit}[args.workload]
         line = run(args, world, rank, local)
         if rank == 0:
             print(json.dumps(line), flush=True)

@@ -241,6 +241,49 @@ typedef struct {
 
 qxc_status qxc_attention_layer(qxc_ctx* ctx, qxc_kv* kv, const qxc_layer_args* args);
 
+/* ---- commitments of KV slots and residual checkpoints (BLAKE3) ----------- */
+/* Replaces the reference's verification-hash stage
+ * (GpuDecodeGraph::encode_verification_hashes, qx-metal lib.rs:9247-9330,
+ * kernels/verification_hash.metal; called per token at qx-runtime-v2
+ * lib.rs:2215 and :2440). For token `token` of `seq`, position p in
+ * 0..layers (the arena's layer count) writes 64 bytes at digests + 64 p:
+ *   [0, 32)  state_hash_v1 of residual snapshot p (residuals + p * stride) when
+ *            p == 0, (p % checkpoint_interval) == 0 or p == layers; else zeros
+ *   [32, 64) kv_leaf_hash_v1(p - 1, token, key row, value row) read from the
+ *            arena; zeros at p == 0
+ * (qx-commit state.rs:213-257, :334-368). residual_stride is a power-of-two
+ * number of 256-byte chunks, at most 16; the arena's rows must be 1 to 8
+ * chunks (every arena type is); token < the sequence's length, else
+ * QXC_ERR_POSITION. residuals 16-byte aligned. Device pointers, asynchronous. */
+typedef struct {
+  int32_t seq;
+  int32_t token;
+  const void* residuals;   /* (layers + 1) * residual_stride bytes */
+  int64_t residual_stride; /* bytes */
+  int32_t checkpoint_interval; /* 1..layers */
+  uint8_t* digests;        /* (layers + 1) * 64 bytes */
+} qxc_verification_hash_args;
+
+qxc_status qxc_verification_hashes(qxc_ctx* ctx, qxc_kv* kv, const qxc_verification_hash_args* args);
+
+/* kv_leaf_hash_v1(layer, token, key row, value row) of every slot of
+ * [layer_begin, +layer_count) x [token_begin, +token_count) of `seq`, into
+ * digests[layer_count][token_count][32] (device): the commitments of a whole
+ * prefill or accepted speculative prefix in one launch. Rows must lie below
+ * the sequence's length (else QXC_ERR_POSITION). flags picks the kernel
+ * layout (QXC_HASH_*; 0 chooses by range size; the digests are the same).
+ * Asynchronous. */
+#define QXC_HASH_AUTO 0
+#define QXC_HASH_PER_CHUNK 1 /* a lane per 256-byte chunk: lowest latency */
+#define QXC_HASH_PER_SLOT 2  /* a lane per slot: highest throughput on large ranges */
+qxc_status qxc_kv_slot_hashes(qxc_ctx* ctx, qxc_kv* kv, int32_t seq, int32_t layer_begin, int32_t layer_count,
+                              int32_t token_begin, int32_t token_count, uint8_t* digests, int32_t flags);
+
+/* Measurement helper: BLAKE3 block compressions per second on this device
+ * with no memory traffic (every SM's integer pipes busy) — the ceiling the
+ * hash kernels are compared against. Synchronous; about 10 ms. */
+qxc_status qxc_blake3_compress_rate(qxc_ctx* ctx, double* compressions_per_second);
+
 /* ---- causal prefill ------------------------------------------------------ */
 /* Prompt prefill of `length` tokens into an EMPTY (sequence, layer) of a
  * Granite arena (cursor must be 0): RoPE on q and k at positions

@@ -68,6 +68,9 @@ def lib():
         _lib.qxo_q4_mat_vec_simd32.argtypes = [u8p, u16p, C.c_int, C.c_int, fp, fp]
         _lib.qxo_granite_attention_layer.argtypes = [fp, fp, u8p, u16p, u8p, u16p, u8p, u16p, u8p, u16p, C.c_int,
                                                      fp, fp, ip, C.c_int, fp, fp]
+        _lib.qxo_blake3_single_chunk.argtypes = [vp, C.c_size_t, u8p]
+        _lib.qxo_chunk_tree_hash.argtypes = [vp, C.c_size_t, C.c_char_p, C.c_char_p, u8p]
+        _lib.qxo_kv_leaf_hash.argtypes = [C.c_uint16, C.c_uint32, vp, C.c_size_t, vp, C.c_size_t, u8p]
     return _lib
 
 
@@ -255,3 +258,49 @@ def granite_attention_layer(hidden, input_norm, qp: Q4Matrix, kp: Q4Matrix, vp: 
                                            _u16(op.scales), position, _fp(cache.keys), _fp(cache.values),
                                            C.byref(cache.length), cache.max_context, _fp(out), _fp(att))
     return st, out, att
+
+
+# ---- KV-slot commitments (qx-commit state.rs) -----------------------------------------
+def blake3_single_chunk(data: bytes) -> bytes:
+    out = np.zeros(32, np.uint8)
+    buf = np.frombuffer(bytes(data), np.uint8) if data else np.zeros(1, np.uint8)
+    assert lib().qxo_blake3_single_chunk(buf.ctypes.data, len(data), _u8(out)) == 1
+    return out.tobytes()
+
+
+def chunk_tree_hash(data: bytes, leaf_domain: bytes, tree_domain: bytes) -> bytes:
+    out = np.zeros(32, np.uint8)
+    buf = np.frombuffer(bytes(data), np.uint8)
+    assert lib().qxo_chunk_tree_hash(buf.ctypes.data, len(data), leaf_domain, tree_domain, _u8(out)) == 1
+    return out.tobytes()
+
+
+def kv_leaf_hash(layer: int, token: int, key: bytes, value: bytes) -> bytes:
+    """kv_leaf_hash_v1: the 32-byte commitment of one (layer, token) K/V slot."""
+    out = np.zeros(32, np.uint8)
+    kb, vb = np.frombuffer(bytes(key), np.uint8), np.frombuffer(bytes(value), np.uint8)
+    assert lib().qxo_kv_leaf_hash(layer, token, kb.ctypes.data, len(key), vb.ctypes.data, len(value), _u8(out)) == 1
+    return out.tobytes()
+
+
+def state_hash(residual: bytes) -> bytes:
+    """state_hash_v1 (qx-commit state.rs:253-257): the chunk tree of a
+    residual snapshot under QX:STATE:CHUNK:V1 / QX:STATE:V1."""
+    return chunk_tree_hash(residual, b"QX:STATE:CHUNK:V1", b"QX:STATE:V1")
+
+
+def verification_hashes(residuals: bytes, residual_stride: int, checkpoint_interval: int, layers: int,
+                        key_rows, value_rows, token: int) -> bytes:
+    """The bytes encode_verification_hashes writes for one token
+    (kernels/verification_hash.metal:428-522): per position p in 0..layers,
+    32 bytes of state root (p == 0, p % interval == 0 or p == layers; else
+    zeros) then 32 bytes of kv_leaf_hash_v1(p - 1, token, ...) (zeros at
+    p == 0). key_rows[l] / value_rows[l] are layer l's row bytes."""
+    out = bytearray()
+    for p in range(layers + 1):
+        if p == 0 or p % checkpoint_interval == 0 or p == layers:
+            out += state_hash(residuals[p * residual_stride:(p + 1) * residual_stride])
+        else:
+            out += bytes(32)
+        out += bytes(32) if p == 0 else kv_leaf_hash(p - 1, token, key_rows[p - 1], value_rows[p - 1])
+    return bytes(out)

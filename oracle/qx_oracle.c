@@ -730,3 +730,139 @@ int qxo_granite_attention_layer(const float* hidden, const float* input_norm,
   for (int i = 0; i < G_HIDDEN; ++i) out[i] = fmaf(0.22f, projection[i], hidden[i]); /* RESIDUAL_MULTIPLIER */
   return QXO_OK;
 }
+
+/* ===================================================================== */
+/* KV-slot commitments: BLAKE3 and qx-commit's chunk trees               */
+/* ===================================================================== */
+
+/* BLAKE3 as published (the reference links the blake3 crate 1.8.7). Only
+ * single-chunk inputs (<= 1024 bytes) occur on this path. */
+static const uint32_t B3_IV[8] = {0x6A09E667u, 0xBB67AE85u, 0x3C6EF372u, 0xA54FF53Au,
+                                  0x510E527Fu, 0x9B05688Cu, 0x1F83D9ABu, 0x5BE0CD19u};
+static const uint8_t B3_PERM[16] = {2, 6, 3, 10, 7, 0, 4, 13, 1, 11, 12, 5, 9, 14, 15, 8};
+
+static uint32_t b3_rotr(uint32_t v, int n) { return (v >> n) | (v << (32 - n)); }
+
+static void b3_g(uint32_t* s, int a, int b, int c, int d, uint32_t x, uint32_t y) {
+  s[a] = s[a] + s[b] + x;
+  s[d] = b3_rotr(s[d] ^ s[a], 16);
+  s[c] = s[c] + s[d];
+  s[b] = b3_rotr(s[b] ^ s[c], 12);
+  s[a] = s[a] + s[b] + y;
+  s[d] = b3_rotr(s[d] ^ s[a], 8);
+  s[c] = s[c] + s[d];
+  s[b] = b3_rotr(s[b] ^ s[c], 7);
+}
+
+static void b3_compress(const uint32_t cv[8], const uint8_t block[64], uint32_t block_len, uint32_t flags,
+                        uint32_t out[8]) {
+  uint32_t m[16], s[16], t[16];
+  for (int i = 0; i < 16; ++i)
+    m[i] = (uint32_t)block[4 * i] | ((uint32_t)block[4 * i + 1] << 8) | ((uint32_t)block[4 * i + 2] << 16) |
+           ((uint32_t)block[4 * i + 3] << 24);
+  for (int i = 0; i < 8; ++i) s[i] = cv[i];
+  for (int i = 0; i < 4; ++i) s[8 + i] = B3_IV[i];
+  s[12] = 0; /* chunk counter: one chunk */
+  s[13] = 0;
+  s[14] = block_len;
+  s[15] = flags;
+  for (int round = 0; round < 7; ++round) {
+    b3_g(s, 0, 4, 8, 12, m[0], m[1]);
+    b3_g(s, 1, 5, 9, 13, m[2], m[3]);
+    b3_g(s, 2, 6, 10, 14, m[4], m[5]);
+    b3_g(s, 3, 7, 11, 15, m[6], m[7]);
+    b3_g(s, 0, 5, 10, 15, m[8], m[9]);
+    b3_g(s, 1, 6, 11, 12, m[10], m[11]);
+    b3_g(s, 2, 7, 8, 13, m[12], m[13]);
+    b3_g(s, 3, 4, 9, 14, m[14], m[15]);
+    for (int i = 0; i < 16; ++i) t[i] = m[B3_PERM[i]];
+    memcpy(m, t, sizeof(m));
+  }
+  for (int i = 0; i < 8; ++i) out[i] = s[i] ^ s[i + 8];
+}
+
+int qxo_blake3_single_chunk(const uint8_t* input, size_t len, uint8_t out[32]) {
+  if (len > 1024) return 0;
+  uint32_t cv[8];
+  memcpy(cv, B3_IV, sizeof(cv));
+  const size_t blocks = len == 0 ? 1 : (len + 63) / 64;
+  for (size_t b = 0; b < blocks; ++b) {
+    uint8_t block[64] = {0};
+    const size_t n = b + 1 < blocks ? 64 : len - b * 64;
+    memcpy(block, input + b * 64, n);
+    uint32_t flags = (b == 0 ? 1u : 0u) | (b + 1 == blocks ? 2u | 8u : 0u); /* CHUNK_START, CHUNK_END|ROOT */
+    uint32_t next[8];
+    b3_compress(cv, block, (uint32_t)n, flags, next);
+    memcpy(cv, next, sizeof(cv));
+  }
+  for (int i = 0; i < 8; ++i) {
+    out[4 * i] = (uint8_t)cv[i];
+    out[4 * i + 1] = (uint8_t)(cv[i] >> 8);
+    out[4 * i + 2] = (uint8_t)(cv[i] >> 16);
+    out[4 * i + 3] = (uint8_t)(cv[i] >> 24);
+  }
+  return 1;
+}
+
+/* hash_domain (qx-commit hash.rs): domain, then per field u64 LE length and
+ * the field's bytes. */
+static int b3_domain(const char* domain, const uint8_t* const* fields, const size_t* lens, int n, uint8_t out[32]) {
+  uint8_t buf[1024];
+  size_t at = strlen(domain);
+  memcpy(buf, domain, at);
+  for (int f = 0; f < n; ++f) {
+    if (at + 8 + lens[f] > sizeof(buf)) return 0;
+    for (int i = 0; i < 8; ++i) buf[at + i] = (uint8_t)((uint64_t)lens[f] >> (8 * i));
+    at += 8;
+    memcpy(buf + at, fields[f], lens[f]);
+    at += lens[f];
+  }
+  return qxo_blake3_single_chunk(buf, at, out);
+}
+
+int qxo_chunk_tree_hash(const uint8_t* bytes, size_t len, const char* leaf_domain, const char* tree_domain,
+                        uint8_t out[32]) {
+  if (len == 0) return 0;
+  const size_t leaves = (len + 255) / 256;
+  size_t cap = 1;
+  while (cap < leaves) cap <<= 1;
+  uint8_t (*nodes)[32] = malloc(cap * 32);
+  if (!nodes) return 0;
+  for (size_t i = 0; i < leaves; ++i) {
+    const uint8_t index[4] = {(uint8_t)i, (uint8_t)(i >> 8), (uint8_t)(i >> 16), (uint8_t)(i >> 24)};
+    const size_t n = i + 1 < leaves ? 256 : len - i * 256;
+    const uint8_t* fields[2] = {index, bytes + i * 256};
+    const size_t lens[2] = {4, n};
+    b3_domain(leaf_domain, fields, lens, 2, nodes[i]);
+  }
+  if (cap > leaves) {
+    uint8_t empty[32];
+    const uint8_t* fields[1] = {(const uint8_t*)tree_domain};
+    const size_t lens[1] = {strlen(tree_domain)};
+    b3_domain("QX:MERKLE:EMPTY:V1", fields, lens, 1, empty);
+    for (size_t i = leaves; i < cap; ++i) memcpy(nodes[i], empty, 32);
+  }
+  for (size_t width = cap; width > 1; width /= 2)
+    for (size_t i = 0; i < width / 2; ++i) {
+      uint8_t pair[64];
+      memcpy(pair, nodes[2 * i], 32);
+      memcpy(pair + 32, nodes[2 * i + 1], 32);
+      qxo_blake3_single_chunk(pair, 64, nodes[i]);
+    }
+  memcpy(out, nodes[0], 32);
+  free(nodes);
+  return 1;
+}
+
+int qxo_kv_leaf_hash(uint16_t layer, uint32_t token, const uint8_t* key_bytes, size_t key_len,
+                     const uint8_t* value_bytes, size_t value_len, uint8_t out[32]) {
+  uint8_t key_root[32], value_root[32];
+  if (!qxo_chunk_tree_hash(key_bytes, key_len, "QX:KV:KEY:CHUNK:V1", "QX:KV:KEY:TREE:V1", key_root)) return 0;
+  if (!qxo_chunk_tree_hash(value_bytes, value_len, "QX:KV:VALUE:CHUNK:V1", "QX:KV:VALUE:TREE:V1", value_root))
+    return 0;
+  const uint8_t l[2] = {(uint8_t)layer, (uint8_t)(layer >> 8)};
+  const uint8_t t[4] = {(uint8_t)token, (uint8_t)(token >> 8), (uint8_t)(token >> 16), (uint8_t)(token >> 24)};
+  const uint8_t* fields[4] = {l, t, key_root, value_root};
+  const size_t lens[4] = {2, 4, 32, 32};
+  return b3_domain("QX:KV:V1", fields, lens, 4, out);
+}

@@ -142,6 +142,22 @@ int qxo_granite_attention_layer(const float* hidden, const float* input_norm,
                                 int position, float* keys, float* values, int* length,
                                 int capacity, float* out, float* attention_out);
 
+/* ---- KV-slot commitments (qx-commit state.rs:213-251 and :334-368) ---- */
+/* BLAKE3 (the blake3 crate 1.8.7, Cargo.lock:656-657; the published
+ * algorithm) of an input of at most 1024 bytes, i.e. one chunk: every
+ * commitment input on this path fits one. Returns 0 for longer inputs. */
+int qxo_blake3_single_chunk(const uint8_t* input, size_t len, uint8_t out[32]);
+/* chunk_tree_hash (state.rs:213-251): 256-byte leaves hashed as
+ * hash_domain(leaf_domain, [u32 index LE, chunk]), padded with the empty
+ * leaf hash_domain(QX:MERKLE:EMPTY:V1, [tree_domain]) to a power of two,
+ * reduced by BLAKE3(left || right). Returns 0 on empty input. */
+int qxo_chunk_tree_hash(const uint8_t* bytes, size_t len, const char* leaf_domain, const char* tree_domain,
+                        uint8_t out[32]);
+/* kv_leaf_hash_v1 (state.rs:334-368): the K and V chunk-tree roots bound to
+ * (layer, token) under QX:KV:V1. */
+int qxo_kv_leaf_hash(uint16_t layer, uint32_t token, const uint8_t* key_bytes, size_t key_len,
+                     const uint8_t* value_bytes, size_t value_len, uint8_t out[32]);
+
 #ifdef __cplusplus
 }
 #endif

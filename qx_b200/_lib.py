@@ -18,6 +18,7 @@ OK, ERR_INVALID_ARG, ERR_POSITION, ERR_NONFINITE, ERR_CUDA, ERR_NCCL, ERR_TIMEOU
 MODEL_GRANITE, MODEL_QWEN3 = 0, 1
 F32, BF16, F16 = 0, 1, 2
 DECODE_NO_ADVANCE, DECODE_NATIVE_EXP, DECODE_PINNED_EXP = 0x1, 0x2, 0x4
+HASH_AUTO, HASH_PER_CHUNK, HASH_PER_SLOT = 0, 1, 2
 
 
 class KvDesc(C.Structure):
@@ -66,6 +67,12 @@ class LayerArgs(C.Structure):
                 ("hidden_out", C.c_void_p), ("input_norm", C.c_void_p), ("q_proj", Q4Matrix), ("k_proj", Q4Matrix),
                 ("v_proj", Q4Matrix), ("o_proj", Q4Matrix), ("attention_out", C.c_void_p), ("flags", C.c_int32),
                 ("split", C.c_int32)]
+
+
+class VerificationHashArgs(C.Structure):
+    """qxc_verification_hash_args (per-token state roots and KV slot leaves)."""
+    _fields_ = [("seq", C.c_int32), ("token", C.c_int32), ("residuals", C.c_void_p),
+                ("residual_stride", C.c_int64), ("checkpoint_interval", C.c_int32), ("digests", C.c_void_p)]
 
 
 class StaticDecodeArgs(C.Structure):
@@ -124,6 +131,9 @@ def load() -> C.CDLL:
         "qxc_q4_mat_vec": (C.c_int, [vp, C.POINTER(Q4Matrix), vp, vp, vp]),
         "qxc_attention_layer": (C.c_int, [vp, vp, C.POINTER(LayerArgs)]),
         "qxc_lse_merge": (C.c_int, [vp, i32, i32, vp, vp, i32]),
+        "qxc_verification_hashes": (C.c_int, [vp, vp, C.POINTER(VerificationHashArgs)]),
+        "qxc_kv_slot_hashes": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp, i32]),
+        "qxc_blake3_compress_rate": (C.c_int, [vp, C.POINTER(C.c_double)]),
         "qxc_granite_decode_static_scratch": (C.c_int, [C.POINTER(StaticDecodeArgs), vp, C.c_char_p, C.c_size_t]),
     }
     for name, (res, args) in sig.items():

@@ -27,6 +27,7 @@
 #include "append.cuh"
 #include "layer.cuh"
 #include "prefill.cuh"
+#include "commit.cuh"
 
 using namespace qx;
 
@@ -630,6 +631,63 @@ qxc_status launch_append(qxc_ctx* ctx, const AppendParams& a, int grid) {
   cfg.numAttrs = 1;
   QXC_CUDA(ctx, cudaLaunchKernelEx(&cfg, qx_append_rows_kernel<M, KT, VT>, a));
   ctx->launches++;
+  return QXC_OK;
+}
+
+// Hash kernel, a programmatic dependent like the decode (it waits for the
+// stream's previous kernel before reading rows).
+qxc_status launch_hash(qxc_ctx* ctx, const HashParams& p, int ctas, void (*fn)(HashParams) = qx_kv_hash_kernel,
+                       int smem = 0, int warps_per_cta = kHashWarps) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(ctas);
+  cfg.blockDim = dim3(32 * warps_per_cta);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QXC_CUDA(ctx, cudaLaunchKernelEx(&cfg, fn, p));
+  ctx->launches++;
+  return QXC_OK;
+}
+
+// Row geometry shared by both hash entry points: rows of 1, 2, 4 or 8
+// 256-byte chunks (encode_verification_hashes' rule, qx-metal lib.rs:9288-9302).
+qxc_status hash_params(qxc_ctx* ctx, const qxc_kv* kv, int seq, HashParams* p) {
+  memset(p, 0, sizeof(*p));
+  const long long krow = (long long)kv->hkv * kv->d * (long long)kv->kes;
+  const long long vrow = (long long)kv->hkv * kv->d * (long long)kv->ves;
+  for (long long b : {krow, vrow}) {
+    const long long c = b / 256;
+    if (b % 256 != 0 || c < 1 || c > 8 || (c & (c - 1)) != 0)
+      return fail(ctx, QXC_ERR_UNSUPPORTED, "KV row of %lld bytes is not 1, 2, 4 or 8 chunks of 256", b);
+  }
+  p->k_region = kv->k_region;
+  p->v_region = kv->v_region;
+  p->k_unit_bytes = (long long)kv->k_unit;
+  p->v_unit_bytes = (long long)kv->v_unit;
+  p->key_row_bytes = (int)krow;
+  p->value_row_bytes = (int)vrow;
+  p->layers = kv->desc.layers;
+  p->seq = seq;
+  p->checkpoint_interval = 1;
+  // hash_domain's framing of a chunk leaf up to the chunk bytes (qx-commit
+  // state.rs:225-233): domain, u64 4, u32 index (zero here), u64 256
+  const char* domains[3] = {"QX:STATE:CHUNK:V1", "QX:KV:KEY:CHUNK:V1", "QX:KV:VALUE:CHUNK:V1"};
+  for (int r = 0; r < 3; ++r) {
+    unsigned char b[48] = {0};
+    const size_t n = strlen(domains[r]);
+    memcpy(b, domains[r], n);
+    b[n] = 4;          // u64 4
+    b[n + 12 + 1] = 1;  // u64 256 = 00 01 00 ...
+    p->prefix_len[r] = (int)n + 20;
+    for (int w = 0; w < 12; ++w)
+      p->prefix[r][w] = (uint32_t)b[4 * w] | (uint32_t)b[4 * w + 1] << 8 | (uint32_t)b[4 * w + 2] << 16 |
+                        (uint32_t)b[4 * w + 3] << 24;
+  }
   return QXC_OK;
 }
 
@@ -1370,6 +1428,113 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
   QXC_CUDA(ctx, cudaLaunchKernelEx(&cfg, qx_prefill_attn_tc_kernel, p));
   ctx->launches += 2;
   if (!(a->flags & QXC_DECODE_NO_ADVANCE)) kv->len[a->seq] = a->length;
+  return QXC_OK;
+}
+
+// ---- commitments -----------------------------------------------------------------
+qxc_status qxc_verification_hashes(qxc_ctx* ctx, qxc_kv* kv, const qxc_verification_hash_args* a) {
+  if (!ctx || !kv || !a) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (kv->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "KV arena belongs to another context");
+  qxc_status st = check_seq(ctx, kv, a->seq);
+  if (st != QXC_OK) return st;
+  if (!a->residuals || !a->digests) return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
+  const int layers = kv->desc.layers;
+  // the reference's own limits (qx-metal lib.rs:9262-9302)
+  if (a->checkpoint_interval < 1 || a->checkpoint_interval > layers)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "verification checkpoint interval %d is outside 1..=%d",
+                a->checkpoint_interval, layers);
+  const long long chunks = a->residual_stride / 256;
+  if (a->residual_stride <= 0 || a->residual_stride % 256 != 0 || chunks > 16 || (chunks & (chunks - 1)) != 0)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "verification residual size %lld is not 1..16 (a power of two) chunks of 256",
+                (long long)a->residual_stride);
+  if ((uintptr_t)a->residuals & 15u) return fail(ctx, QXC_ERR_INVALID_ARG, "residual snapshots must be 16-byte aligned");
+  if (a->token < 0 || a->token >= kv->len[a->seq])
+    return fail(ctx, QXC_ERR_POSITION, "token %d is not below cache length %d", a->token, kv->len[a->seq]);
+  HashParams p;
+  st = hash_params(ctx, kv, a->seq, &p);
+  if (st != QXC_OK) return st;
+  p.mode = kHashModeVerify;
+  p.token = a->token;
+  p.residuals = static_cast<const char*>(a->residuals);
+  p.residual_stride = a->residual_stride;
+  p.checkpoint_interval = a->checkpoint_interval;
+  p.out = a->digests;
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  return launch_hash(ctx, p, (layers + 1 + kHashWarps - 1) / kHashWarps);
+}
+
+qxc_status qxc_kv_slot_hashes(qxc_ctx* ctx, qxc_kv* kv, int32_t seq, int32_t layer_begin, int32_t layer_count,
+                              int32_t token_begin, int32_t token_count, uint8_t* digests, int32_t flags) {
+  if (!ctx || !kv) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (kv->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "KV arena belongs to another context");
+  qxc_status st = check_seq(ctx, kv, seq);
+  if (st != QXC_OK) return st;
+  if (!digests) return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
+  if (layer_count < 1 || layer_begin < 0 || layer_begin + layer_count > kv->desc.layers)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "layers [%d, %d) outside the arena's %d layers", layer_begin,
+                layer_begin + layer_count, kv->desc.layers);
+  if (token_count < 1 || token_begin < 0 || token_begin + token_count > kv->len[seq])
+    return fail(ctx, QXC_ERR_POSITION, "tokens [%d, %d) are not below cache length %d", token_begin,
+                token_begin + token_count, kv->len[seq]);
+  HashParams p;
+  st = hash_params(ctx, kv, seq, &p);
+  if (st != QXC_OK) return st;
+  p.mode = kHashModeSlots;
+  p.layer_begin = layer_begin;
+  p.layer_count = layer_count;
+  p.token_begin = token_begin;
+  p.token_count = token_count;
+  const int chunks = std::max(p.key_row_bytes, p.value_row_bytes) / 256;
+  p.seg = chunks;  // a power of two <= 8
+  p.out = digests;
+  const long long slots = (long long)layer_count * token_count;
+  if (slots > (1ll << 31) - 1) return fail(ctx, QXC_ERR_INVALID_ARG, "too many slots");
+  if (flags < QXC_HASH_AUTO || flags > QXC_HASH_PER_SLOT) return fail(ctx, QXC_ERR_INVALID_ARG, "unknown hash flags");
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  // a lane pair per slot once the range gives every SM at least 8 full warps
+  bool serial = flags == QXC_HASH_PER_SLOT;
+  if (flags == QXC_HASH_AUTO) serial = slots >= 16ll * 8 * ctx->sm_count;
+  if (!serial) {
+    const long long per_cta = 32 / (2 * p.seg) * kHashWarps;
+    return launch_hash(ctx, p, (int)((slots + per_cta - 1) / per_cta));
+  }
+  static unsigned long long configured = 0;
+  const unsigned long long bit = 1ull << (ctx->device & 63);
+  if (!(configured & bit)) {
+    QXC_CUDA(ctx, cudaFuncSetAttribute(qx_kv_hash_serial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kHashSerialSmem));
+    configured |= bit;
+  }
+  const long long per_cta = 16ll * kHashSerialWarps;  // a lane pair per slot
+  return launch_hash(ctx, p, (int)((slots + per_cta - 1) / per_cta), qx_kv_hash_serial_kernel, kHashSerialSmem,
+                     kHashSerialWarps);
+}
+
+qxc_status qxc_blake3_compress_rate(qxc_ctx* ctx, double* per_second) {
+  if (!ctx || !per_second) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  int sms = 0;
+  QXC_CUDA(ctx, cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device));
+  int per_sm = 0;
+  QXC_CUDA(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qx_b3_compress_rate_kernel, 256, 0));
+  const int grid = sms * std::max(per_sm, 1), iters = 2048;
+  cudaEvent_t e0, e1;
+  QXC_CUDA(ctx, cudaEventCreate(&e0));
+  QXC_CUDA(ctx, cudaEventCreate(&e1));
+  float best = 1e30f;
+  for (int rep = 0; rep < 4; ++rep) {  // the first is warm-up
+    cudaEventRecord(e0, ctx->stream);
+    qx_b3_compress_rate_kernel<<<grid, 256, 0, ctx->stream>>>(iters);
+    cudaEventRecord(e1, ctx->stream);
+    cudaEventSynchronize(e1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    if (rep > 0) best = std::min(best, ms);
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  QXC_CUDA(ctx, cudaGetLastError());
+  *per_second = (double)grid * 256 * iters / (best * 1e-3);
   return QXC_OK;
 }
 

@@ -24,7 +24,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from ._lib import BF16, F16, F32, MODEL_GRANITE, MODEL_QWEN3  # noqa: F401
+from ._lib import BF16, F16, F32, HASH_AUTO, HASH_PER_CHUNK, HASH_PER_SLOT, MODEL_GRANITE, MODEL_QWEN3  # noqa: F401
 
 HIDDEN, ATTENTION_HEADS, KV_HEADS, HEAD_DIM, MAX_CONTEXT, LAYERS = 1024, 16, 8, 64, 4096, 24  # qx-model lib.rs:9-17
 ATTENTION_MULTIPLIER = 0.015625  # qx-model lib.rs:20
@@ -111,6 +111,13 @@ class Context:
     def last_split(self) -> int:
         """Cache positions per split chosen by the last decode call."""
         return int(self.lib.qxc_last_split(self.handle))
+
+    def blake3_compress_rate(self) -> float:
+        """BLAKE3 block compressions per second with no memory traffic (the
+        ceiling the hash kernels are measured against); synchronous."""
+        r = C.c_double()
+        self.check(self.lib.qxc_blake3_compress_rate(self.handle, C.byref(r)))
+        return r.value
 
     def lse_merge(self, model: int, n_parts: int, partials, out, out_dtype: int = F32) -> None:
         self.check(self.lib.qxc_lse_merge(self.handle, model, n_parts, _ptr(partials), _ptr(out), out_dtype))
@@ -274,6 +281,24 @@ class KvArena:
         a = _lib.LayerArgs(seq, layer, position, _ptr(hidden_in), _ptr(hidden_out), _ptr(input_norm),
                            q_proj.ref(), k_proj.ref(), v_proj.ref(), o_proj.ref(), _ptr(attention_out), flags, split)
         self.ctx.check(self.lib.qxc_attention_layer(self.ctx.handle, self.handle, C.byref(a)))
+
+    def verification_hashes(self, token: int, residuals, residual_stride: int, checkpoint_interval: int, digests,
+                            seq: int = 0) -> None:
+        """Per-token commitments (qxc_verification_hashes): digests[p] = state
+        root of residual snapshot p (checkpoint positions, else zeros) || KV
+        slot leaf of layer p-1 (zeros at p = 0), p in 0..layers; device
+        tensors, the reference's encode_verification_hashes stage."""
+        a = _lib.VerificationHashArgs(seq, token, _ptr(residuals), residual_stride, checkpoint_interval,
+                                      _ptr(digests))
+        self.ctx.check(self.lib.qxc_verification_hashes(self.ctx.handle, self.handle, C.byref(a)))
+
+    def slot_hashes(self, digests, layer_begin: int, layer_count: int, token_begin: int, token_count: int,
+                    seq: int = 0, layout: int = 0) -> None:
+        """kv_leaf_hash_v1 of every (layer, token) slot of the range into the
+        device tensor digests [layer_count][token_count][32]
+        (qxc_kv_slot_hashes; layout: HASH_AUTO, HASH_PER_CHUNK or HASH_PER_SLOT)."""
+        self.ctx.check(self.lib.qxc_kv_slot_hashes(self.ctx.handle, self.handle, seq, layer_begin, layer_count,
+                                                   token_begin, token_count, _ptr(digests), layout))
 
     def decode_host(self, q: np.ndarray, k: np.ndarray, v: np.ndarray, positions, layer_begin: int = 0,
                     layer_count: int | None = None, seq_ids=None, q_dtype: int | None = None,

@@ -226,3 +226,96 @@ def test_attention_layer_oracle_composes_its_parts(oracle):
     o = W[3].mat_vec(att2)
     assert np.array_equal(out, (np.float32(0.22) * o.astype(np.float64) + h).astype(np.float32)) or \
         np.abs(out - (0.22 * o.astype(np.float64) + h)).max() <= 1e-6
+
+
+# ---- KV-slot commitments (qx-commit state.rs:213-251, :334-368) ----------------------
+def _blake3_ref():
+    import blake3  # the blake3 crate's official Python binding: the reference's own hash library
+    return lambda data: blake3.blake3(data).digest()
+
+
+def _hash_domain(b3, domain, fields):
+    """qx-commit hash.rs hash_domain for Blake3V1: domain, then u64 LE length + bytes per field."""
+    import struct
+    return b3(domain + b"".join(struct.pack("<Q", len(f)) + f for f in fields))
+
+
+def _tree_ref(b3, data, leaf_domain, tree_domain):
+    """qx-commit chunk_tree_hash (state.rs:213-251) over 256-byte chunks."""
+    import struct
+    leaves = [_hash_domain(b3, leaf_domain, [struct.pack("<I", i), data[i * 256:(i + 1) * 256]])
+              for i in range((len(data) + 255) // 256)]
+    cap = 1
+    while cap < len(leaves):
+        cap *= 2
+    leaves += [_hash_domain(b3, b"QX:MERKLE:EMPTY:V1", [tree_domain])] * (cap - len(leaves))
+    while len(leaves) > 1:
+        leaves = [b3(leaves[2 * i] + leaves[2 * i + 1]) for i in range(len(leaves) // 2)]
+    return leaves[0]
+
+
+def _kv_leaf_ref(b3, layer, token, key, value):
+    """qx-commit kv_leaf_hash_v1 (state.rs:334-368)."""
+    import struct
+    kr = _tree_ref(b3, key, b"QX:KV:KEY:CHUNK:V1", b"QX:KV:KEY:TREE:V1")
+    vr = _tree_ref(b3, value, b"QX:KV:VALUE:CHUNK:V1", b"QX:KV:VALUE:TREE:V1")
+    return _hash_domain(b3, b"QX:KV:V1", [struct.pack("<H", layer), struct.pack("<I", token), kr, vr])
+
+
+@pytest.mark.parametrize("n", [0, 1, 63, 64, 65, 127, 128, 129, 300, 1023, 1024])
+def test_blake3_restatement_matches_the_blake3_crate(oracle, n):
+    b3 = _blake3_ref()
+    data = bytes((i * 7 + 3) % 251 for i in range(n))
+    assert oracle.blake3_single_chunk(data) == b3(data)
+
+
+@pytest.mark.parametrize("key_len,value_len", [(2048, 2048), (1024, 1024), (1024, 2048), (300, 700), (256, 1)])
+def test_kv_leaf_hash_matches_qx_commit(oracle, key_len, value_len):
+    b3 = _blake3_ref()
+    rng = np.random.default_rng(key_len * 7 + value_len)
+    key = rng.integers(0, 256, key_len, dtype=np.uint8).tobytes()
+    value = rng.integers(0, 256, value_len, dtype=np.uint8).tobytes()
+    assert oracle.kv_leaf_hash(3, 4095, key, value) == _kv_leaf_ref(b3, 3, 4095, key, value)
+    # the coordinates are committed (qx-commit state.rs:375-387)
+    assert oracle.kv_leaf_hash(3, 4095, key, value) != oracle.kv_leaf_hash(4, 4095, key, value)
+    assert oracle.kv_leaf_hash(3, 4095, key, value) != oracle.kv_leaf_hash(3, 4094, key, value)
+
+
+@pytest.mark.parametrize("n", [256, 1024, 4096, 3000])
+def test_state_hash_matches_qx_commit(oracle, n):
+    b3 = _blake3_ref()
+    data = np.random.default_rng(n).integers(0, 256, n, dtype=np.uint8).tobytes()
+    assert oracle.state_hash(data) == _tree_ref(b3, data, b"QX:STATE:CHUNK:V1", b"QX:STATE:V1")
+
+
+def test_verification_hashes_reference_golden_case(oracle):
+    """The reference's verification_hash_matches_cpu_golden_oracle case
+    (qx-metal lib.rs:15531-15604): one layer, checkpoint interval 1, token 11;
+    snapshot 0 and 1 hold the same residual; the expected bytes are the CPU
+    state_hash_v1 / kv_leaf_hash_v1, restated here on the blake3 package."""
+    b3 = _blake3_ref()
+    residual = (np.arange(1024, dtype=np.float32) * np.float32(0.125) - np.float32(64.0)).tobytes()
+    key = (np.arange(512, dtype=np.float32) * np.float32(-0.25) + np.float32(3.0)).tobytes()
+    value = (np.arange(512, dtype=np.float32) / np.float32(17.0)).tobytes()
+    out = oracle.verification_hashes(residual + residual, len(residual), 1, 1, [key], [value], 11)
+    state = _tree_ref(b3, residual, b"QX:STATE:CHUNK:V1", b"QX:STATE:V1")
+    assert len(out) == 128
+    assert out[:32] == state and out[32:64] == bytes(32)
+    assert out[64:96] == state and out[96:128] == _kv_leaf_ref(b3, 0, 11, key, value)
+
+
+def test_verification_hashes_checkpoint_positions(oracle):
+    """Positions that are not checkpoints carry a zero state root
+    (verification_hash.metal:446-459)."""
+    rng = np.random.default_rng(5)
+    layers, stride = 6, 512
+    res = rng.integers(0, 256, (layers + 1) * stride, dtype=np.uint8).tobytes()
+    keys = [rng.integers(0, 256, 1024, dtype=np.uint8).tobytes() for _ in range(layers)]
+    vals = [rng.integers(0, 256, 1024, dtype=np.uint8).tobytes() for _ in range(layers)]
+    out = oracle.verification_hashes(res, stride, 4, layers, keys, vals, 7)
+    for p in range(layers + 1):
+        state = out[64 * p:64 * p + 32]
+        if p in (0, 4, 6):
+            assert state == oracle.state_hash(res[p * stride:(p + 1) * stride])
+        else:
+            assert state == bytes(32)
