@@ -878,14 +878,29 @@ def run_config4(args, world, rank, local):
     ctx = Context(local)
     stream = torch.cuda.Stream(device=dev)
     ctx.set_stream(stream)
-    arena = KvArena(ctx, MODEL_GRANITE, LAYERS, n, 4096, BF16, BF16)
+    page = args.paged
     g = torch.Generator(device=dev)
     g.manual_seed(0x51580401 + rank)
-    with torch.cuda.stream(stream):
+    if page:
+        # a paged arena sized to the batch: each sequence maps ceil(L / page)
+        # pages of the shared pool instead of a 4096-row cache per layer
+        pool = sum((lengths[i] + page - 1) // page for i in mine)
+        arena = KvArena(ctx, MODEL_GRANITE, LAYERS, n, 4096, BF16, BF16, page_size=page, pool_pages=pool)
+        with torch.cuda.stream(stream):
+            arena.pool_tensor(True).view(torch.bfloat16).normal_(generator=g)
+            arena.pool_tensor(False).view(torch.bfloat16).normal_(generator=g)
         for s, i in enumerate(mine):
-            for l in range(LAYERS):
-                arena.tensor(s, l, True)[:lengths[i] - 1].view(torch.bfloat16).normal_(generator=g)
-                arena.tensor(s, l, False)[:lengths[i] - 1].view(torch.bfloat16).normal_(generator=g)
+            arena.set_len(s, lengths[i])  # maps the pages
+        kv_bytes = 2 * LAYERS * pool * page * 8 * 64 * 2
+    else:
+        arena = KvArena(ctx, MODEL_GRANITE, LAYERS, n, 4096, BF16, BF16)
+        with torch.cuda.stream(stream):
+            for s, i in enumerate(mine):
+                for l in range(LAYERS):
+                    arena.tensor(s, l, True)[:lengths[i] - 1].view(torch.bfloat16).normal_(generator=g)
+                    arena.tensor(s, l, False)[:lengths[i] - 1].view(torch.bfloat16).normal_(generator=g)
+        kv_bytes = 2 * LAYERS * n * 4096 * 8 * 64 * 2
+    with torch.cuda.stream(stream):
         q = torch.randn(n, LAYERS, 1024, device=dev, generator=g)
         k = torch.randn(n, LAYERS, 512, device=dev, generator=g)
         v = torch.randn(n, LAYERS, 512, device=dev, generator=g)
@@ -915,6 +930,9 @@ def run_config4(args, world, rank, local):
                       "parallelism": f"sequences sharded x{world} by LPT on KV bytes, no collective"},
                      clk, launches)
     line["config"]["split"] = ctx.last_split
+    line["config"]["kv_arena_bytes_per_rank"] = int(kv_bytes)
+    if page:
+        line["config"]["workload"] += f"; paged arena, {page}-row pages, pool sized to the batch"
     line["roofline"] = hbm_roofline(my_bytes, per, "qx_decode_kernel<Granite,bf16,bf16>")
     arena.close()
     ctx.close()
@@ -995,6 +1013,7 @@ def main():
                     choices=["config0", "config1", "config2", "config3", "config4", "layer", "commit"])
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
+    ap.add_argument("--paged", type=int, default=0, help="config4: paged KV arena with this many rows per page")
     ap.add_argument("--prefill-len", type=int, default=2048, help="config2 prompt length (512 or 2048)")
     ap.add_argument("--qwen-context", type=int, default=32768, help="config3 KV length")
     ap.add_argument("--native-exp", action="store_true", help="hardware exp2 instead of qx's pinned exp_f32")

@@ -123,6 +123,40 @@ qxc_status qxc_kv_read(qxc_kv* kv, int32_t seq, int32_t layer, int32_t begin, in
 qxc_status qxc_kv_write(qxc_kv* kv, int32_t seq, int32_t layer, int32_t begin, int32_t count,
                         const void* host_keys, const void* host_values);
 
+/* ---- paged arenas -------------------------------------------------------- */
+/* A paged arena replaces the fixed [capacity] cache per (sequence, layer) for
+ * serving many sequences of uneven length (new; the reference plans one
+ * fixed-size cache per layer, qx-runtime-v2 lib.rs:6566-6636). Per layer, a
+ * pool of `pool_pages` pages of `page_size` rows ([page][kv_heads][head_dim]);
+ * each sequence has one block table, shared by its layers, mapping its logical
+ * pages to physical pages. Pages are mapped on demand, in order, by the calls
+ * that write rows (decode, verify, partials, qxc_kv_write) and by
+ * qxc_kv_set_len; a call the pool cannot serve fails with
+ * QXC_ERR_OUT_OF_MEMORY and maps nothing. qxc_kv_reset returns a sequence's
+ * pages to the pool; rollback / commit keep them for the sequence's regrowth;
+ * qxc_kv_trim returns the pages past its length. desc->capacity is the
+ * longest sequence. The decode, verify, partials and hash entry points read
+ * rows through the table with the same results as a contiguous arena;
+ * qxc_prefill and the contiguous views (qxc_kv_key_buffer / value_buffer)
+ * return QXC_ERR_UNSUPPORTED. */
+typedef struct qxc_kv_paging {
+  int32_t page_size;  /* rows per page: a power of two in 64..=4096 (a 64-row TMA box never straddles pages) */
+  int32_t pool_pages; /* physical pages per layer, shared by all sequences */
+} qxc_kv_paging;
+
+qxc_status qxc_kv_paged_bytes(const qxc_kv_desc* desc, const qxc_kv_paging* paging, size_t* key_bytes,
+                              size_t* value_bytes);
+qxc_status qxc_kv_create_paged(qxc_ctx* ctx, const qxc_kv_desc* desc, const qxc_kv_paging* paging, qxc_kv** out);
+/* Pages mapped by `seq` (seq < 0: by all sequences) and pages free in the pool. */
+qxc_status qxc_kv_page_stats(const qxc_kv* kv, int32_t seq, int32_t* mapped_pages, int32_t* free_pages);
+/* Return the pages of `seq` past its current length to the pool (no-op on a
+ * contiguous arena). */
+qxc_status qxc_kv_trim(qxc_kv* kv, int32_t seq);
+/* Device view of a paged arena's whole key (or value) page pool,
+ * [layers][pool_pages][page_size][kv_heads][head_dim], e.g. to initialise
+ * it; physical page p of layer l starts at row (l * pool_pages + p) * page_size. */
+qxc_status qxc_kv_pool_buffer(qxc_kv* kv, int32_t key, void** device_ptr, size_t* bytes);
+
 /* ---- decode ------------------------------------------------------------ */
 /* One token step for `seq_count` sequences over layers
  * [layer_begin, layer_begin + layer_count). Per (sequence, layer): RoPE on

@@ -69,6 +69,11 @@ class LayerArgs(C.Structure):
                 ("split", C.c_int32)]
 
 
+class KvPaging(C.Structure):
+    """qxc_kv_paging (paged arena: rows per page, physical pages per layer)."""
+    _fields_ = [("page_size", C.c_int32), ("pool_pages", C.c_int32)]
+
+
 class VerificationHashArgs(C.Structure):
     """qxc_verification_hash_args (per-token state roots and KV slot leaves)."""
     _fields_ = [("seq", C.c_int32), ("token", C.c_int32), ("residuals", C.c_void_p),
@@ -110,6 +115,12 @@ def load() -> C.CDLL:
         "qxc_last_split": (C.c_int32, [vp]),
         "qxc_kv_bytes": (C.c_int, [C.POINTER(KvDesc), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
         "qxc_kv_create": (C.c_int, [vp, C.POINTER(KvDesc), pp]),
+        "qxc_kv_create_paged": (C.c_int, [vp, C.POINTER(KvDesc), C.POINTER(KvPaging), pp]),
+        "qxc_kv_paged_bytes": (C.c_int, [C.POINTER(KvDesc), C.POINTER(KvPaging), C.POINTER(C.c_size_t),
+                                         C.POINTER(C.c_size_t)]),
+        "qxc_kv_page_stats": (C.c_int, [vp, i32, C.POINTER(i32), C.POINTER(i32)]),
+        "qxc_kv_trim": (C.c_int, [vp, i32]),
+        "qxc_kv_pool_buffer": (C.c_int, [vp, i32, pp, C.POINTER(C.c_size_t)]),
         "qxc_kv_destroy": (None, [vp]),
         "qxc_kv_len": (C.c_int, [vp, i32, C.POINTER(i32)]),
         "qxc_kv_reset": (C.c_int, [vp, i32]),

@@ -17,7 +17,8 @@ namespace qx {
 struct AppendParams {
   char* k_region;
   char* v_region;
-  long long k_unit_bytes, v_unit_bytes;  // bytes per (sequence, layer) cache
+  int capacity;      // rows per (sequence, layer) of a contiguous arena
+  KvPaging paging;   // or the page map of a paged one
   int layers, layer_begin, layer_count;
   int seq;     // sequence index in the arena
   int start;   // cache row of token 0
@@ -35,13 +36,13 @@ __global__ void __launch_bounds__(128) qx_append_rows_kernel(const __grid_consta
   constexpr int D = M::D, HKV = M::HKV;
   const int t = blockIdx.x / p.layer_count, l = blockIdx.x - t * p.layer_count;
   const int row = p.start + t;
-  const long long unit = (long long)p.seq * p.layers + p.layer_begin + l;
-  KT* kdst = reinterpret_cast<KT*>(p.k_region + unit * p.k_unit_bytes) + (long long)row * HKV * D;
-  VT* vdst = reinterpret_cast<VT*>(p.v_region + unit * p.v_unit_bytes) + (long long)row * HKV * D;
   const long long src = ((long long)t * p.layer_count + l) * HKV * D;
   const int tid = threadIdx.x;
   bool bad = false;
-  pdl_wait();
+  pdl_wait();  // the page table and the rows may come from the previous launch
+  const long long arow = kv_row(p.paging, p.capacity, p.layers, p.seq, p.layer_begin + l, row);
+  KT* kdst = reinterpret_cast<KT*>(p.k_region) + arow * HKV * D;
+  VT* vdst = reinterpret_cast<VT*>(p.v_region) + arow * HKV * D;
   if constexpr (!M::QWEN) {
     // rotate-half RoPE with qx's pinned sin/cos (granite_rope_pair,
     // qx-consensus-math lib.rs:199-207), as the decode kernel's new row

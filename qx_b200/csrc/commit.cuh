@@ -31,7 +31,7 @@
 #pragma once
 #include <stdint.h>
 
-#include "qx_ptx.cuh"
+#include "decode.cuh"
 
 namespace qx {
 
@@ -121,7 +121,8 @@ enum : int { kHashModeVerify = 0, kHashModeSlots = 1 };
 struct HashParams {
   const char* k_region;
   const char* v_region;
-  long long k_unit_bytes, v_unit_bytes;  // bytes per (sequence, layer) cache
+  int capacity;                          // rows per (sequence, layer) of a contiguous arena
+  KvPaging paging;                       // or the page map of a paged one
   int key_row_bytes, value_row_bytes;    // one token's row, all kv heads
   int layers;                            // layers of the arena
   int seq;
@@ -246,12 +247,11 @@ __global__ void __launch_bounds__(32 * kHashWarps) qx_kv_hash_kernel(const __gri
     partner = p.seg;
     row = nullptr;
   }
+  pdl_wait();  // the rows and the page table may come from the previous launch on the stream
   if (role != 0) {
-    const long long unit = (long long)p.seq * p.layers + layer;
-    row = role == 1 ? p.k_region + unit * p.k_unit_bytes + (long long)token * p.key_row_bytes
-                    : p.v_region + unit * p.v_unit_bytes + (long long)token * p.value_row_bytes;
+    const long long arow = kv_row(p.paging, p.capacity, p.layers, p.seq, layer, token);
+    row = role == 1 ? p.k_region + arow * p.key_row_bytes : p.v_region + arow * p.value_row_bytes;
   }
-  pdl_wait();  // the rows may come from the previous launch on the stream
   uint32_t* m = msg[warp][lane];
   uint32_t digest[8];
   const bool active = chunk < count;
@@ -312,14 +312,13 @@ __global__ void __launch_bounds__(32 * kHashSerialWarps) qx_kv_hash_serial_kerne
   const int token = valid ? p.token_begin + (int)(slot - (long long)lidx * p.token_count) : 0;
   uint32_t* m = hsm + (warp * 32 + lane) * kHashSerialLaneWords;
   uint32_t* node = m + kHashMsgWords;
-  const long long unit = (long long)p.seq * p.layers + layer;
   const int row_bytes = half ? p.value_row_bytes : p.key_row_bytes;
   const int n = valid ? row_bytes / 256 : 0;
-  const char* row = half ? p.v_region + unit * p.v_unit_bytes + (long long)token * row_bytes
-                         : p.k_region + unit * p.k_unit_bytes + (long long)token * row_bytes;
   const uint32_t* pfx = p.prefix[1 + half];
   const int plen = p.prefix_len[1 + half];
-  pdl_wait();
+  pdl_wait();  // the rows and the page table may come from the previous launch on the stream
+  const long long arow = valid ? kv_row(p.paging, p.capacity, p.layers, p.seq, layer, token) : 0;
+  const char* row = (half ? p.v_region : p.k_region) + arow * row_bytes;
   uint32_t d[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) d[j] = 0u;

@@ -56,18 +56,36 @@ struct SeqInfo {
   int pad[3];
 };
 
+// How a (sequence, layer, slot) finds its cache row in the arena's regions
+// (rows of [kv_heads][head_dim]). A contiguous arena keeps each (sequence,
+// layer) cache as `capacity` consecutive rows. A paged arena keeps, per
+// layer, a pool of pages of 2^shift rows; a sequence's block table (shared
+// by all layers, as in vLLM) maps its logical page to a physical page.
+struct KvPaging {
+  const int* table;  // device [sequences][stride] physical page per logical page; null: contiguous
+  int stride;        // logical pages per sequence
+  int shift;         // log2 of rows per page (>= 6: a 64-row TMA box never straddles pages)
+  int pool;          // physical pages per layer
+};
+
+__device__ __forceinline__ long long kv_row(const KvPaging& pg, int capacity, int layers, int seq, int layer,
+                                            int slot) {
+  if (!pg.table) return ((long long)seq * layers + layer) * capacity + slot;
+  const int page = __ldg(pg.table + (long long)seq * pg.stride + (slot >> pg.shift));
+  return (((long long)layer * pg.pool + page) << pg.shift) + (slot & ((1 << pg.shift) - 1));
+}
+
 struct DecodeParams {
   // 3-D tensor maps over the key / value regions of the arena:
   // dims {head_dim, kv_heads, sequences*layers*capacity}, box
   // {128 bytes of head_dim, 1, 64 positions}, 128-byte swizzle.
   CUtensorMap tmk;
   CUtensorMap tmv;
-  int capacity;  // rows per (sequence, layer) in the tensor maps
+  int capacity;  // rows per (sequence, layer) in the tensor maps (contiguous arenas)
+  KvPaging paging;
   // arena
   char* k_region;
   char* v_region;
-  long long k_unit_bytes;  // one (sequence, layer) key cache
-  long long v_unit_bytes;
   int layers;
   // call
   int layer_begin, layer_count, n_seq;
@@ -366,9 +384,6 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
   const int h = r / nsplit;
   const int s = r - h * nsplit;
   const int layer = p.layer_begin + lloc;
-  const long long unit = (long long)si.seq_id * p.layers + layer;
-  const char* kunit = p.k_region + unit * p.k_unit_bytes;
-  const char* vunit = p.v_region + unit * p.v_unit_bytes;
   const int begin = s * p.chunk;
   const int end = min(begin + p.chunk, si.attend);
   const bool has_new = si.new_slot >= begin && si.new_slot < end;  // last split only
@@ -382,9 +397,9 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
     if (lane == 0) {
       prefetch_tmap(&p.tmk);
       prefetch_tmap(&p.tmv);
-      const int z0 = (int)(unit * p.capacity) + begin;
       for (int tile = 0; tile < ntiles; ++tile) {
         const int st = tile % STAGES;
+        const int z = (int)kv_row(p.paging, p.capacity, p.layers, si.seq_id, layer, begin + tile * T);
         if (tile >= STAGES && !mbar_wait_bounded(&empty[st], (uint32_t)((tile / STAGES) - 1) & 1u, p.err)) {
           s_flag[1] = 1;
           break;
@@ -394,10 +409,10 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
         mbar_arrive_expect_tx(&full[st], (uint32_t)(C::STAGE_K + C::STAGE_V));
 #pragma unroll
         for (int b = 0; b < C::KB; ++b)
-          tma_load_3d(kt + b * C::BOX, &p.tmk, b * (128 / (int)sizeof(KT)), h, z0 + tile * T, &full[st]);
+          tma_load_3d(kt + b * C::BOX, &p.tmk, b * (128 / (int)sizeof(KT)), h, z, &full[st]);
 #pragma unroll
         for (int b = 0; b < C::VB; ++b)
-          tma_load_3d(vt + b * C::BOX, &p.tmv, b * (128 / (int)sizeof(VT)), h, z0 + tile * T, &full[st]);
+          tma_load_3d(vt + b * C::BOX, &p.tmv, b * (128 / (int)sizeof(VT)), h, z, &full[st]);
       }
     }
   } else {
@@ -487,8 +502,9 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
     consumers_sync(32 * NWC);
     if (has_new) {
       // Append: slot new_slot of this kv head.
-      char* kdst = const_cast<char*>(kunit) + ((long long)si.new_slot * HKV + h) * C::KROW;
-      char* vdst = const_cast<char*>(vunit) + ((long long)si.new_slot * HKV + h) * C::VROW;
+      const long long row = kv_row(p.paging, p.capacity, p.layers, si.seq_id, layer, si.new_slot);
+      char* kdst = p.k_region + (row * HKV + h) * C::KROW;
+      char* vdst = p.v_region + (row * HKV + h) * C::VROW;
       for (int i = tid; i < C::KROW / 16; i += 32 * NWC)
         reinterpret_cast<uint4*>(kdst)[i] = reinterpret_cast<const uint4*>(newk)[i];
       for (int i = tid; i < C::VROW / 16; i += 32 * NWC)

@@ -124,9 +124,6 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
   const int h = r / nsplit;
   const int s = r - h * nsplit;
   const int layer = p.layer_begin + lloc;
-  const long long unit = (long long)si.seq_id * p.layers + layer;
-  const char* kunit = p.k_region + unit * p.k_unit_bytes;
-  const char* vunit = p.v_region + unit * p.v_unit_bytes;
   const int begin = s * p.chunk;
   const int end = min(begin + p.chunk, si.attend);
   const bool has_new = si.new_slot >= begin && si.new_slot < end;
@@ -148,7 +145,6 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
       uint64_t* empty = lane == 0 ? kempty : vempty;
       unsigned char* ring = sm + (lane == 0 ? C::OFF_K : C::OFF_V);
       prefetch_tmap(map);
-      const int z0 = (int)(unit * p.capacity) + begin;
       // the prologue's few loads go first: behind the ring's ~200 KB per SM
       // they would wait for most of it
       ok &= mbar_wait_bounded(loaded, 0, p.err);
@@ -157,11 +153,12 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
         if (t >= NS) ok &= mbar_wait_bounded(&empty[st], (uint32_t)(t / NS - 1) & 1u, p.err);
         mbar_arrive_expect_tx(&full[st], (uint32_t)C::STAGE);
 #pragma unroll
-        for (int b = 0; b < 2; ++b)
+        for (int half = 0; half < 2; ++half) {
+          const int z = (int)kv_row(p.paging, p.capacity, p.layers, si.seq_id, layer, begin + t * T + half * 64);
 #pragma unroll
-          for (int half = 0; half < 2; ++half)
-            tma_load_3d(ring + st * C::STAGE + b * C::BLK + half * 8192, map, b * 64, h, z0 + t * T + half * 64,
-                        &full[st]);
+          for (int b = 0; b < 2; ++b)
+            tma_load_3d(ring + st * C::STAGE + b * C::BLK + half * 8192, map, b * 64, h, z, &full[st]);
+        }
       }
       // no copy may still be landing when the CTA exits
       for (int t = ntiles > NS ? ntiles - NS : 0; t < ntiles; ++t)
@@ -290,8 +287,9 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
     consumers_sync(128);
     if (tid == 0) mbar_arrive(qready);
     if (has_new) {
-      char* kdst = const_cast<char*>(kunit) + ((long long)si.new_slot * HKV + h) * (D * 2);
-      char* vdst = const_cast<char*>(vunit) + ((long long)si.new_slot * HKV + h) * (D * 2);
+      const long long row = kv_row(p.paging, p.capacity, p.layers, si.seq_id, layer, si.new_slot);
+      char* kdst = p.k_region + (row * HKV + h) * (D * 2);
+      char* vdst = p.v_region + (row * HKV + h) * (D * 2);
       if (tid < 16) reinterpret_cast<uint4*>(kdst)[tid] = reinterpret_cast<const uint4*>(newk)[tid];
       else if (tid < 32) reinterpret_cast<uint4*>(vdst)[tid - 16] = reinterpret_cast<const uint4*>(newv)[tid - 16];
     }

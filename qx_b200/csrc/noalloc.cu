@@ -179,8 +179,6 @@ extern "C" qxc_status qxc_granite_decode_static_scratch(const qxc_static_decode_
   p.capacity = a->capacity;
   p.k_region = static_cast<char*>(a->key_cache);
   p.v_region = static_cast<char*>(a->value_cache);
-  p.k_unit_bytes = (long long)a->capacity * 8 * 64 * (long long)esize(kd);
-  p.v_unit_bytes = (long long)a->capacity * 8 * 64 * (long long)esize(vd);
   p.layers = 1;
   p.layer_begin = 0;
   p.layer_count = 1;

@@ -28,6 +28,7 @@
 #include "layer.cuh"
 #include "prefill.cuh"
 #include "commit.cuh"
+#include "pages.cuh"
 
 using namespace qx;
 
@@ -80,7 +81,32 @@ struct qxc_kv {
   std::vector<int> len;
   float2* rope_table = nullptr;  // Qwen (cos, sin) per absolute position (owned by ctx)
   CUtensorMap tmk, tmv;          // tensor maps over the key / value regions
+  // paged arenas (page_shift > 0): per layer a pool of pool_pages pages of
+  // 2^page_shift rows; a sequence's logical pages [0, mapped[seq]) map to
+  // physical pages through table (host mirror of table_dev, -1 unmapped)
+  int page_shift = 0;
+  int pool_pages = 0;
+  int table_stride = 0;  // logical pages per sequence
+  int* table_dev = nullptr;
+  std::vector<int> table;
+  std::vector<int> mapped;
+  std::vector<int> free_pages;  // a stack: the next page to hand out is at the back
+  bool paged() const { return page_shift != 0; }
+  int pages_for(long long rows) const { return (int)((rows + (1ll << page_shift) - 1) >> page_shift); }
 };
+
+// The row map the kernels use for this arena (null table: contiguous).
+static KvPaging kv_paging(const qxc_kv* kv) {
+  KvPaging g;
+  memset(&g, 0, sizeof(g));
+  if (kv->paged()) {
+    g.table = kv->table_dev;
+    g.stride = kv->table_stride;
+    g.shift = kv->page_shift;
+    g.pool = kv->pool_pages;
+  }
+  return g;
+}
 
 namespace {
 
@@ -443,10 +469,9 @@ qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer
   p->tmk = kv->tmk;
   p->tmv = kv->tmv;
   p->capacity = kv->desc.capacity;
+  p->paging = kv_paging(kv);
   p->k_region = kv->k_region;
   p->v_region = kv->v_region;
-  p->k_unit_bytes = (long long)kv->k_unit;
-  p->v_unit_bytes = (long long)kv->v_unit;
   p->layers = kv->desc.layers;
   p->layer_begin = layer_begin;
   p->layer_count = layer_count;
@@ -634,6 +659,61 @@ qxc_status launch_append(qxc_ctx* ctx, const AppendParams& a, int grid) {
   return QXC_OK;
 }
 
+// ---- paged arenas ----------------------------------------------------------------
+// Send new block-table entries to the device in stream order.
+qxc_status push_table(qxc_ctx* ctx, qxc_kv* kv, const std::vector<int>& idx, const std::vector<int>& val) {
+  for (size_t at = 0; at < idx.size(); at += kPageUpdates) {
+    PageUpdates u;
+    u.table = kv->table_dev;
+    u.n = (int)std::min<size_t>(kPageUpdates, idx.size() - at);
+    for (int i = 0; i < u.n; ++i) {
+      u.index[i] = idx[at + i];
+      u.page[i] = val[at + i];
+    }
+    qx_page_table_kernel<<<1, 128, 0, ctx->stream>>>(u);
+    QXC_CUDA(ctx, cudaGetLastError());
+    ctx->launches++;
+  }
+  return QXC_OK;
+}
+
+// Map pages so that rows [0, rows[i]) of sequence seqs[i] exist, all or
+// nothing: when the pool cannot cover every request, nothing is mapped.
+qxc_status ensure_pages(qxc_ctx* ctx, qxc_kv* kv, int n, const int* seqs, const int* rows) {
+  if (!kv->paged()) return QXC_OK;
+  long long need = 0;
+  for (int i = 0; i < n; ++i) need += std::max(0, kv->pages_for(rows[i]) - kv->mapped[seqs[i]]);
+  if (need == 0) return QXC_OK;
+  if (need > (long long)kv->free_pages.size())
+    return fail(ctx, QXC_ERR_OUT_OF_MEMORY, "KV page pool exhausted: %lld more pages needed, %zu of %d free", need,
+                kv->free_pages.size(), kv->pool_pages);
+  std::vector<int> idx, val;
+  for (int i = 0; i < n; ++i) {
+    const int seq = seqs[i], want = kv->pages_for(rows[i]);
+    while (kv->mapped[seq] < want) {
+      const int page = kv->free_pages.back();
+      kv->free_pages.pop_back();
+      const int e = seq * kv->table_stride + kv->mapped[seq];
+      kv->table[e] = page;
+      idx.push_back(e);
+      val.push_back(page);
+      kv->mapped[seq]++;
+    }
+  }
+  return push_table(ctx, kv, idx, val);
+}
+
+// Return the pages of `seq` past its first `keep` logical pages to the pool.
+// Their device table entries stay as they were: nothing reads them until the
+// pages are mapped again, which sends fresh entries.
+void release_pages(qxc_kv* kv, int seq, int keep) {
+  while (kv->mapped[seq] > keep) {
+    const int e = seq * kv->table_stride + --kv->mapped[seq];
+    kv->free_pages.push_back(kv->table[e]);
+    kv->table[e] = -1;
+  }
+}
+
 // Hash kernel, a programmatic dependent like the decode (it waits for the
 // stream's previous kernel before reading rows).
 qxc_status launch_hash(qxc_ctx* ctx, const HashParams& p, int ctas, void (*fn)(HashParams) = qx_kv_hash_kernel,
@@ -667,8 +747,8 @@ qxc_status hash_params(qxc_ctx* ctx, const qxc_kv* kv, int seq, HashParams* p) {
   }
   p->k_region = kv->k_region;
   p->v_region = kv->v_region;
-  p->k_unit_bytes = (long long)kv->k_unit;
-  p->v_unit_bytes = (long long)kv->v_unit;
+  p->capacity = kv->desc.capacity;
+  p->paging = kv_paging(kv);
   p->key_row_bytes = (int)krow;
   p->value_row_bytes = (int)vrow;
   p->layers = kv->desc.layers;
@@ -799,11 +879,30 @@ qxc_status qxc_kv_bytes(const qxc_kv_desc* d, size_t* key_bytes, size_t* value_b
   return QXC_OK;
 }
 
-qxc_status qxc_kv_create(qxc_ctx* ctx, const qxc_kv_desc* desc, qxc_kv** out) {
+static qxc_status check_paging(qxc_ctx* ctx, const qxc_kv_desc* d, const qxc_kv_paging* pg) {
+  if (!pg) return fail(ctx, QXC_ERR_INVALID_ARG, "null paging descriptor");
+  if (pg->page_size < 64 || pg->page_size > 4096 || (pg->page_size & (pg->page_size - 1)) != 0)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "page size %d must be a power of two in 64..=4096", pg->page_size);
+  if (pg->pool_pages < 1) return fail(ctx, QXC_ERR_INVALID_ARG, "the page pool needs at least one page");
+  if (d->first_position != 0) return fail(ctx, QXC_ERR_UNSUPPORTED, "a paged arena cannot be a KV-length shard");
+  // TMA row coordinates are 32-bit
+  if ((long long)d->layers * pg->pool_pages * pg->page_size > 0x7fffffffLL)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "%d layers x %d pages x %d rows exceed 2^31 rows", d->layers,
+                pg->pool_pages, pg->page_size);
+  return QXC_OK;
+}
+
+// One allocation: keys [layers][pool][page][kv_heads][head_dim] (paged) or
+// [sequences][layers][capacity][kv_heads][head_dim] (contiguous), then values.
+static qxc_status kv_create(qxc_ctx* ctx, const qxc_kv_desc* desc, const qxc_kv_paging* paging, qxc_kv** out) {
   if (!ctx || !out) return QXC_ERR_INVALID_ARG;
   *out = nullptr;
   qxc_status st = check_desc(ctx, desc);
   if (st != QXC_OK) return st;
+  if (paging) {
+    st = check_paging(ctx, desc, paging);
+    if (st != QXC_OK) return st;
+  }
   QXC_CUDA(ctx, cudaSetDevice(ctx->device));
   qxc_kv* kv = new (std::nothrow) qxc_kv();
   if (!kv) return fail(ctx, QXC_ERR_OUT_OF_MEMORY, "host allocation failed");
@@ -814,10 +913,23 @@ qxc_status qxc_kv_create(qxc_ctx* ctx, const qxc_kv_desc* desc, qxc_kv** out) {
   kv->ves = dtype_size(desc->value_dtype);
   kv->k_unit = (size_t)desc->capacity * kv->hkv * kv->d * kv->kes;
   kv->v_unit = (size_t)desc->capacity * kv->hkv * kv->d * kv->ves;
-  const size_t units = (size_t)desc->layers * desc->sequences;
-  const size_t kbytes = kv->k_unit * units, vbytes = kv->v_unit * units;
+  size_t rows = (size_t)desc->layers * desc->sequences * desc->capacity;
+  if (paging) {
+    for (int s2 = 1; (1 << s2) <= paging->page_size; ++s2) kv->page_shift = s2;
+    kv->pool_pages = paging->pool_pages;
+    kv->table_stride = kv->pages_for(desc->capacity);
+    kv->table.assign((size_t)desc->sequences * kv->table_stride, -1);
+    kv->mapped.assign(desc->sequences, 0);
+    for (int pg = paging->pool_pages - 1; pg >= 0; --pg) kv->free_pages.push_back(pg);
+    rows = (size_t)desc->layers * paging->pool_pages * paging->page_size;
+  }
+  const size_t kbytes = rows * kv->hkv * kv->d * kv->kes, vbytes = rows * kv->hkv * kv->d * kv->ves;
   const size_t koff_v = ((kbytes + 255) / 256) * 256;
   cudaError_t e = cudaMalloc(&kv->base, koff_v + vbytes);
+  if (e == cudaSuccess && paging) {
+    e = cudaMalloc(&kv->table_dev, kv->table.size() * sizeof(int));
+    if (e != cudaSuccess) cudaFree(kv->base);
+  }
   if (e != cudaSuccess) {
     delete kv;
     return fail(ctx, e == cudaErrorMemoryAllocation ? QXC_ERR_OUT_OF_MEMORY : QXC_ERR_CUDA,
@@ -825,15 +937,16 @@ qxc_status qxc_kv_create(qxc_ctx* ctx, const qxc_kv_desc* desc, qxc_kv** out) {
   }
   // Zero-initialised like KvCache::new (qx-runtime lib.rs:359-368).
   cudaMemsetAsync(kv->base, 0, koff_v + vbytes, ctx->stream);
+  if (kv->table_dev) cudaMemsetAsync(kv->table_dev, 0xff, kv->table.size() * sizeof(int), ctx->stream);  // -1
   kv->k_region = kv->base;
   kv->v_region = kv->base + koff_v;
   kv->len.assign(desc->sequences, 0);
-  qxc_status mst = encode_kv_map(ctx, &kv->tmk, kv->k_region, desc->key_dtype, kv->hkv, kv->d, units * desc->capacity);
-  if (mst == QXC_OK)
-    mst = encode_kv_map(ctx, &kv->tmv, kv->v_region, desc->value_dtype, kv->hkv, kv->d, units * desc->capacity);
+  qxc_status mst = encode_kv_map(ctx, &kv->tmk, kv->k_region, desc->key_dtype, kv->hkv, kv->d, rows);
+  if (mst == QXC_OK) mst = encode_kv_map(ctx, &kv->tmv, kv->v_region, desc->value_dtype, kv->hkv, kv->d, rows);
   if (mst == QXC_OK && desc->model == QXC_MODEL_QWEN3) mst = ensure_qwen_rope(ctx);
   if (mst != QXC_OK) {
     cudaFree(kv->base);
+    if (kv->table_dev) cudaFree(kv->table_dev);
     delete kv;
     return mst;
   }
@@ -843,11 +956,60 @@ qxc_status qxc_kv_create(qxc_ctx* ctx, const qxc_kv_desc* desc, qxc_kv** out) {
   return QXC_OK;
 }
 
+qxc_status qxc_kv_create(qxc_ctx* ctx, const qxc_kv_desc* desc, qxc_kv** out) {
+  return kv_create(ctx, desc, nullptr, out);
+}
+
+qxc_status qxc_kv_create_paged(qxc_ctx* ctx, const qxc_kv_desc* desc, const qxc_kv_paging* paging, qxc_kv** out) {
+  if (!paging) return fail(ctx, QXC_ERR_INVALID_ARG, "null paging descriptor");
+  return kv_create(ctx, desc, paging, out);
+}
+
+qxc_status qxc_kv_paged_bytes(const qxc_kv_desc* d, const qxc_kv_paging* pg, size_t* key_bytes, size_t* value_bytes) {
+  qxc_status st = check_desc(nullptr, d);
+  if (st != QXC_OK) return st;
+  st = check_paging(nullptr, d, pg);
+  if (st != QXC_OK) return st;
+  int hq, hkv, hd;
+  model_shape(d->model, &hq, &hkv, &hd);
+  const size_t per = (size_t)d->layers * pg->pool_pages * pg->page_size * hkv * hd;
+  if (key_bytes) *key_bytes = per * dtype_size(d->key_dtype);
+  if (value_bytes) *value_bytes = per * dtype_size(d->value_dtype);
+  return QXC_OK;
+}
+
+qxc_status qxc_kv_page_stats(const qxc_kv* kv, int32_t seq, int32_t* mapped_pages, int32_t* free_pages) {
+  if (!kv) return QXC_ERR_INVALID_ARG;
+  if (!kv->paged()) return fail(kv->ctx, QXC_ERR_UNSUPPORTED, "the arena is not paged");
+  if (seq >= kv->desc.sequences) return fail(kv->ctx, QXC_ERR_INVALID_ARG, "sequence %d out of range", seq);
+  if (mapped_pages) *mapped_pages = seq < 0 ? kv->pool_pages - (int)kv->free_pages.size() : kv->mapped[seq];
+  if (free_pages) *free_pages = (int)kv->free_pages.size();
+  return QXC_OK;
+}
+
+qxc_status qxc_kv_pool_buffer(qxc_kv* kv, int32_t key, void** ptr, size_t* bytes) {
+  if (!kv || !ptr) return QXC_ERR_INVALID_ARG;
+  if (!kv->paged()) return fail(kv->ctx, QXC_ERR_UNSUPPORTED, "the arena is not paged");
+  const size_t rows = (size_t)kv->desc.layers * kv->pool_pages << kv->page_shift;
+  *ptr = key ? kv->k_region : kv->v_region;
+  if (bytes) *bytes = rows * kv->hkv * kv->d * (key ? kv->kes : kv->ves);
+  return QXC_OK;
+}
+
+qxc_status qxc_kv_trim(qxc_kv* kv, int32_t seq) {
+  if (!kv) return QXC_ERR_INVALID_ARG;
+  qxc_status st = check_seq(kv->ctx, kv, seq);
+  if (st != QXC_OK) return st;
+  if (kv->paged()) release_pages(kv, seq, kv->pages_for(kv->len[seq]));
+  return QXC_OK;
+}
+
 void qxc_kv_destroy(qxc_kv* kv) {
   if (!kv) return;
   cudaSetDevice(kv->ctx->device);
   cudaStreamSynchronize(kv->ctx->stream);
   cudaFree(kv->base);
+  if (kv->table_dev) cudaFree(kv->table_dev);
   delete kv;
 }
 
@@ -858,14 +1020,18 @@ qxc_status qxc_kv_len(const qxc_kv* kv, int32_t seq, int32_t* length) {
   return QXC_OK;
 }
 
+// A reset sequence's pages go back to the pool (paged arenas).
 qxc_status qxc_kv_reset(qxc_kv* kv, int32_t seq) {
   if (!kv) return QXC_ERR_INVALID_ARG;
   if (seq < 0) {
     std::fill(kv->len.begin(), kv->len.end(), 0);
+    if (kv->paged())
+      for (int i = 0; i < kv->desc.sequences; ++i) release_pages(kv, i, 0);
     return QXC_OK;
   }
   if (seq >= kv->desc.sequences) return fail(kv->ctx, QXC_ERR_INVALID_ARG, "sequence %d out of range", seq);
   kv->len[seq] = 0;
+  if (kv->paged()) release_pages(kv, seq, 0);
   return QXC_OK;
 }
 
@@ -875,6 +1041,8 @@ qxc_status qxc_kv_set_len(qxc_kv* kv, int32_t seq, int32_t length) {
   if (st != QXC_OK) return st;
   if (length < 0 || length > kv->desc.capacity)
     return fail(kv->ctx, QXC_ERR_POSITION, "KV length %d is outside capacity %d", length, kv->desc.capacity);
+  st = ensure_pages(kv->ctx, kv, 1, &seq, &length);
+  if (st != QXC_OK) return st;
   kv->len[seq] = length;
   return QXC_OK;
 }
@@ -916,6 +1084,8 @@ static qxc_status kv_view(qxc_kv* kv, int32_t seq, int32_t layer, bool key, void
   if (seq < 0 || seq >= kv->desc.sequences) return fail(kv->ctx, QXC_ERR_INVALID_ARG, "sequence %d out of range", seq);
   if (layer < 0 || layer >= kv->desc.layers)
     return fail(kv->ctx, QXC_ERR_INVALID_ARG, "KV layer %d is outside the plan", layer);
+  if (kv->paged())
+    return fail(kv->ctx, QXC_ERR_UNSUPPORTED, "a paged arena has no contiguous view of one cache");
   const size_t unit = (size_t)seq * kv->desc.layers + layer;
   *ptr = key ? kv->k_region + unit * kv->k_unit : kv->v_region + unit * kv->v_unit;
   if (bytes) *bytes = key ? kv->k_unit : kv->v_unit;
@@ -933,24 +1103,52 @@ static qxc_status kv_copy(qxc_kv* kv, int32_t seq, int32_t layer, int32_t begin,
                           void* hv, bool to_host) {
   if (!kv) return QXC_ERR_INVALID_ARG;
   qxc_ctx* ctx = kv->ctx;
-  void *kp, *vp;
-  qxc_status st = kv_view(kv, seq, layer, true, &kp, nullptr);
+  qxc_status st = check_seq(ctx, kv, seq);
   if (st != QXC_OK) return st;
-  kv_view(kv, seq, layer, false, &vp, nullptr);
+  if (layer < 0 || layer >= kv->desc.layers)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "KV layer %d is outside the plan", layer);
   if (begin < 0 || count < 0 || (long long)begin + count > kv->desc.capacity)
     return fail(ctx, QXC_ERR_INVALID_ARG, "slots [%d, %d) outside capacity %d", begin, begin + count, kv->desc.capacity);
-  const size_t row = (size_t)kv->hkv * kv->d;
   QXC_CUDA(ctx, cudaSetDevice(ctx->device));
-  QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-  char* kdev = static_cast<char*>(kp) + (size_t)begin * row * kv->kes;
-  char* vdev = static_cast<char*>(vp) + (size_t)begin * row * kv->ves;
-  if (hk) {
-    if (to_host) QXC_CUDA(ctx, cudaMemcpy(hk, kdev, (size_t)count * row * kv->kes, cudaMemcpyDeviceToHost));
-    else QXC_CUDA(ctx, cudaMemcpy(kdev, hk, (size_t)count * row * kv->kes, cudaMemcpyHostToDevice));
+  if (kv->paged()) {
+    const int end = begin + count;
+    if (to_host) {
+      if (kv->pages_for(end) > kv->mapped[seq])
+        return fail(ctx, QXC_ERR_INVALID_ARG, "slots [%d, %d) are not all mapped (%d pages of %d rows)", begin, end,
+                    kv->mapped[seq], 1 << kv->page_shift);
+    } else {
+      st = ensure_pages(ctx, kv, 1, &seq, &end);
+      if (st != QXC_OK) return st;
+    }
   }
-  if (hv) {
-    if (to_host) QXC_CUDA(ctx, cudaMemcpy(hv, vdev, (size_t)count * row * kv->ves, cudaMemcpyDeviceToHost));
-    else QXC_CUDA(ctx, cudaMemcpy(vdev, hv, (size_t)count * row * kv->ves, cudaMemcpyHostToDevice));
+  QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  const size_t krow = (size_t)kv->hkv * kv->d * kv->kes, vrow = (size_t)kv->hkv * kv->d * kv->ves;
+  const KvPaging pg = kv_paging(kv);
+  // runs of rows contiguous in the arena: the whole range, or one page at a time
+  for (int r = begin; r < begin + count;) {
+    int n = begin + count - r;
+    long long arow;
+    if (kv->paged()) {
+      const int page_rows = 1 << kv->page_shift;
+      n = std::min(n, page_rows - (r & (page_rows - 1)));
+      arow = ((long long)layer * pg.pool + kv->table[seq * pg.stride + (r >> pg.shift)]) * page_rows +
+             (r & (page_rows - 1));
+    } else {
+      arow = ((long long)seq * kv->desc.layers + layer) * kv->desc.capacity + r;
+    }
+    char* kdev = kv->k_region + arow * krow;
+    char* vdev = kv->v_region + arow * vrow;
+    char* kh = hk ? static_cast<char*>(hk) + (size_t)(r - begin) * krow : nullptr;
+    char* vh = hv ? static_cast<char*>(hv) + (size_t)(r - begin) * vrow : nullptr;
+    if (kh) {
+      if (to_host) QXC_CUDA(ctx, cudaMemcpy(kh, kdev, (size_t)n * krow, cudaMemcpyDeviceToHost));
+      else QXC_CUDA(ctx, cudaMemcpy(kdev, kh, (size_t)n * krow, cudaMemcpyHostToDevice));
+    }
+    if (vh) {
+      if (to_host) QXC_CUDA(ctx, cudaMemcpy(vh, vdev, (size_t)n * vrow, cudaMemcpyDeviceToHost));
+      else QXC_CUDA(ctx, cudaMemcpy(vdev, vh, (size_t)n * vrow, cudaMemcpyHostToDevice));
+    }
+    r += n;
   }
   return QXC_OK;
 }
@@ -997,6 +1195,12 @@ qxc_status qxc_decode(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* a) {
     rope[i] = position;
   }
   QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  {
+    std::vector<int> ids(a->seq_count);
+    for (int i = 0; i < a->seq_count; ++i) ids[i] = a->seq_ids ? a->seq_ids[i] : i;
+    qxc_status st = ensure_pages(ctx, kv, a->seq_count, ids.data(), attend.data());
+    if (st != QXC_OK) return st;
+  }
   CallPlan plan;
   qxc_status st = plan_call(ctx, kv, a->seq_count, a->seq_ids, attend.data(), new_slot.data(), rope.data(),
                             a->layer_count, a->split, &plan);
@@ -1136,13 +1340,18 @@ qxc_status qxc_decode_verify(qxc_ctx* ctx, qxc_kv* kv, const qxc_verify_args* a)
     return fail(ctx, QXC_ERR_POSITION, "KV position %d exceeds context %d", a->start + a->tokens - 1,
                 kv->desc.capacity);
   QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  {
+    const int rows = a->start + a->tokens;
+    st = ensure_pages(ctx, kv, 1, &a->seq, &rows);
+    if (st != QXC_OK) return st;
+  }
   // 1. the candidates' rows
   AppendParams ap;
   memset(&ap, 0, sizeof(ap));
   ap.k_region = kv->k_region;
   ap.v_region = kv->v_region;
-  ap.k_unit_bytes = (long long)kv->k_unit;
-  ap.v_unit_bytes = (long long)kv->v_unit;
+  ap.capacity = kv->desc.capacity;
+  ap.paging = kv_paging(kv);
   ap.layers = kv->desc.layers;
   ap.layer_begin = a->layer_begin;
   ap.layer_count = a->layer_count;
@@ -1311,6 +1520,8 @@ qxc_status qxc_decode_partials(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args*
   QXC_CUDA(ctx, cudaSetDevice(ctx->device));
   CallPlan plan;
   const int seq = a->seq, rope = a->position;
+  st = ensure_pages(ctx, kv, 1, &seq, &attend);
+  if (st != QXC_OK) return st;
   st = plan_call(ctx, kv, 1, &seq, &attend, &new_slot, &rope, 1, a->split, &plan);
   if (st != QXC_OK) return st;
   DecodeParams p;
@@ -1355,6 +1566,7 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
   if (!ctx || !kv || !a) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
   if (kv->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "KV arena belongs to another context");
   if (kv->desc.model != QXC_MODEL_GRANITE) return fail(ctx, QXC_ERR_UNSUPPORTED, "prefill supports Granite only");
+  if (kv->paged()) return fail(ctx, QXC_ERR_UNSUPPORTED, "prefill needs a contiguous arena");
   if (kv->desc.key_dtype != QXC_BF16 || kv->desc.value_dtype != QXC_BF16)
     return fail(ctx, QXC_ERR_UNSUPPORTED, "prefill requires a bf16 KV arena");
   if (a->in_dtype != QXC_BF16) return fail(ctx, QXC_ERR_UNSUPPORTED, "prefill inputs must be bf16");

@@ -148,12 +148,20 @@ class KvArena:
 
     def __init__(self, ctx: Context, model: int = MODEL_GRANITE, layers: int = 1, sequences: int = 1,
                  capacity: int = MAX_CONTEXT, key_dtype: int = F32, value_dtype: int | None = None,
-                 first_position: int = 0):
+                 first_position: int = 0, page_size: int = 0, pool_pages: int = 0):
+        """page_size > 0 makes a paged arena (qxc_kv_create_paged): per layer
+        `pool_pages` pages of `page_size` rows shared by all sequences,
+        mapped on demand; `capacity` is then the longest sequence."""
         self.ctx, self.lib = ctx, ctx.lib
         value_dtype = key_dtype if value_dtype is None else value_dtype
         self.desc = _lib.KvDesc(model, layers, sequences, capacity, key_dtype, value_dtype, first_position)
         h = C.c_void_p()
-        ctx.check(self.lib.qxc_kv_create(ctx.handle, C.byref(self.desc), C.byref(h)))
+        if page_size:
+            self.paging = _lib.KvPaging(page_size, pool_pages)
+            ctx.check(self.lib.qxc_kv_create_paged(ctx.handle, C.byref(self.desc), C.byref(self.paging), C.byref(h)))
+        else:
+            self.paging = None
+            ctx.check(self.lib.qxc_kv_create(ctx.handle, C.byref(self.desc), C.byref(h)))
         self.handle = h
         ctx._arenas.add(self)
         self.model, self.layers, self.sequences, self.capacity = model, layers, sequences, capacity
@@ -180,6 +188,30 @@ class KvArena:
 
     def reset(self, seq: int = -1) -> None:
         self.ctx.check(self.lib.qxc_kv_reset(self.handle, seq))
+
+    def page_stats(self, seq: int = -1) -> tuple[int, int]:
+        """(pages mapped by `seq`, or by all sequences when seq < 0; pages free)."""
+        m, f = C.c_int32(), C.c_int32()
+        self.ctx.check(self.lib.qxc_kv_page_stats(self.handle, seq, C.byref(m), C.byref(f)))
+        return m.value, f.value
+
+    def pool_tensor(self, key: bool = True):
+        """Zero-copy torch view [layers][pool_pages][page_size][kv_heads][head_dim]
+        of a paged arena's key (or value) pool (int16 for 16-bit storage)."""
+        import torch
+        p, n = C.c_void_p(), C.c_size_t()
+        self.ctx.check(self.lib.qxc_kv_pool_buffer(self.handle, 1 if key else 0, C.byref(p), C.byref(n)))
+        dt = self.key_dtype if key else self.value_dtype
+        shape = (self.layers, self.paging.pool_pages, self.paging.page_size, self.hkv, self.d)
+
+        class _View:
+            __cuda_array_interface__ = {"shape": shape, "typestr": "<f4" if dt == F32 else "<i2",
+                                        "data": (p.value, False), "version": 3, "strides": None}
+        return torch.as_tensor(_View(), device=f"cuda:{self.ctx.device}")
+
+    def trim(self, seq: int) -> None:
+        """Return the pages of `seq` past its length to the pool (qxc_kv_trim)."""
+        self.ctx.check(self.lib.qxc_kv_trim(self.handle, seq))
 
     def set_len(self, seq: int, length: int) -> None:
         self.ctx.check(self.lib.qxc_kv_set_len(self.handle, seq, length))
