@@ -558,7 +558,7 @@ def run_config3(args, world, rank, local):
     """Config 3: Qwen3 attention decode, bf16 KV, KV length 32768; N>1 splits the KV length."""
     import torch
     from qx_b200 import BF16, MODEL_QWEN3, Context, KvArena
-    from qx_b200.distributed import all_gather_partials, kv_ranges
+    from qx_b200.distributed import all_gather_partials, kv_ranges, open_peer_group
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     L = args.qwen_context
@@ -590,6 +590,10 @@ def run_config3(args, world, rank, local):
     stream.synchronize()
     for s in range(NSET):
         arena.set_len(s, cached)
+    # N>1: the partials cross NVLink through qxc_exchange_merge (peer stores
+    # into every rank's area + merge, one kernel), or with --exchange nccl
+    # through an NCCL all-gather and qxc_lse_merge
+    peers = open_peer_group(ctx) if world > 1 and args.exchange in ("peer", "kernel") else None
 
     def step(i):
         s = i % NSET
@@ -598,9 +602,15 @@ def run_config3(args, world, rank, local):
             arena.decode(q, k, v, out, [P], seq_ids=[s], split=args.split)
             return
         arena.set_len(s, cached)
+        if args.exchange == "peer":  # the exchange inside the split merge kernel
+            arena.decode_exchange(q, k, v, merged, P, append=owner, group=peers, seq=s, split=args.split)
+            return
         arena.decode_partials(q, k, v, parts, P, append=owner, seq=s, split=args.split)
-        allp = all_gather_partials(parts)
-        ctx.lse_merge(MODEL_QWEN3, world, allp, merged)
+        if peers is not None:
+            peers.exchange_merge(MODEL_QWEN3, parts, merged)
+        else:
+            allp = all_gather_partials(parts)
+            ctx.lse_merge(MODEL_QWEN3, world, allp, merged)
 
     K, W = args.steps, args.warmup
     # one step is tens of microseconds of GPU work, comparable to the host's
@@ -624,6 +634,9 @@ def run_config3(args, world, rank, local):
         total, per, clk, launches = timed_steps(replay, K, W, stream, world, dev, local, ctx)
     stream.synchronize()
     del graph  # a graph holding NCCL work must go before the process group
+    if peers is not None:
+        barrier(world)  # no rank closes its area while a peer may still store into it
+        peers.close()
     per = [x / R for x in per]  # per call
     launches = K * per_replay
     K *= R                          # total covers all K * R calls
@@ -634,7 +647,13 @@ def run_config3(args, world, rank, local):
                      {"workload": "config3: Qwen3 layer decode, 32 q / 4 kv heads, d=128, bf16 KV, length 32768",
                       "l2": f"calls rotate over {NSET} cache copies ({NSET * per_rank_bytes / 2**20:.0f} MB > 126 MB L2)",
                       "parallelism": "single GPU" if world == 1 else
-                      f"KV length split x{world}, NCCL all-gather of (m,l,O) partials + LSE merge",
+                      {"peer": f"KV length split x{world}; the split merge kernel pushes each rank's (m,l,O) "
+                               "partials to every rank with tagged NVLink peer stores and merges them "
+                               "(qxc_decode_exchange)",
+                       "kernel": f"KV length split x{world}; (m,l,O) partials exchanged with NVLink peer stores "
+                                 "and merged by a separate kernel (qxc_exchange_merge)",
+                       "nccl": f"KV length split x{world}, NCCL all-gather of (m,l,O) partials + LSE merge"}
+                      [args.exchange],
                       "timing": f"{R} steps per CUDA graph replay"},
                      clk, launches)
     line["config"]["split"] = ctx.last_split
@@ -1014,6 +1033,9 @@ def main():
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--paged", type=int, default=0, help="config4: paged KV arena with this many rows per page")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "kernel", "nccl"],
+                    help="config3 N>1: partials exchanged inside the split merge kernel (peer), by a separate "
+                         "exchange kernel (kernel), or by an NCCL all-gather (nccl)")
     ap.add_argument("--prefill-len", type=int, default=2048, help="config2 prompt length (512 or 2048)")
     ap.add_argument("--qwen-context", type=int, default=32768, help="config3 KV length")
     ap.add_argument("--native-exp", action="store_true", help="hardware exp2 instead of qx's pinned exp_f32")

@@ -364,6 +364,44 @@ typedef struct qxc_partial_args {
   int32_t split;
 } qxc_partial_args;
 qxc_status qxc_decode_partials(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args* args);
+/* Exchange + merge over NVLink in one kernel, replacing the all-gather of the
+ * partials and qxc_lse_merge when every rank's GPU can address every other's
+ * memory (one node). A peer group is each rank's exchange area (about 540 KB
+ * at 8 ranks); every rank creates one, exports its handle, and attaches every
+ * other rank's, then each step calls qxc_exchange_merge with this rank's
+ * partials from qxc_decode_partials. The kernel stores the partials into every
+ * rank's area with peer stores, each value paired with the step's tag in one
+ * 8-byte store (no memory fence), waits until every rank's values of its query
+ * head carry the tag (bounded: QXC_ERR_TIMEOUT at qxc_sync, after which the
+ * groups must be re-created on every rank) and merges in rank order: the
+ * output equals qxc_lse_merge over the gathered partials, bit for bit, on
+ * every rank. Every rank must issue the same sequence of exchange calls. */
+#define QXC_PEER_HANDLE_BYTES 64
+typedef struct qxc_peer_group qxc_peer_group;
+qxc_status qxc_peer_group_create(qxc_ctx* ctx, int32_t rank, int32_t world, qxc_peer_group** out);
+void qxc_peer_group_destroy(qxc_peer_group* group);
+/* The CUDA IPC handle of this rank's area (QXC_PEER_HANDLE_BYTES bytes), for
+ * the other processes' qxc_peer_group_open. */
+qxc_status qxc_peer_group_handle(const qxc_peer_group* group, void* handle);
+qxc_status qxc_peer_group_open(qxc_peer_group* group, int32_t peer, const void* handle);
+/* One process driving several GPUs: attach another group's area directly
+ * (qxc_peer_group_base of that group); enables peer access when needed. */
+qxc_status qxc_peer_group_base(const qxc_peer_group* group, void** base);
+qxc_status qxc_peer_group_set_peer(qxc_peer_group* group, int32_t peer, void* base);
+qxc_status qxc_exchange_merge(qxc_ctx* ctx, qxc_peer_group* group, int32_t model, const float* partials, void* out,
+                              int32_t out_dtype);
+/* qxc_decode_partials and qxc_exchange_merge in one pass, with the exchange
+ * fused into the split merge: the kernel that combines this rank's KV splits
+ * stores the combined partial of each (query head, 32 dims) into every rank's
+ * area and merges all ranks' into out [q_heads][head_dim] (out_dtype), so no
+ * separate exchange launch runs. args->partials is not used. Same output as
+ * qxc_decode_partials + qxc_exchange_merge, bit for bit, when the range has
+ * one split or more than 8 (with 2 to 8, qxc_decode_partials combines them
+ * inside the decode kernel, in another order: equal within fp32 rounding).
+ * Every rank must call it for the same steps, and not mix it with
+ * qxc_exchange_merge on one group. */
+qxc_status qxc_decode_exchange(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args* args, qxc_peer_group* group,
+                               void* out, int32_t out_dtype);
 /* Log-sum-exp merge of n_parts partial sets [n_parts][q_heads][head_dim+2]
  * (device) into out [q_heads][head_dim] (device, out_dtype):
  * M = max m_i, O = sum e^(m_i-M) O_i / sum e^(m_i-M) l_i. */

@@ -19,6 +19,7 @@ MODEL_GRANITE, MODEL_QWEN3 = 0, 1
 F32, BF16, F16 = 0, 1, 2
 DECODE_NO_ADVANCE, DECODE_NATIVE_EXP, DECODE_PINNED_EXP = 0x1, 0x2, 0x4
 HASH_AUTO, HASH_PER_CHUNK, HASH_PER_SLOT = 0, 1, 2
+PEER_HANDLE_BYTES = 64
 
 
 class KvDesc(C.Structure):
@@ -142,6 +143,14 @@ def load() -> C.CDLL:
         "qxc_q4_mat_vec": (C.c_int, [vp, C.POINTER(Q4Matrix), vp, vp, vp]),
         "qxc_attention_layer": (C.c_int, [vp, vp, C.POINTER(LayerArgs)]),
         "qxc_lse_merge": (C.c_int, [vp, i32, i32, vp, vp, i32]),
+        "qxc_peer_group_create": (C.c_int, [vp, i32, i32, pp]),
+        "qxc_peer_group_destroy": (None, [vp]),
+        "qxc_peer_group_handle": (C.c_int, [vp, vp]),
+        "qxc_peer_group_base": (C.c_int, [vp, pp]),
+        "qxc_peer_group_open": (C.c_int, [vp, i32, vp]),
+        "qxc_peer_group_set_peer": (C.c_int, [vp, i32, vp]),
+        "qxc_exchange_merge": (C.c_int, [vp, vp, i32, vp, vp, i32]),
+        "qxc_decode_exchange": (C.c_int, [vp, vp, C.POINTER(PartialArgs), vp, vp, i32]),
         "qxc_verification_hashes": (C.c_int, [vp, vp, C.POINTER(VerificationHashArgs)]),
         "qxc_kv_slot_hashes": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp, i32]),
         "qxc_blake3_compress_rate": (C.c_int, [vp, C.POINTER(C.c_double)]),

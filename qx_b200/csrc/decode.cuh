@@ -109,6 +109,15 @@ struct DecodeParams {
   int* tickets;       // scratch [n_seq][layer_count][HKV], zero between calls
   unsigned* err;
   unsigned long long* trace;  // stage timeline (diagnostics), or null
+  // KV-length split across GPUs, merged by qx_split_merge_kernel itself
+  // (xworld > 0): every rank's inbox of [2][xworld][HQ * D/32][34] tagged
+  // values (32 dims of O, m, l per query head and 32-dim slice) and this
+  // rank's step counter per (query head, slice); see exchange.cuh
+  uint2* xinbox[8];
+  unsigned* xstep;
+  int xrank, xworld;
+  void* xout;  // final output [HQ][D]
+  int xout_dtype;
 };
 
 template <class M, typename KT, typename VT>
@@ -228,7 +237,9 @@ __device__ __forceinline__ void finish_outputs(const DecodeParams& p, const floa
                                                int nsplit, int s, long long cu, int h, int tid, int warp, int lane,
                                                bool pinned, float* merge_smem, float* stat_smem, int* s_flag) {
   const long long obase = (cu * HQ + (long long)h * G) * D;
-  if (nsplit == 1) {
+  // (with an exchange across GPUs even one split goes to qx_split_merge_kernel,
+  // which pushes it to the peers)
+  if (nsplit == 1 && !p.xworld) {
     bool nonfinite = false;
 #pragma unroll
     for (int k = 0; k < OPT; ++k) {
@@ -736,7 +747,7 @@ __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_consta
   const int slot = (int)(cu / p.layer_count), lloc = (int)(cu % p.layer_count);
   const SeqInfo si = p.seq_table ? p.seq_table[slot] : p.single;
   const int n = (si.attend + p.chunk - 1) / p.chunk;
-  if (n <= 1) return;  // the decode kernel wrote this head's output itself
+  if (n <= 1 && !p.xworld) return;  // the decode kernel wrote this head's output itself
   const long long item0 = si.item_begin + (long long)(lloc * HKV + h) * n;
   const float* first = p.partials + item0 * G * (D + 2) + (long long)g * (D + 2);
   const long long stride = (long long)G * (D + 2);
@@ -773,6 +784,72 @@ __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_consta
     L = fmaf(L, a, Ls);
     o = fmaf(o, a, os);
     M = Mn;
+  }
+  if (p.xworld) {
+    // KV-length split across GPUs: this CTA's slice of this rank's partial
+    // (32 dims of O, and m, l) goes tagged into every rank's inbox; then
+    // the slices of all ranks are merged in rank order (qx_lse_merge's
+    // arithmetic) straight into the output. The grid is one wave, so the
+    // peers' matching CTAs are running too.
+    constexpr int S = D / 32, ROW = 34;
+    const int slice = blk % S, dl = tid >> 2;
+    const long long qh = (long long)h * G + g;
+    const int W = p.xworld;
+    unsigned* stp = p.xstep + qh * S + slice;
+    const unsigned st = *stp, tag = st + 1u, half = st & 1u;
+    const long long rows = (long long)HQ * S;
+    const long long mine = ((long long)half * W + p.xrank) * rows + qh * S + slice;
+    if (q == 0)
+      for (int r = 0; r < W; ++r) st_tagged(p.xinbox[r] + mine * ROW + dl, o, tag);
+    if (tid == 0)
+      for (int r = 0; r < W; ++r) {
+        st_tagged(p.xinbox[r] + mine * ROW + 32, M, tag);
+        st_tagged(p.xinbox[r] + mine * ROW + 33, L, tag);
+      }
+    __shared__ float xml[16];  // m_r, l_r of up to 8 ranks
+    __shared__ int xok;
+    if (tid == 0) xok = 1;
+    __syncthreads();
+    const uint2* in = p.xinbox[p.xrank] + ((long long)half * W * rows + qh * S + slice) * ROW;
+    bool ok = true;
+    float ov[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) ov[r] = 0.0f;
+    if (tid < 32) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r < W && ok) ok = wait_tagged(in + r * rows * ROW + tid, tag, &ov[r]);
+    }
+    if (tid < 2 * W) {
+      float v = 0.0f;
+      if (ok) ok = wait_tagged(in + (tid >> 1) * rows * ROW + 32 + (tid & 1), tag, &v);
+      xml[tid] = v;
+    }
+    if (!ok) {
+      flag_error(p.err, QX_ERR_BIT_TIMEOUT);
+      xok = 0;
+    }
+    __syncthreads();
+    if (!xok) return;
+    if (tid < 32) {
+      float mx = -INFINITY;
+      for (int r = 0; r < W; ++r) mx = fmaxf(mx, xml[2 * r]);
+      float Lt = 0.0f, Ot = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r >= W) break;
+        const float m = xml[2 * r];
+        if (m == -INFINITY) continue;  // empty shard
+        const float w = softmax_exp(m - mx, pinned);
+        Lt = fmaf(w, xml[2 * r + 1], Lt);
+        Ot = fmaf(w, ov[r], Ot);
+      }
+      const float v = Ot / Lt;
+      if (!isfinite(v)) flag_error(p.err, QX_ERR_BIT_NONFINITE);
+      store_any(p.xout, (cu * HQ + qh) * D + slice * 32 + tid, p.xout_dtype, v);
+    }
+    if (tid == 0) *stp = st + 1u;
+    return;
   }
   if (q == 0) {
     const long long qh = (long long)h * G + g;

@@ -32,6 +32,32 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
+// Tagged values for exchanges between GPUs without a memory fence: a 32-bit
+// value and a 32-bit tag travel in one 8-byte store, which a reader sees
+// whole or not at all, so a reader that polls until the tag is the one it
+// expects has the value that came with it.
+__device__ __forceinline__ void st_tagged(uint2* p, float v, unsigned tag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag) : "memory");
+}
+__device__ __forceinline__ uint2 ld_tagged(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
+// Poll one tagged value until it carries `tag`; false after kMaxWaitNs.
+__device__ __forceinline__ bool wait_tagged(const uint2* p, unsigned tag, float* v) {
+  uint2 x = ld_tagged(p);
+  if (x.y != tag) {
+    const unsigned long long t0 = global_ns();
+    while ((x = ld_tagged(p)).y != tag) {
+      if (global_ns() - t0 > kMaxWaitNs) return false;
+    }
+  }
+  *v = __uint_as_float(x.x);
+  return true;
+}
+
 // Stage timeline for diagnostics (host switch QXC_TRACE): one writer thread
 // per CTA stores %globaltimer at stage boundaries into kTraceSlots slots of a
 // per-launch buffer; a null buffer makes every mark a no-op.

@@ -29,6 +29,7 @@
 #include "prefill.cuh"
 #include "commit.cuh"
 #include "pages.cuh"
+#include "exchange.cuh"
 
 using namespace qx;
 
@@ -68,6 +69,22 @@ struct qxc_ctx {
 };
 
 constexpr int kQwenMaxPositions = 40960;  // max_position_embeddings, qx-model lib.rs:308
+
+static constexpr int kExchHeads = 32, kExchRow = 130;
+
+// One rank's exchange area and the views of every rank's (see exchange.cuh),
+// sized for the largest model (Qwen3: 32 query heads, head_dim 128):
+//   inbox  [2][world][32][130] {value, tag}     qx_exchange_merge_kernel
+//   xinbox [2][world][32 * 4][34] {value, tag}  qx_split_merge_kernel's exchange
+//   steps  [32] u32, then [32][4] u32           one counter per writer
+struct qxc_peer_group {
+  qxc_ctx* ctx = nullptr;
+  int rank = 0, world = 1;
+  char* base = nullptr;
+  size_t bytes = 0, off_xinbox = 0, off_step = 0;
+  char* peer[kMaxPeers] = {};    // every rank's base as seen from this device
+  bool opened[kMaxPeers] = {};   // opened through CUDA IPC (closed on destroy)
+};
 
 struct qxc_kv {
   qxc_ctx* ctx = nullptr;
@@ -1485,13 +1502,19 @@ qxc_status qxc_apply_granite_rope(qxc_ctx* ctx, float* q, float* k, int32_t posi
 }
 
 // ---- KV-length split ---------------------------------------------------------
-qxc_status qxc_decode_partials(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args* a) {
+// qxc_decode_partials, and with a peer group the fused exchange: every
+// split partial, even a lone one, goes through the split merge kernel, which
+// pushes this rank's merged partials to every rank and merges all ranks'
+// into xout. So the path does not depend on a rank's split count, and every
+// rank takes it.
+static qxc_status decode_partials_impl(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args* a, qxc_peer_group* g,
+                                       void* xout, int xout_dtype) {
   if (!ctx || !kv || !a) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
   if (kv->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "KV arena belongs to another context");
   qxc_status st = check_seq(ctx, kv, a->seq);
   if (st != QXC_OK) return st;
   if (a->layer < 0 || a->layer >= kv->desc.layers) return fail(ctx, QXC_ERR_INVALID_ARG, "layer %d out of range", a->layer);
-  if (!a->q || !a->partials || (a->append && (!a->k || !a->v)))
+  if (!a->q || (!a->partials && !g) || (a->append && (!a->k || !a->v)))
     return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
   if (kv->desc.model == QXC_MODEL_QWEN3 && (a->q_dtype != kv->desc.key_dtype || (a->append && a->in_dtype != kv->desc.key_dtype)))
     return fail(ctx, QXC_ERR_INVALID_ARG, "Qwen q/k/v must use the KV cache's 16-bit type");
@@ -1538,10 +1561,23 @@ qxc_status qxc_decode_partials(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args*
   p.out_dtype = QXC_F32;
   p.pinned_exp = default_pinned(kv, a->flags) ? 1 : 0;
   p.emit_partials = 1;
+  if (g) {
+    p.external_merge = 1;
+    for (int r = 0; r < g->world; ++r) p.xinbox[r] = reinterpret_cast<uint2*>(g->peer[r] + g->off_xinbox);
+    p.xstep = reinterpret_cast<unsigned*>(g->base + g->off_step) + kExchHeads;
+    p.xrank = g->rank;
+    p.xworld = g->world;
+    p.xout = xout;
+    p.xout_dtype = xout_dtype;
+  }
   st = launch_decode(ctx, kv, p, plan.items);
   if (st != QXC_OK) return st;
   if (a->append) kv->len[a->seq] += 1;
   return QXC_OK;
+}
+
+qxc_status qxc_decode_partials(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args* a) {
+  return decode_partials_impl(ctx, kv, a, nullptr, nullptr, 0);
 }
 
 qxc_status qxc_lse_merge(qxc_ctx* ctx, int32_t model, int32_t n_parts, const float* partials, void* out,
@@ -1559,6 +1595,158 @@ qxc_status qxc_lse_merge(qxc_ctx* ctx, int32_t model, int32_t n_parts, const flo
   QXC_CUDA(ctx, cudaGetLastError());
   ctx->launches++;
   return QXC_OK;
+}
+
+// ---- exchange over NVLink (KV-length split across GPUs) --------------------------
+
+qxc_status qxc_peer_group_create(qxc_ctx* ctx, int32_t rank, int32_t world, qxc_peer_group** out) {
+  if (!ctx || !out) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "rank %d of world %d (at most %d ranks)", rank, world, kMaxPeers);
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  qxc_peer_group* g = new (std::nothrow) qxc_peer_group();
+  if (!g) return fail(ctx, QXC_ERR_OUT_OF_MEMORY, "host allocation failed");
+  g->ctx = ctx;
+  g->rank = rank;
+  g->world = world;
+  const size_t inbox = (size_t)2 * world * kExchHeads * kExchRow * sizeof(uint2);
+  const size_t xinbox = (size_t)2 * world * kExchHeads * 4 * 34 * sizeof(uint2);
+  g->off_xinbox = (inbox + 255) / 256 * 256;
+  g->off_step = g->off_xinbox + (xinbox + 255) / 256 * 256;
+  g->bytes = g->off_step + 1024;  // [32] exchange-kernel steps, then [32][4] split-merge steps
+  cudaError_t e = cudaMalloc(&g->base, g->bytes);
+  if (e != cudaSuccess) {
+    delete g;
+    return fail(ctx, QXC_ERR_OUT_OF_MEMORY, "exchange area of %zu bytes: %s", g->bytes, cudaGetErrorString(e));
+  }
+  e = cudaMemset(g->base, 0, g->bytes);
+  if (e != cudaSuccess) {
+    cudaFree(g->base);
+    delete g;
+    return fail(ctx, QXC_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(e));
+  }
+  g->peer[rank] = g->base;
+  *out = g;
+  return QXC_OK;
+}
+
+void qxc_peer_group_destroy(qxc_peer_group* g) {
+  if (!g) return;
+  cudaSetDevice(g->ctx->device);
+  cudaStreamSynchronize(g->ctx->stream);
+  for (int r = 0; r < g->world; ++r)
+    if (g->opened[r]) cudaIpcCloseMemHandle(g->peer[r]);
+  cudaFree(g->base);
+  delete g;
+}
+
+qxc_status qxc_peer_group_handle(const qxc_peer_group* g, void* handle) {
+  if (!g || !handle) return QXC_ERR_INVALID_ARG;
+  qxc_ctx* ctx = g->ctx;
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  cudaIpcMemHandle_t h;
+  QXC_CUDA(ctx, cudaIpcGetMemHandle(&h, g->base));
+  static_assert(sizeof(cudaIpcMemHandle_t) == QXC_PEER_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return QXC_OK;
+}
+
+qxc_status qxc_peer_group_base(const qxc_peer_group* g, void** base) {
+  if (!g || !base) return QXC_ERR_INVALID_ARG;
+  *base = g->base;
+  return QXC_OK;
+}
+
+qxc_status qxc_peer_group_open(qxc_peer_group* g, int32_t peer, const void* handle) {
+  if (!g || !handle) return QXC_ERR_INVALID_ARG;
+  qxc_ctx* ctx = g->ctx;
+  if (peer < 0 || peer >= g->world || peer == g->rank)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "peer %d is not another rank of world %d", peer, g->world);
+  if (g->peer[peer]) return fail(ctx, QXC_ERR_INVALID_ARG, "peer %d is already attached", peer);
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  QXC_CUDA(ctx, cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  g->peer[peer] = static_cast<char*>(p);
+  g->opened[peer] = true;
+  return QXC_OK;
+}
+
+qxc_status qxc_peer_group_set_peer(qxc_peer_group* g, int32_t peer, void* base) {
+  if (!g || !base) return QXC_ERR_INVALID_ARG;
+  qxc_ctx* ctx = g->ctx;
+  if (peer < 0 || peer >= g->world || peer == g->rank)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "peer %d is not another rank of world %d", peer, g->world);
+  if (g->peer[peer]) return fail(ctx, QXC_ERR_INVALID_ARG, "peer %d is already attached", peer);
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  cudaPointerAttributes attr;
+  QXC_CUDA(ctx, cudaPointerGetAttributes(&attr, base));
+  if (attr.type != cudaMemoryTypeDevice) return fail(ctx, QXC_ERR_INVALID_ARG, "peer base is not device memory");
+  if (attr.device != ctx->device) {
+    int ok = 0;
+    QXC_CUDA(ctx, cudaDeviceCanAccessPeer(&ok, ctx->device, attr.device));
+    if (!ok) return fail(ctx, QXC_ERR_UNSUPPORTED, "device %d cannot access device %d", ctx->device, attr.device);
+    cudaError_t e = cudaDeviceEnablePeerAccess(attr.device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+    else if (e != cudaSuccess) return fail(ctx, QXC_ERR_CUDA, "cudaDeviceEnablePeerAccess: %s", cudaGetErrorString(e));
+  }
+  g->peer[peer] = static_cast<char*>(base);
+  return QXC_OK;
+}
+
+qxc_status qxc_exchange_merge(qxc_ctx* ctx, qxc_peer_group* g, int32_t model, const float* partials, void* out,
+                              int32_t out_dtype) {
+  if (!ctx || !g || !partials || !out) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (g->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "peer group belongs to another context");
+  if (!valid_dtype(out_dtype)) return fail(ctx, QXC_ERR_INVALID_ARG, "unknown dtype");
+  if (model != QXC_MODEL_QWEN3 && model != QXC_MODEL_GRANITE)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "unknown model %d", model);
+  ExchangeParams p;
+  memset(&p, 0, sizeof(p));
+  for (int r = 0; r < g->world; ++r) {
+    if (!g->peer[r]) return fail(ctx, QXC_ERR_INVALID_ARG, "peer %d is not attached", r);
+    p.inbox[r] = reinterpret_cast<uint2*>(g->peer[r]);
+  }
+  p.step = reinterpret_cast<unsigned*>(g->base + g->off_step);
+  p.rank = g->rank;
+  p.world = g->world;
+  p.hq = model == QXC_MODEL_QWEN3 ? 32 : 16;
+  p.d = model == QXC_MODEL_QWEN3 ? 128 : 64;
+  p.partials = partials;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.pinned = model == QXC_MODEL_GRANITE ? 1 : 0;
+  p.err = ctx->err_dev;
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  TraceRun tr(ctx, "exchange", (size_t)p.hq);
+  p.trace = tr.buf;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(p.hq);
+  cfg.blockDim = dim3(kExchThreads);
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QXC_CUDA(ctx, cudaLaunchKernelEx(&cfg, qx_exchange_merge_kernel, p));
+  ctx->launches++;
+  return QXC_OK;
+}
+
+qxc_status qxc_decode_exchange(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args* a, qxc_peer_group* g, void* out,
+                               int32_t out_dtype) {
+  if (!ctx || !kv || !a || !g || !out) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (g->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "peer group belongs to another context");
+  if (!valid_dtype(out_dtype)) return fail(ctx, QXC_ERR_INVALID_ARG, "unknown dtype");
+  for (int r = 0; r < g->world; ++r)
+    if (!g->peer[r]) return fail(ctx, QXC_ERR_INVALID_ARG, "peer %d is not attached", r);
+  if ((kv->desc.model == QXC_MODEL_QWEN3 ? 32 : 16) * (kv->d / 32) > ctx->sm_count * 8)
+    return fail(ctx, QXC_ERR_UNSUPPORTED, "the merge grid must fit one wave");
+  return decode_partials_impl(ctx, kv, a, g, out, out_dtype);
 }
 
 // ---- prefill -------------------------------------------------------------------

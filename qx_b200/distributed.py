@@ -9,8 +9,10 @@ Two ways the path spreads over GPUs of one node:
   position ranges, one per rank; the last range owns the new token (RoPE +
   append). Each rank computes per-query-head partials (O, m, l) over its
   range with qxc_decode_partials; the partials ([q_heads][head_dim + 2]
-  f32, 16,640 bytes per rank for Qwen3) are all-gathered (NCCL over NVLink)
-  and merged with qxc_lse_merge.
+  f32, 16,640 bytes per rank for Qwen3) are exchanged over NVLink and
+  merged: qxc_exchange_merge pushes them into every rank's memory with peer
+  stores and merges in one kernel (open_peer_group sets it up); the NCCL
+  all-gather + qxc_lse_merge path (all_gather_partials) gives the same bits.
 """
 from __future__ import annotations
 
@@ -61,3 +63,26 @@ def all_gather_partials(partials, group=None):
     out = torch.empty((world * flat.numel(),), dtype=partials.dtype, device=partials.device)
     dist.all_gather_into_tensor(out, flat, group=group)  # rank-major concatenation
     return out.view(world, *partials.shape)
+
+
+def exchange_handles(local: bytes, group=None) -> list:
+    """Every rank's bytes, in rank order (all_gather_object on the process group)."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, local, group=group)
+    return out
+
+
+def open_peer_group(ctx, group=None):
+    """Create this rank's qx_b200.PeerGroup and attach every other rank's area
+    through CUDA IPC handles exchanged over the process group."""
+    import torch.distributed as dist
+    from .runtime import PeerGroup
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    pg = PeerGroup(ctx, rank, world)
+    handles = exchange_handles(pg.ipc_handle(), group)
+    for r, h in enumerate(handles):
+        if r != rank:
+            pg.open(r, h)
+    dist.barrier(group)
+    return pg

@@ -123,6 +123,55 @@ class Context:
         self.check(self.lib.qxc_lse_merge(self.handle, model, n_parts, _ptr(partials), _ptr(out), out_dtype))
 
 
+class PeerGroup:
+    """qxc_peer_group: this rank's area for the NVLink exchange of a KV-length
+    split (qxc_exchange_merge). Attach every other rank's area with open()
+    (a CUDA IPC handle from another process) or set_peer() (another group of
+    this process); qx_b200.distributed.open_peer_group does it for a
+    torch.distributed job."""
+
+    def __init__(self, ctx: Context, rank: int, world: int):
+        self.ctx, self.lib = ctx, ctx.lib
+        h = C.c_void_p()
+        ctx.check(self.lib.qxc_peer_group_create(ctx.handle, rank, world, C.byref(h)))
+        self.handle, self.rank, self.world = h, rank, world
+
+    def close(self):
+        if getattr(self, "handle", None):
+            if self.ctx.handle:
+                self.lib.qxc_peer_group_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def ipc_handle(self) -> bytes:
+        buf = C.create_string_buffer(_lib.PEER_HANDLE_BYTES)
+        self.ctx.check(self.lib.qxc_peer_group_handle(self.handle, buf))
+        return buf.raw
+
+    def base(self) -> int:
+        p = C.c_void_p()
+        self.ctx.check(self.lib.qxc_peer_group_base(self.handle, C.byref(p)))
+        return p.value
+
+    def open(self, peer: int, ipc_handle: bytes) -> None:
+        buf = C.create_string_buffer(bytes(ipc_handle), _lib.PEER_HANDLE_BYTES)
+        self.ctx.check(self.lib.qxc_peer_group_open(self.handle, peer, buf))
+
+    def set_peer(self, peer: int, base: int) -> None:
+        self.ctx.check(self.lib.qxc_peer_group_set_peer(self.handle, peer, C.c_void_p(base)))
+
+    def exchange_merge(self, model: int, partials, out, out_dtype: int = F32) -> None:
+        """Push this rank's partials [q_heads][head_dim + 2] to every rank and
+        merge all ranks' into out [q_heads][head_dim] (device tensors)."""
+        self.ctx.check(self.lib.qxc_exchange_merge(self.ctx.handle, self.handle, model, _ptr(partials), _ptr(out),
+                                                   out_dtype))
+
+
 _default_ctx: Context | None = None
 
 
@@ -365,6 +414,21 @@ class KvArena:
                              _ptr(k_norm), _ptr(partials), dflt if q_dtype is None else q_dtype,
                              dflt if in_dtype is None else in_dtype, flags, split)
         self.ctx.check(self.lib.qxc_decode_partials(self.ctx.handle, self.handle, C.byref(a)))
+
+
+    def decode_exchange(self, q, k, v, out, position: int, append: bool, group: "PeerGroup", seq: int = 0,
+                        layer: int = 0, out_dtype: int = F32, q_dtype: int | None = None,
+                        in_dtype: int | None = None, flags: int = 0, split: int = 0, q_norm=None,
+                        k_norm=None) -> None:
+        """This rank's part of a KV-length split decode, exchanged with every
+        rank over NVLink inside the split merge kernel (qxc_decode_exchange):
+        out [q_heads][head_dim] holds the merged attention of all ranks."""
+        dflt = self.key_dtype if self.model == MODEL_QWEN3 else F32
+        a = _lib.PartialArgs(seq, layer, position, int(bool(append)), _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm),
+                             _ptr(k_norm), None, dflt if q_dtype is None else q_dtype,
+                             dflt if in_dtype is None else in_dtype, flags, split)
+        self.ctx.check(self.lib.qxc_decode_exchange(self.ctx.handle, self.handle, C.byref(a), group.handle,
+                                                    _ptr(out), out_dtype))
 
 
 # ---- qx-runtime (V1) mirror ---------------------------------------------------
