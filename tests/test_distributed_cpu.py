@@ -100,3 +100,51 @@ def test_partial_exchange_two_gloo_ranks():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert q.get(timeout=5) < 1e-5
+
+
+def _handle_worker(rank, world, port, result_q):
+    """open_peer_group's host side: every rank's IPC handle reaches every
+    other rank, which attaches it under the sender's rank (the CUDA calls are
+    replaced by a recording stand-in)."""
+    import sys
+    import torch.distributed as dist
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import qx_b200.runtime as rt
+    from qx_b200.distributed import open_peer_group
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+
+    class Recorder:
+        def __init__(self, ctx, r, w):
+            self.rank, self.world, self.opened = r, w, {}
+
+        def ipc_handle(self):
+            return bytes([65 + self.rank]) * 64
+
+        def open(self, peer, handle):
+            self.opened[peer] = handle
+
+    rt.PeerGroup = Recorder
+    g = open_peer_group(None)
+    result_q.put((rank, g.rank, g.world, sorted((p, h) for p, h in g.opened.items())))
+    dist.destroy_process_group()
+
+
+def test_peer_group_handles_three_gloo_ranks():
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 3
+    procs = [ctx.Process(target=_handle_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    got = sorted(q.get(timeout=5) for _ in range(world))
+    for rank, grank, gworld, opened in got:
+        assert (grank, gworld) == (rank, world)
+        assert opened == [(p, bytes([65 + p]) * 64) for p in range(world) if p != rank]
