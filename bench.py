@@ -10,7 +10,7 @@ reference's speculative rollback does), so every step reads ~400 MB of KV,
 far more than the 126 MB L2.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload config1|config0|config2|config3|config4|layer|commit]
+                    [--workload config1|config0|config2|config3|config4|layer|commit|verify]
 
 Prints one JSON line on rank 0. N>1 runs under torchrun: one independent
 sequence (replica) per GPU, no collective on the data path ("weak" scaling),
@@ -879,6 +879,64 @@ def run_commit(args, world, rank, local):
     return line
 
 
+def run_verify(args, world, rank, local):
+    """Speculative verify (the reference's batched verifier stage): each step
+    checks K = 4 candidate tokens of one sequence through the Granite
+    24-layer stack, fp32 KV, context 4096, in one qxc_decode_verify call
+    (the candidates' rows appended, token t attending [0, start + t]); the
+    cursor then rolls back to the checkpoint, as after a rejected draft."""
+    import torch
+    from qx_b200 import F32, MODEL_GRANITE, Context, KvArena
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L, Kc = args.context, 4
+    P = L - Kc
+    ctx = Context(local)
+    stream = torch.cuda.Stream(device=dev)
+    ctx.set_stream(stream)
+    arena = KvArena(ctx, MODEL_GRANITE, LAYERS, 1, L, F32, F32)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0x51580700 + rank)
+    NSET = 16  # candidate sets, cycled
+    with torch.cuda.stream(stream):
+        for l in range(LAYERS):
+            arena.tensor(0, l, True)[:P].normal_(generator=g)
+            arena.tensor(0, l, False)[:P].normal_(generator=g)
+        q = torch.randn(NSET, Kc, LAYERS, 1024, device=dev, generator=g)
+        k = torch.randn(NSET, Kc, LAYERS, 512, device=dev, generator=g)
+        v = torch.randn(NSET, Kc, LAYERS, 512, device=dev, generator=g)
+        out = torch.zeros(Kc, LAYERS, 1024, device=dev)
+    stream.synchronize()
+    arena.set_len(0, P)
+
+    def step(i):
+        arena.rollback(0, P)
+        j = i % NSET
+        arena.decode_verify(q[j], k[j], v[j], out, P, Kc, split=args.split)
+
+    with torch.cuda.stream(stream):
+        total, per, clk, launches = timed_steps(step, args.steps, args.warmup, stream, world, dev, local, ctx)
+    stream.synchronize()
+    K = args.steps
+    # algorithmic bytes: the cache read once (P + K rows per layer) and the
+    # candidates' q/k/v/out; the K tokens share every row
+    row = 8 * 64 * 4
+    B = LAYERS * (2 * (P + Kc) * row + Kc * (1024 + 512 + 512 + 1024) * 4)
+    line = base_line("speculative verify tok/s (Granite 24-layer stack, 4 candidates per step, fp32 KV)",
+                     world * K * Kc / (total / 1e3), "tok/s", world, K, args.warmup, total, True, "weak", "f32",
+                     {"workload": f"qxc_decode_verify of {Kc} candidate tokens at positions {P}..{L - 1} through "
+                                  f"24 Granite layers, fp32 KV, context {L}, cursor rolled back after each step",
+                      "l2": "inputs larger than L2: ~%.0f MB of KV per step" % (LAYERS * 2 * P * row / 1e6),
+                      "candidates": Kc},
+                     clk, launches)
+    line["verify_steps_per_s"] = world * K / (total / 1e3)
+    line["config"]["split"] = ctx.last_split
+    line["roofline"] = hbm_roofline(B, per, "qx_append_rows_kernel + qx_decode_kernel<Granite,float,float>")
+    arena.close()
+    ctx.close()
+    return line
+
+
 def run_config4(args, world, rank, local):
     """Config 4: 256 independent Granite sequences, lengths U{128..4096}, bf16 KV,
     one decode step through 24 layers; sequences sharded over ranks by LPT on KV bytes."""
@@ -1029,7 +1087,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config1",
-                    choices=["config0", "config1", "config2", "config3", "config4", "layer", "commit"])
+                    choices=["config0", "config1", "config2", "config3", "config4", "layer", "commit", "verify"])
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--paged", type=int, default=0, help="config4: paged KV arena with this many rows per page")
@@ -1064,7 +1122,8 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         run = {"config0": run_config0, "config1": run_config1, "config2": run_config2, "config3": run_config3,
-               "config4": run_config4, "layer": run_layer, "commit": run_commit}[args.workload]
+               "config4": run_config4, "layer": run_layer, "commit": run_commit,
+               "verify": run_verify}[args.workload]
         line = run(args, world, rank, local)
         if rank == 0:
             print(json.dumps(line), flush=True)

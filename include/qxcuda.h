@@ -231,6 +231,12 @@ typedef struct {
   int32_t split; /* 0: automatic */
 } qxc_verify_args;
 
+/* Granite, 2 to 4 candidates: every cache tile is read once and scored
+ * against all candidates' queries (one work item per layer, kv head and
+ * split). QXC_VERIFY_PER_TOKEN in flags forces one causal decode entry per
+ * candidate instead (each reads the cache: the layout Qwen and longer
+ * drafts use). */
+#define QXC_VERIFY_PER_TOKEN 0x8
 qxc_status qxc_decode_verify(qxc_ctx* ctx, qxc_kv* kv, const qxc_verify_args* args);
 
 /* ---- Q4 projections around attention (Granite layer) --------------------- */

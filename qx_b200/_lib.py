@@ -18,6 +18,7 @@ OK, ERR_INVALID_ARG, ERR_POSITION, ERR_NONFINITE, ERR_CUDA, ERR_NCCL, ERR_TIMEOU
 MODEL_GRANITE, MODEL_QWEN3 = 0, 1
 F32, BF16, F16 = 0, 1, 2
 DECODE_NO_ADVANCE, DECODE_NATIVE_EXP, DECODE_PINNED_EXP = 0x1, 0x2, 0x4
+VERIFY_PER_TOKEN = 0x8
 HASH_AUTO, HASH_PER_CHUNK, HASH_PER_SLOT = 0, 1, 2
 PEER_HANDLE_BYTES = 64
 

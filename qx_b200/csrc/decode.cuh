@@ -35,15 +35,24 @@
 
 namespace qx {
 
+// G query rows per kv head in a work item: NTOK tokens x G0 query heads.
 struct Granite {
-  static constexpr int HQ = 16, HKV = 8, D = 64, G = 2;
+  static constexpr int HQ = 16, HKV = 8, D = 64, G = 2, NTOK = 1, G0 = 2;
   static constexpr bool QWEN = false;
   static constexpr float SCALE = 0.015625f;  // ATTENTION_MULTIPLIER, qx-model lib.rs:20
 };
 struct Qwen3 {
-  static constexpr int HQ = 32, HKV = 4, D = 128, G = 8;
+  static constexpr int HQ = 32, HKV = 4, D = 128, G = 8, NTOK = 1, G0 = 8;
   static constexpr bool QWEN = true;
   static constexpr float SCALE = 0.08838834764831845f;  // 1/sqrt(128)
+};
+// Speculative verify of up to 4 candidate tokens of one sequence: every
+// cache tile is scored against the 4 tokens' queries at once, token t
+// seeing rows [0, start + t] (HQ counts the 4 tokens' heads).
+struct GraniteVerify4 {
+  static constexpr int HQ = 64, HKV = 8, D = 64, G = 8, NTOK = 4, G0 = 2;
+  static constexpr bool QWEN = false;
+  static constexpr float SCALE = Granite::SCALE;
 };
 
 // Per-sequence entry of one call.
@@ -118,7 +127,22 @@ struct DecodeParams {
   int xrank, xworld;
   void* xout;  // final output [HQ][D]
   int xout_dtype;
+  int ntok;  // candidate tokens of a multi-token item (GraniteVerify4), <= its NTOK
 };
+
+// Element d of output row g (of the G rows of kv head h) of unit cu. One
+// token per item: [unit][HQ][D]. NTOK tokens per item (one sequence): row g
+// is token g / G0's query head h * G0 + g % G0, stored [token][layer][HQ / NTOK][D]
+// like the q and out tensors of a verify call; cu is then the layer within it.
+template <int G, int D, int HQ, int NTOK, int G0>
+__device__ __forceinline__ long long out_elem(const DecodeParams& p, long long cu, int h, int g, int d) {
+  if constexpr (NTOK == 1) {
+    return (cu * HQ + (long long)h * G + g) * D + d;
+  } else {
+    const int t = g / G0;
+    return (((long long)t * p.layer_count + cu) * (HQ / NTOK) + h * G0 + g % G0) * D + d;
+  }
+}
 
 template <class M, typename KT, typename VT>
 struct DecodeCfg {
@@ -232,11 +256,10 @@ __device__ __forceinline__ int find_slot(const DecodeParams& p, SeqInfo* info) {
 // CTA of the (sequence, layer, kv head) to finish (atomic ticket, no
 // spinning) merges them by log-sum-exp and resets the ticket.
 // merge_smem must hold 2 * G * nsplit floats, stat_smem 2 * G floats.
-template <int G, int D, int HKV, int HQ, int OPT>
+template <int G, int D, int HKV, int HQ, int OPT, int NTOK = 1, int G0 = G>
 __device__ __forceinline__ void finish_outputs(const DecodeParams& p, const float* O, const float* Mg, const float* Lg,
                                                int nsplit, int s, long long cu, int h, int tid, int warp, int lane,
                                                bool pinned, float* merge_smem, float* stat_smem, int* s_flag) {
-  const long long obase = (cu * HQ + (long long)h * G) * D;
   // (with an exchange across GPUs even one split goes to qx_split_merge_kernel,
   // which pushes it to the peers)
   if (nsplit == 1 && !p.xworld) {
@@ -251,10 +274,10 @@ __device__ __forceinline__ void finish_outputs(const DecodeParams& p, const floa
           part[D] = Mg[k];
           part[D + 1] = Lg[k];
         }
-      } else {
+      } else if (NTOK == 1 || g / G0 < p.ntok) {
         const float o = O[k] / Lg[k];
         nonfinite |= !isfinite(o);
-        store_any(p.out, obase + idx, p.out_dtype, o);
+        store_any(p.out, out_elem<G, D, HQ, NTOK, G0>(p, cu, h, g, d), p.out_dtype, o);
       }
     }
     if (nonfinite) flag_error(p.err, QX_ERR_BIT_NONFINITE);
@@ -340,10 +363,10 @@ __device__ __forceinline__ void finish_outputs(const DecodeParams& p, const floa
         dst[D] = mx;
         dst[D + 1] = L;
       }
-    } else {
+    } else if (NTOK == 1 || g / G0 < p.ntok) {
       const float v = o[k] / L;
       nonfinite |= !isfinite(v);
-      store_any(p.out, obase + idx, p.out_dtype, v);
+      store_any(p.out, out_elem<G, D, HQ, NTOK, G0>(p, cu, h, g, d), p.out_dtype, v);
     }
   }
   if (nonfinite) flag_error(p.err, QX_ERR_BIT_NONFINITE);
@@ -351,7 +374,7 @@ __device__ __forceinline__ void finish_outputs(const DecodeParams& p, const floa
 }
 
 template <class M, typename KT, typename VT>
-__global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(const __grid_constant__ DecodeParams p) {
+__device__ __forceinline__ void decode_body(const DecodeParams& p) {
   using C = DecodeCfg<M, KT, VT>;
   if (p.early_trigger) pdl_launch_dependents();  // the merge grid may get resident meanwhile
   constexpr int D = M::D, G = M::G, HKV = M::HKV, HQ = M::HQ, T = C::T, NWC = C::NWC, WT = C::WT;
@@ -435,12 +458,16 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
       // 32 rotation pairs per head: warps 0-1 the G=2 query heads, warp 2 k.
       if (tid < G * 32) {
         const int g = tid >> 5, pair = tid & 31;
-        float left = load_any(p.q, qbase + g * D + pair, p.q_dtype);
-        float right = load_any(p.q, qbase + g * D + pair + 32, p.q_dtype);
+        // several candidate tokens per item: row g is token g / G0 at its own position
+        const int tok = g / M::G0;
+        const bool live = M::NTOK == 1 || tok < p.ntok;
+        const long long qa = M::NTOK == 1 ? qbase + g * D : out_elem<G, D, HQ, M::NTOK, M::G0>(p, cu, h, g, 0);
+        float left = live ? load_any(p.q, qa + pair, p.q_dtype) : 0.0f;
+        float right = live ? load_any(p.q, qa + pair + 32, p.q_dtype) : 0.0f;
         float sn, cs, a = 0.f, b = 0.f;
-        bool ok = granite_sin_cos((uint32_t)si.rope_pos, pair, &sn, &cs) &&
+        bool ok = granite_sin_cos((uint32_t)(si.rope_pos + tok), pair, &sn, &cs) &&
                   granite_rotate(left, right, sn, cs, &a, &b);
-        bad |= !ok;
+        bad |= live && !ok;
         q_s[g * D + pair] = a;
         q_s[g * D + pair + 32] = b;
         if (p.q_rot_out && last_split) {
@@ -584,6 +611,13 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
           }
 #pragma unroll
           for (int j = 0; j < QPL; ++j) sc[j] = ((part[j][0] + part[j][1]) + (part[j][2] + part[j][3])) * M::SCALE;
+          if constexpr (M::NTOK > 1) {
+            // candidate t sees rows [0, start + t]: attend = start + ntok
+            const int row = begin + tile * T + r0 + trow;
+#pragma unroll
+            for (int j = 0; j < QPL; ++j)
+              if (row > si.attend - p.ntok + (hq0 + j) / M::G0) sc[j] = -INFINITY;
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < QPL; ++j) sc[j] = -INFINITY;
@@ -600,7 +634,9 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
             if (gg == g) mold = m_run[gg];
           const float mnew = fmaxf(mold, mt);
           a_l[j] = (mold == -INFINITY) ? 0.0f : softmax_exp(mold - mnew, pinned);
-          const float pw = trow < mine ? softmax_exp(sc[j] - mnew, pinned) : 0.0f;
+          // (a candidate may see none of these rows yet: then mnew is -inf too)
+          const bool seen = M::NTOK == 1 ? trow < mine : (trow < mine && sc[j] != -INFINITY);
+          const float pw = seen ? softmax_exp(sc[j] - mnew, pinned) : 0.0f;
           Pw[trow * G + g] = pw;
           s_l[j] = half_sum(pw);
           m_l[j] = mnew;
@@ -712,8 +748,21 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
     Lg[k] = L;
   }
 
-  finish_outputs<G, D, HKV, HQ, OPT>(p, O, Mg, Lg, nsplit, s, cu, h, tid, warp, lane, pinned,
-                                     reinterpret_cast<float*>(sm + C::OFF_K), stat, s_flag);
+  finish_outputs<G, D, HKV, HQ, OPT, M::NTOK, M::G0>(p, O, Mg, Lg, nsplit, s, cu, h, tid, warp, lane, pinned,
+                                                    reinterpret_cast<float*>(sm + C::OFF_K), stat, s_flag);
+}
+
+template <class M, typename KT, typename VT>
+__global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(const __grid_constant__ DecodeParams p) {
+  decode_body<M, KT, VT>(p);
+}
+
+// The multi-token verify variant: its group of 8 query rows would hold one
+// CTA per SM by registers; two resident CTAs keep more loads in flight.
+template <typename KT, typename VT>
+__global__ void __launch_bounds__(DecodeCfg<GraniteVerify4, KT, VT>::NT, 2)
+    qx_verify_kernel(const __grid_constant__ DecodeParams p) {
+  decode_body<GraniteVerify4, KT, VT>(p);
 }
 
 // ---- split merge as its own kernel (many splits) ----------------------------
@@ -731,7 +780,7 @@ __global__ void __launch_bounds__(DecodeCfg<M, KT, VT>::NT) qx_decode_kernel(con
 // the decode kernel used.
 constexpr int kMergeLoads = 16;
 
-template <int G, int D, int HKV, int HQ>
+template <int G, int D, int HKV, int HQ, int NTOK = 1, int G0 = G>
 __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_constant__ DecodeParams p) {
   const int tid = threadIdx.x, q = tid & 3;
   const int blk = blockIdx.x;
@@ -860,10 +909,10 @@ __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_consta
         dst[D] = M;
         dst[D + 1] = L;
       }
-    } else {
+    } else if (NTOK == 1 || g / G0 < p.ntok) {
       const float v = o / L;
       if (!isfinite(v)) flag_error(p.err, QX_ERR_BIT_NONFINITE);
-      store_any(p.out, (cu * HQ + qh) * D + d, p.out_dtype, v);
+      store_any(p.out, out_elem<G, D, HQ, NTOK, G0>(p, cu, h, g, d), p.out_dtype, v);
     }
   }
   trace.mark();  // done

@@ -788,6 +788,69 @@ qxc_status hash_params(qxc_ctx* ctx, const qxc_kv* kv, int seq, HashParams* p) {
   return QXC_OK;
 }
 
+// Speculative verify of 2..4 Granite candidates with shared tiles
+// (GraniteVerify4): one work item per (layer, kv head, split) scores each
+// cache tile against all candidates' query rows, so the cache is read once
+// per call instead of once per candidate.
+template <typename KT, typename VT>
+qxc_status launch_verify_typed(qxc_ctx* ctx, qxc_kv* kv, const qxc_verify_args* a) {
+  using C = DecodeCfg<GraniteVerify4, KT, VT>;
+  static int slots_cache[64] = {};
+  int& slots = slots_cache[ctx->device & 63];
+  if (!slots) {
+    QXC_CUDA(ctx, cudaFuncSetAttribute(qx_verify_kernel<KT, VT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    int n = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qx_verify_kernel<KT, VT>, C::NT, C::SMEM) != cudaSuccess || n < 1)
+      n = 1;
+    slots = ctx->sm_count * n;
+  }
+  int attend = a->start + a->tokens, none = -1, rope = a->start, seq = a->seq;
+  const int split = a->split ? a->split : auto_chunk(slots, &attend, 1, a->layer_count * kv->hkv, C::MAX_SPLITS, 64);
+  if ((attend + split - 1) / split > C::MAX_SPLITS)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "split %d gives %d splits; at most %d fit the merge", split,
+                (attend + split - 1) / split, C::MAX_SPLITS);
+  CallPlan plan;
+  qxc_status st = plan_call(ctx, kv, 1, &seq, &attend, &none, &rope, a->layer_count, split, &plan);
+  if (st != QXC_OK) return st;
+  DecodeParams p;
+  st = fill_params(ctx, kv, plan, a->layer_begin, a->layer_count, &p);
+  if (st != QXC_OK) return st;
+  st = grow(ctx, &ctx->partials, &ctx->partials_cap, (size_t)plan.items * C::G * (C::D + 2), false);
+  if (st != QXC_OK) return st;
+  p.partials = ctx->partials;
+  p.early_trigger = plan.items <= slots ? 1 : 0;
+  p.q = a->q;
+  p.k = a->k;  // not read: the rows were appended already
+  p.v = a->v;
+  p.out = a->out;
+  p.q_dtype = a->q_dtype;
+  p.in_dtype = a->in_dtype;
+  p.out_dtype = a->out_dtype;
+  p.pinned_exp = default_pinned(kv, a->flags) ? 1 : 0;
+  p.ntok = a->tokens;
+  {
+    TraceRun tr(ctx, "verify", plan.items);
+    p.trace = tr.buf;
+    QXC_CUDA(ctx, launch_pdl(ctx, qx_verify_kernel<KT, VT>, plan.items, C::NT, C::SMEM, p));
+    ctx->launches++;
+  }
+  if (!p.external_merge) return QXC_OK;
+  p.trace = nullptr;
+  const int grid = a->layer_count * GraniteVerify4::HQ * (GraniteVerify4::D / 32);
+  QXC_CUDA(ctx, launch_pdl(ctx, qx_split_merge_kernel<8, 64, 8, 64, 4, 2>, grid, 128, 0, p));
+  ctx->launches++;
+  return QXC_OK;
+}
+
+qxc_status launch_verify_shared(qxc_ctx* ctx, qxc_kv* kv, const qxc_verify_args* a) {
+  const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
+  if (kd == QXC_F32 && vd == QXC_F32) return launch_verify_typed<float, float>(ctx, kv, a);
+  if (kd == QXC_F32 && vd == QXC_F16) return launch_verify_typed<float, __half>(ctx, kv, a);
+  if (kd == QXC_F16 && vd == QXC_F32) return launch_verify_typed<__half, float>(ctx, kv, a);
+  if (kd == QXC_F16 && vd == QXC_F16) return launch_verify_typed<__half, __half>(ctx, kv, a);
+  return launch_verify_typed<__nv_bfloat16, __nv_bfloat16>(ctx, kv, a);
+}
+
 extern "C" {
 
 int qxc_abi_version(void) { return QXC_ABI_VERSION; }
@@ -1392,7 +1455,15 @@ qxc_status qxc_decode_verify(qxc_ctx* ctx, qxc_kv* kv, const qxc_verify_args* a)
   else if (kd == QXC_F16 && vd == QXC_F16) st = launch_append<Granite, __half, __half>(ctx, ap, grid);
   else st = launch_append<Granite, __nv_bfloat16, __nv_bfloat16>(ctx, ap, grid);
   if (st != QXC_OK) return st;
-  // 2. token t attends [0, start + t]: one decode launch, one causal entry per token
+  // 2. token t attends [0, start + t]
+  if (kv->desc.model == QXC_MODEL_GRANITE && a->tokens >= 2 && a->tokens <= GraniteVerify4::NTOK &&
+      !(a->flags & QXC_VERIFY_PER_TOKEN)) {
+    st = launch_verify_shared(ctx, kv, a);
+    if (st != QXC_OK) return st;
+    if (!(a->flags & QXC_DECODE_NO_ADVANCE)) kv->len[a->seq] += a->tokens;
+    return QXC_OK;
+  }
+  // one decode launch with one causal entry per token
   std::vector<int> ids(a->tokens, a->seq), attend(a->tokens), none(a->tokens, -1), rope(a->tokens);
   for (int t = 0; t < a->tokens; ++t) {
     attend[t] = a->start + t + 1;

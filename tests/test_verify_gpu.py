@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 from helpers import as_kv, normwise
-from qx_b200 import BF16, F32, MODEL_GRANITE, MODEL_QWEN3, KvArena, QxError
+from qx_b200 import BF16, F16, F32, MODEL_GRANITE, MODEL_QWEN3, KvArena, QxError
 from qx_b200 import synthetic as syn
 
 pytestmark = pytest.mark.gpu
@@ -34,7 +34,7 @@ def filled(ctx, model, layers, cap, kd, vd, kc, vc):
     return a
 
 
-@pytest.mark.parametrize("prefix,tokens", [(0, 1), (37, 4), (500, 4), (1023, 3)])
+@pytest.mark.parametrize("prefix,tokens", [(0, 1), (0, 4), (37, 4), (63, 2), (500, 4), (1023, 3)])
 def test_granite_verify_equals_successive_decodes(gpu_ctx, oracle, prefix, tokens):
     import torch
     layers, cap = 2, 1100
@@ -156,3 +156,35 @@ def test_verify_rejects_bad_positions(gpu_ctx):
     with pytest.raises(QxError, match="at least one token"):
         a.decode_verify(z, zk, zk, z, 5, 0)
     assert a.len(0) == 5
+
+
+@pytest.mark.parametrize("prefix,tokens,split", [(300, 4, 64), (4000, 4, 0), (4000, 3, 64), (126, 2, 64),
+                                                 (2000, 4, 2048)])
+@pytest.mark.parametrize("kd,vd", [(F32, F32), (BF16, BF16), (F16, F32)])
+def test_shared_tile_verify_equals_per_token(gpu_ctx, prefix, tokens, split, kd, vd):
+    """2..4 Granite candidates share every cache tile (one work item per
+    layer, kv head and split); against one causal decode entry per
+    candidate (QXC_VERIFY_PER_TOKEN): rows bit-identical, outputs within
+    fp32 rounding. Splits cover the in-kernel merge (5 splits), the
+    separate merge (63) and one split; the draft crosses a 64-row tile."""
+    import torch
+    from helpers import as_kv
+    from qx_b200._lib import VERIFY_PER_TOKEN
+    layers, cap = 2, 4096
+    kc, vc, q, k, v = granite_case(0x7500 + prefix + tokens, prefix, tokens, layers)
+    kc, vc = as_kv(kc, kd), as_kv(vc, vd)
+    a = filled(gpu_ctx, MODEL_GRANITE, layers, cap, kd, vd, kc, vc)
+    b = filled(gpu_ctx, MODEL_GRANITE, layers, cap, kd, vd, kc, vc)
+    dev = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    oa = torch.zeros(tokens, layers, 1024, device="cuda")
+    ob = torch.zeros_like(oa)
+    a.decode_verify(dev(q), dev(k), dev(v), oa, prefix, tokens, split=split)
+    b.decode_verify(dev(q), dev(k), dev(v), ob, prefix, tokens, split=split, flags=VERIFY_PER_TOKEN)
+    gpu_ctx.sync()
+    for l in range(layers):
+        ak, av = a.read(0, l, 0, prefix + tokens)
+        bk, bv = b.read(0, l, 0, prefix + tokens)
+        assert np.array_equal(ak, bk) and np.array_equal(av, bv)
+    tol = 1e-5 if kd == F32 and vd == F32 else 2e-2
+    assert normwise(oa.cpu().numpy(), ob.cpu().numpy()) <= tol
+    assert torch.isfinite(oa).all()
