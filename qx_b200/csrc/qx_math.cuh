@@ -55,16 +55,6 @@ __device__ __forceinline__ float native_exp(float x) {
 }
 
 // Hardware base-2 exponential (MUFU.EX2); exp2(-inf) = +0.
-// 2^a, 2^b for two f32 exponents, evaluated and returned as packed bf16
-// (ex2.approx on bf16x2: the arguments are rounded to bf16 first; a in the
-// low half). Exact zero for -inf.
-__device__ __forceinline__ uint32_t exp2_bf16x2(float a, float b) {
-  const __nv_bfloat162 x = __floats2bfloat162_rn(a, b);
-  uint32_t y;
-  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(*reinterpret_cast<const uint32_t*>(&x)));
-  return y;
-}
-
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -215,12 +205,6 @@ __device__ __forceinline__ void store_any(void* base, long long i, int dtype, fl
   if (dtype == 1) reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
   else if (dtype == 2) reinterpret_cast<__half*>(base)[i] = __float2half_rn(v);
   else reinterpret_cast<float*>(base)[i] = v;
-}
-// Round f32 to a 16-bit type and back (bf16 / f16), identity for f32.
-__device__ __forceinline__ float round_to(float v, int dtype) {
-  if (dtype == 1) return __bfloat162float(__float2bfloat16_rn(v));
-  if (dtype == 2) return __half2float(__float2half_rn(v));
-  return v;
 }
 
 // Four consecutive elements from shared memory as f32.

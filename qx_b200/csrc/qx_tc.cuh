@@ -104,8 +104,6 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
 // Store 32 consecutive f32 columns of this thread's TMEM lane (x32) or one
 // column (x1); tmem_wait_st() waits for this thread's stores.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {

@@ -282,8 +282,7 @@ using KernelFn = void (*)(DecodeParams);
 // previous kernel: its CTAs may become resident and set up (barriers, TMEM)
 // while that kernel drains, and wait for it in griddepcontrol.wait.
 cudaError_t launch_pdl(qxc_ctx* ctx, KernelFn fn, int grid, int threads, int smem, const DecodeParams& p) {
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
@@ -624,8 +623,7 @@ qxc_status ensure_qwen_rope(qxc_ctx* ctx) {
 qxc_status launch_matvec(qxc_ctx* ctx, const LayerParams& p) {
   int rows = 0;
   for (int m = 0; m < p.nmat; ++m) rows += p.w[m].rows;
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(std::min(1024, (rows + 7) / 8));
   cfg.blockDim = dim3(256);
   cfg.stream = ctx->stream;
@@ -661,8 +659,7 @@ Q4Ref q4ref(const qxc_q4_matrix& w) {
 // Append kernel of qxc_decode_verify, a programmatic dependent like the decode.
 template <class M, typename KT, typename VT>
 qxc_status launch_append(qxc_ctx* ctx, const AppendParams& a, int grid) {
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(128);
   cfg.stream = ctx->stream;
@@ -735,8 +732,7 @@ void release_pages(qxc_kv* kv, int seq, int keep) {
 // stream's previous kernel before reading rows).
 qxc_status launch_hash(qxc_ctx* ctx, const HashParams& p, int ctas, void (*fn)(HashParams) = qx_kv_hash_kernel,
                        int smem = 0, int warps_per_cta = kHashWarps) {
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas);
   cfg.blockDim = dim3(32 * warps_per_cta);
   cfg.dynamicSmemBytes = smem;
@@ -1686,10 +1682,11 @@ qxc_status qxc_peer_group_create(qxc_ctx* ctx, int32_t rank, int32_t world, qxc_
   g->off_xinbox = (inbox + 255) / 256 * 256;
   g->off_step = g->off_xinbox + (xinbox + 255) / 256 * 256;
   g->bytes = g->off_step + 1024;  // [32] exchange-kernel steps, then [32][4] split-merge steps
-  cudaError_t e = cudaMalloc(&g->base, g->bytes);
+  const size_t bytes = g->bytes;
+  cudaError_t e = cudaMalloc(&g->base, bytes);
   if (e != cudaSuccess) {
     delete g;
-    return fail(ctx, QXC_ERR_OUT_OF_MEMORY, "exchange area of %zu bytes: %s", g->bytes, cudaGetErrorString(e));
+    return fail(ctx, QXC_ERR_OUT_OF_MEMORY, "exchange area of %zu bytes: %s", bytes, cudaGetErrorString(e));
   }
   e = cudaMemset(g->base, 0, g->bytes);
   if (e != cudaSuccess) {
@@ -1793,8 +1790,7 @@ qxc_status qxc_exchange_merge(qxc_ctx* ctx, qxc_peer_group* g, int32_t model, co
   QXC_CUDA(ctx, cudaSetDevice(ctx->device));
   TraceRun tr(ctx, "exchange", (size_t)p.hq);
   p.trace = tr.buf;
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.hq);
   cfg.blockDim = dim3(kExchThreads);
   cfg.stream = ctx->stream;
@@ -1885,8 +1881,7 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
   // the attention grid is a programmatic dependent of the RoPE grid: its CTAs
   // initialise barriers and TMEM while the RoPE grid drains, and wait for it
   // (griddepcontrol.wait) before the first TMA load
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
+  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nqb * 8);
   cfg.blockDim = dim3(PrefillCfg::NT);
   cfg.dynamicSmemBytes = PrefillCfg::SMEM;
