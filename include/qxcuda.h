@@ -187,8 +187,10 @@ typedef struct qxc_decode_args {
   int32_t split;            /* cache positions per CTA split, multiple of 64; 0 = automatic */
 } qxc_decode_args;
 qxc_status qxc_decode(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* args);
-/* Same with q, k, v, out (and q_rot_out) in HOST memory: copies in, decodes,
- * copies out, waits. */
+/* Same with q, k, v, out (and q_rot_out) in HOST memory, synchronous. When
+ * every one of them is pinned memory the device can address (cudaHostAlloc,
+ * or cudaHostRegister with cudaHostRegisterMapped) the kernels read and write
+ * it in place over PCIe; otherwise the call copies in, decodes, copies out. */
 qxc_status qxc_decode_host(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* args);
 
 /* granite_attention_decode (qx-runtime lib.rs:444-452): host arrays

@@ -1511,11 +1511,42 @@ qxc_status qxc_decode_host(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* a) {
   auto al = [](size_t x) { return ((x + 255) / 256) * 256; };
   const size_t off_k = al(qb), off_v = off_k + al(kb), off_o = off_v + al(kb), off_r = off_o + al(ob);
   const size_t total = off_r + al(rb);
+  // Pinned host buffers that the device can address (cudaHostAlloc, which
+  // maps them under unified addressing, or cudaHostRegister with the mapped
+  // flag; torch's pin_memory is the former): the kernels read q/k/v over
+  // PCIe in their prologue, while the KV stream starts, and write the
+  // outputs straight back, so no copy is queued before or after them.
+  {
+    auto mapped = [](const void* h, void** d) {
+      cudaPointerAttributes at;
+      if (cudaPointerGetAttributes(&at, h) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+      }
+      if (at.type != cudaMemoryTypeHost || !at.devicePointer) return false;
+      *d = at.devicePointer;
+      return true;
+    };
+    void *dq, *dk, *dv, *dout, *drot = nullptr;
+    QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+    if (mapped(a->q, &dq) && mapped(a->k, &dk) && mapped(a->v, &dv) && mapped(a->out, &dout) &&
+        (!a->q_rot_out || mapped(a->q_rot_out, &drot))) {
+      qxc_decode_args d = *a;
+      d.q = dq;
+      d.k = dk;
+      d.v = dv;
+      d.out = dout;
+      d.q_rot_out = static_cast<float*>(drot);
+      qxc_status st = qxc_decode(ctx, kv, &d);
+      if (st != QXC_OK) return st;
+      return qxc_sync(ctx);
+    }
+  }
   qxc_status st = stage_reserve(ctx, total);
   if (st != QXC_OK) return st;
-  // Straight from the caller's buffers: pinned host memory goes by DMA with
-  // no host-side copy; pageable memory is staged by the driver (the copy
-  // still completes in stream order, so the result is the same).
+  // Other host memory: copies from the caller's buffers (pinned memory goes
+  // by DMA with no host-side copy; pageable memory is staged by the driver;
+  // either way the copy completes in stream order).
   QXC_CUDA(ctx, cudaMemcpyAsync(ctx->stage_dev, a->q, qb, cudaMemcpyHostToDevice, ctx->stream));
   QXC_CUDA(ctx, cudaMemcpyAsync(ctx->stage_dev + off_k, a->k, kb, cudaMemcpyHostToDevice, ctx->stream));
   QXC_CUDA(ctx, cudaMemcpyAsync(ctx->stage_dev + off_v, a->v, kb, cudaMemcpyHostToDevice, ctx->stream));

@@ -362,3 +362,40 @@ def test_partials_merge_equals_whole(gpu_ctx, model, shards):
     gk, _ = arenas[-1].read(0, 0, arenas[-1].len(0) - 1, 1)
     wk, _ = whole.read(0, 0, L - 1, 1)
     assert np.array_equal(gk, wk)
+
+
+@pytest.mark.parametrize("model", [MODEL_GRANITE, MODEL_QWEN3])
+def test_decode_host_pinned_buffers_in_place(gpu_ctx, model):
+    """qxc_decode_host with pinned, device-addressable host buffers (torch's
+    pin_memory): the kernels read q/k/v and write the outputs over PCIe in
+    place; the result equals the device-buffer decode bit for bit, rows too."""
+    import torch
+    layers, prefix = 3, 700
+    qwen = model == MODEL_QWEN3
+    hq, hkv, d = (32, 4, 128) if qwen else (16, 8, 64)
+    dt = BF16 if qwen else F32
+    conv = (lambda x: syn.to_bf16_bits(x).view(np.int16)) if qwen else (lambda x: x)
+    kc = conv(syn.normal(0x9A00, (layers, prefix, hkv, d)))
+    vc = conv(syn.normal(0x9A01, (layers, prefix, hkv, d)))
+    arenas = []
+    for _ in range(2):
+        a = KvArena(gpu_ctx, model, layers, 1, prefix + 8, dt, dt)
+        for l in range(layers):
+            a.write(0, l, 0, kc[l], vc[l])
+        a.set_len(0, prefix)
+        arenas.append(a)
+    q = torch.from_numpy(conv(syn.normal(0x9A02, (1, layers, hq * d))))
+    k = torch.from_numpy(conv(syn.normal(0x9A03, (1, layers, hkv * d))))
+    v = torch.from_numpy(conv(syn.normal(0x9A04, (1, layers, hkv * d))))
+    pq, pk, pv = q.pin_memory(), k.pin_memory(), v.pin_memory()
+    pout = torch.zeros(layers, hq * d).pin_memory()
+    host = (lambda t: t.numpy()[0].view(np.uint16)) if qwen else (lambda t: t.numpy()[0])  # views of the pinned memory
+    arenas[0].decode_host(host(pq), host(pk), host(pv), [prefix], out=pout.numpy())
+    dev_out = torch.zeros(1, layers, hq * d, device="cuda")
+    arenas[1].decode(q.cuda(), k.cuda(), v.cuda(), dev_out, [prefix])
+    gpu_ctx.sync()
+    assert torch.equal(pout, dev_out[0].cpu())
+    for l in range(layers):
+        ak, av = arenas[0].read(0, l, 0, prefix + 1)
+        bk, bv = arenas[1].read(0, l, 0, prefix + 1)
+        assert np.array_equal(ak, bk) and np.array_equal(av, bv)
