@@ -585,7 +585,46 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p) {
       if (mine > 0) {
         // scores: lane (row r0+trow, heads hq0..hq0+QPL-1), 4 partial sums
         float sc[QPL];
-        if (trow < mine) {
+        if constexpr (G == 2) {
+          // a group of two heads: each half-warp takes half the dims of its
+          // 16 rows for both heads, so a K element is loaded (and widened
+          // from 16 bits) once instead of once per head; one shuffle joins
+          // the halves, after which lane (row, half) keeps head `half`
+          const int dh = lane >> 4;
+          float part[2][4];
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) part[j][u] = 0.0f;
+          if (trow < mine) {
+            constexpr int VEC = Vec16<KT>::N;
+#pragma unroll
+            for (int i = 0; i < D / 2; i += VEC) {
+              const int d0 = dh * (D / 2) + i;
+              float kf[VEC];
+              Vec16<KT>::load(reinterpret_cast<const KT*>(kt + swz<C::BOX>(r0 + trow, d0 * (int)sizeof(KT))), kf);
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                const float* qrow = &q_s[j * D + d0];
+#pragma unroll
+                for (int v4 = 0; v4 < VEC; v4 += 4) {
+                  const float4 qv = *reinterpret_cast<const float4*>(qrow + v4);
+                  part[j][0] = fmaf(qv.x, kf[v4], part[j][0]);
+                  part[j][1] = fmaf(qv.y, kf[v4 + 1], part[j][1]);
+                  part[j][2] = fmaf(qv.z, kf[v4 + 2], part[j][2]);
+                  part[j][3] = fmaf(qv.w, kf[v4 + 3], part[j][3]);
+                }
+              }
+            }
+          }
+          float s2[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float h = (part[j][0] + part[j][1]) + (part[j][2] + part[j][3]);
+            s2[j] = h + __shfl_xor_sync(0xffffffffu, h, 16);  // dims of both halves: same sum in both lanes
+          }
+          sc[0] = trow < mine ? (dh == 0 ? s2[0] : s2[1]) * M::SCALE : -INFINITY;
+        } else if (trow < mine) {
           float part[QPL][4];
 #pragma unroll
           for (int j = 0; j < QPL; ++j)
