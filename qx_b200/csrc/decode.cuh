@@ -608,11 +608,16 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p) {
                 const float* qrow = &q_s[j * D + d0];
 #pragma unroll
                 for (int v4 = 0; v4 < VEC; v4 += 4) {
+                  // the four chains in pairs, one packed fma per pair (same roundings)
                   const float4 qv = *reinterpret_cast<const float4*>(qrow + v4);
-                  part[j][0] = fmaf(qv.x, kf[v4], part[j][0]);
-                  part[j][1] = fmaf(qv.y, kf[v4 + 1], part[j][1]);
-                  part[j][2] = fmaf(qv.z, kf[v4 + 2], part[j][2]);
-                  part[j][3] = fmaf(qv.w, kf[v4 + 3], part[j][3]);
+                  const float2 lo = __ffma2_rn(make_float2(qv.x, qv.y), make_float2(kf[v4], kf[v4 + 1]),
+                                               make_float2(part[j][0], part[j][1]));
+                  const float2 hi = __ffma2_rn(make_float2(qv.z, qv.w), make_float2(kf[v4 + 2], kf[v4 + 3]),
+                                               make_float2(part[j][2], part[j][3]));
+                  part[j][0] = lo.x;
+                  part[j][1] = lo.y;
+                  part[j][2] = hi.x;
+                  part[j][3] = hi.y;
                 }
               }
             }
@@ -701,11 +706,13 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p) {
             const float* prow = &Pw[tt * G];
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-              const float pw = prow[g];
-              acc[g][0] = fmaf(pw, v4.x, acc[g][0]);
-              acc[g][1] = fmaf(pw, v4.y, acc[g][1]);
-              acc[g][2] = fmaf(pw, v4.z, acc[g][2]);
-              acc[g][3] = fmaf(pw, v4.w, acc[g][3]);
+              const float2 pw = make_float2(prow[g], prow[g]);
+              const float2 lo = __ffma2_rn(pw, make_float2(v4.x, v4.y), make_float2(acc[g][0], acc[g][1]));
+              const float2 hi = __ffma2_rn(pw, make_float2(v4.z, v4.w), make_float2(acc[g][2], acc[g][3]));
+              acc[g][0] = lo.x;
+              acc[g][1] = lo.y;
+              acc[g][2] = hi.x;
+              acc[g][3] = hi.y;
             }
           }
         } else
