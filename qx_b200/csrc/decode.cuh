@@ -646,10 +646,14 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p) {
 #pragma unroll
               for (int v4 = 0; v4 < VEC; v4 += 4) {
                 const float4 qv = *reinterpret_cast<const float4*>(qrow + v4);
-                part[j][0] = fmaf(qv.x, kf[v4], part[j][0]);
-                part[j][1] = fmaf(qv.y, kf[v4 + 1], part[j][1]);
-                part[j][2] = fmaf(qv.z, kf[v4 + 2], part[j][2]);
-                part[j][3] = fmaf(qv.w, kf[v4 + 3], part[j][3]);
+                const float2 lo = __ffma2_rn(make_float2(qv.x, qv.y), make_float2(kf[v4], kf[v4 + 1]),
+                                             make_float2(part[j][0], part[j][1]));
+                const float2 hi = __ffma2_rn(make_float2(qv.z, qv.w), make_float2(kf[v4 + 2], kf[v4 + 3]),
+                                             make_float2(part[j][2], part[j][3]));
+                part[j][0] = lo.x;
+                part[j][1] = lo.y;
+                part[j][2] = hi.x;
+                part[j][3] = hi.y;
               }
             }
           }
