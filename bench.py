@@ -721,7 +721,8 @@ def run_layer(args, world, rank, local):
         for l in range(LAYERS):
             w = weights[l]
             arena.attention_layer(hidden[l % 2], hidden[(l + 1) % 2], w["norm"], w["q"], w["k"], w["v"], w["o"],
-                                  pos, layer=l, flags=_lib.DECODE_NO_ADVANCE if l + 1 < LAYERS else 0)
+                                  pos, layer=l, flags=_lib.DECODE_NO_ADVANCE if l + 1 < LAYERS else 0,
+                                  split=args.split)
 
     # one step is 72 launches of a few microseconds each: capture a whole
     # cycle of 64 tokens in a CUDA graph and replay it (the host cursor is

@@ -326,6 +326,15 @@ qxc_status qxc_kv_slot_hashes(qxc_ctx* ctx, qxc_kv* kv, int32_t seq, int32_t lay
  * hash kernels are compared against. Synchronous; about 10 ms. */
 qxc_status qxc_blake3_compress_rate(qxc_ctx* ctx, double* compressions_per_second);
 
+/* Consensus-math conformance: for each of n inputs x, out[4i..4i+3] = the
+ * bits of the device's pinned exp_f32(x), rsqrt_f32(x) and the (sin, cos) of
+ * granite_rope_sin_cos((uint32)x, i % 32), quiet NaN 0x7fc00000 where the
+ * function has no value. Host pointers; synchronous. Replaces
+ * MetalContext::run_consensus_math_conformance (qx-metal/src/lib.rs:9622-9690,
+ * kernel kernels/consensus_math.metal:102-112); its test compares these bits
+ * with the CPU functions (qx-metal/src/lib.rs:15488-15511). */
+qxc_status qxc_consensus_math_conformance(qxc_ctx* ctx, const float* inputs, int32_t n, uint32_t* out);
+
 /* ---- causal prefill ------------------------------------------------------ */
 /* Prompt prefill of `length` tokens into an EMPTY (sequence, layer) of a
  * Granite arena (cursor must be 0): RoPE on q and k at positions

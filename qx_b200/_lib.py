@@ -155,6 +155,7 @@ def load() -> C.CDLL:
         "qxc_verification_hashes": (C.c_int, [vp, vp, C.POINTER(VerificationHashArgs)]),
         "qxc_kv_slot_hashes": (C.c_int, [vp, vp, i32, i32, i32, i32, i32, vp, i32]),
         "qxc_blake3_compress_rate": (C.c_int, [vp, C.POINTER(C.c_double)]),
+        "qxc_consensus_math_conformance": (C.c_int, [vp, vp, C.c_int32, vp]),
         "qxc_granite_decode_static_scratch": (C.c_int, [C.POINTER(StaticDecodeArgs), vp, C.c_char_p, C.c_size_t]),
     }
     for name, (res, args) in sig.items():

@@ -2007,6 +2007,50 @@ qxc_status qxc_kv_slot_hashes(qxc_ctx* ctx, qxc_kv* kv, int32_t seq, int32_t lay
                      kHashSerialWarps);
 }
 
+// One thread per input: the pinned exp, rsqrt and Granite RoPE (sin, cos)
+// of the input as raw bits, the RoPE position being the input truncated to
+// an unsigned integer and the pair the thread index mod 32. Quiet NaN
+// (0x7fc00000) where the pinned function has no value.
+static __global__ void qx_consensus_math_kernel(const float* in, int n, uint4* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float x = in[i];
+  const unsigned nan_bits = 0x7fc00000u;
+  uint4 r;
+  r.x = isfinite(x) ? __float_as_uint(qx::pinned_exp(x)) : nan_bits;
+  float v = 0.0f;
+  r.y = qx::pinned_rsqrt(x, &v) ? __float_as_uint(v) : nan_bits;
+  float s = 0.0f, c = 0.0f;
+  if (qx::granite_sin_cos(__float2uint_rz(x), i & 31, &s, &c)) {
+    r.z = __float_as_uint(s);
+    r.w = __float_as_uint(c);
+  } else {
+    r.z = r.w = nan_bits;
+  }
+  out[i] = r;
+}
+
+qxc_status qxc_consensus_math_conformance(qxc_ctx* ctx, const float* inputs, int32_t n, uint32_t* out) {
+  if (!ctx || n < 0 || (n > 0 && (!inputs || !out))) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (n == 0) return QXC_OK;
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  float* din = nullptr;
+  uint4* dout = nullptr;
+  QXC_CUDA(ctx, cudaMalloc(&din, sizeof(float) * n));
+  cudaError_t e = cudaMalloc(&dout, sizeof(uint4) * n);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(din, inputs, sizeof(float) * n, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) {
+    qx_consensus_math_kernel<<<(n + 255) / 256, 256, 0, ctx->stream>>>(din, n, dout);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out, dout, sizeof(uint4) * n, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  cudaFree(din);
+  cudaFree(dout);
+  QXC_CUDA(ctx, e);
+  return QXC_OK;
+}
+
 qxc_status qxc_blake3_compress_rate(qxc_ctx* ctx, double* per_second) {
   if (!ctx || !per_second) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
   QXC_CUDA(ctx, cudaSetDevice(ctx->device));

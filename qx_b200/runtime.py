@@ -119,6 +119,18 @@ class Context:
         self.check(self.lib.qxc_blake3_compress_rate(self.handle, C.byref(r)))
         return r.value
 
+    def run_consensus_math_conformance(self, inputs) -> list:
+        """Raw bits [exp, rsqrt, rope sin, rope cos] of the device's pinned
+        math per input (qx-metal/src/lib.rs:9622, the Metal context's
+        conformance dispatch); the RoPE position is the input truncated to
+        u32 and the pair its index mod 32. Quiet NaN bits where the CPU
+        function returns None."""
+        x = np.ascontiguousarray(inputs, dtype=np.float32)
+        out = np.zeros((x.size, 4), dtype=np.uint32)
+        self.check(self.lib.qxc_consensus_math_conformance(
+            self.handle, x.ctypes.data_as(C.c_void_p), int(x.size), out.ctypes.data_as(C.c_void_p)))
+        return [tuple(int(v) for v in row) for row in out]
+
     def lse_merge(self, model: int, n_parts: int, partials, out, out_dtype: int = F32) -> None:
         self.check(self.lib.qxc_lse_merge(self.handle, model, n_parts, _ptr(partials), _ptr(out), out_dtype))
 
