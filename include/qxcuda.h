@@ -158,6 +158,14 @@ qxc_status qxc_kv_trim(qxc_kv* kv, int32_t seq);
 qxc_status qxc_kv_pool_buffer(qxc_kv* kv, int32_t key, void** device_ptr, size_t* bytes);
 
 /* ---- decode ------------------------------------------------------------ */
+/* Stream ordering. Every kernel here is launched as a programmatic
+ * dependent of the stream's previous kernel. A single-sequence decode on a
+ * contiguous Qwen arena may start reading cached rows before the previous
+ * kernel has finished: it reads only rows that no earlier launch of this
+ * context can still be writing. A caller that writes the arena with its own
+ * kernel on the same stream must not launch that kernel with programmatic
+ * stream serialization and trigger its dependents before the writes (plain
+ * launches, copies and events need nothing). */
 /* One token step for `seq_count` sequences over layers
  * [layer_begin, layer_begin + layer_count). Per (sequence, layer): RoPE on
  * q and k at `position` (Qwen: per-head RMSNorm first), append k/v into slot

@@ -113,7 +113,13 @@ struct DecodeParams {
   int pinned_exp;
   int emit_partials;  // write (O, m, l) per query head instead of O / l
   int external_merge;  // splits only store partials; qx_split_merge_kernel merges them
-  int early_trigger;   // one-wave grid: let the next grid launch at once (griddepcontrol)
+  int early_trigger;   // one-wave grid: let the next grid launch early (griddepcontrol)
+  // Single-sequence calls (seq_table == nullptr) on a contiguous arena:
+  // cache rows [0, pre_rows) of the sequence were written by grids that have
+  // completed, so the tensor-core decode may stream them before
+  // griddepcontrol.wait (0: none). The host derives it from the launches it
+  // made on the stream (note_rows_written).
+  int pre_rows;
   float* partials;    // scratch [items][G][D+2]
   int* tickets;       // scratch [n_seq][layer_count][HKV], zero between calls
   unsigned* err;
@@ -376,7 +382,10 @@ __device__ __forceinline__ void finish_outputs(const DecodeParams& p, const floa
 template <class M, typename KT, typename VT>
 __device__ __forceinline__ void decode_body(const DecodeParams& p) {
   using C = DecodeCfg<M, KT, VT>;
-  if (p.early_trigger) pdl_launch_dependents();  // the merge grid may get resident meanwhile
+  // A one-wave grid lets the next grid (the merge, or the next call) get
+  // resident at once. Launches on the stream after this grid may therefore
+  // overlap the grids before it; the host knows (note_rows_written).
+  if (p.early_trigger) pdl_launch_dependents();
   constexpr int D = M::D, G = M::G, HKV = M::HKV, HQ = M::HQ, T = C::T, NWC = C::NWC, WT = C::WT;
   constexpr int QPL = C::QPL, DPL = C::DPL, STAGES = C::STAGES;
   extern __shared__ __align__(1024) unsigned char sm_raw[];

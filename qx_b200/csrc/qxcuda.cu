@@ -58,6 +58,17 @@ struct qxc_ctx {
   size_t stage_cap = 0;
   unsigned long long launches = 0;
   int last_split = 0;
+  // Which cache rows a grid launched now may find still being written.
+  // A grid that triggers its dependents only after its own
+  // griddepcontrol.wait (or at its end) has all grids before it complete by
+  // the time any later grid starts. Since the last such grid on the stream:
+  // kvw_open = some grid that writes rows triggered early (any row may still
+  // be written); else kvw_arena = the arena written (null: none), kvw_seq
+  // its sequence (-1: several) and kvw_row the lowest row written.
+  bool kvw_open = false;
+  const void* kvw_arena = nullptr;
+  int kvw_seq = -1;
+  int kvw_row = 0;
   // Qwen RoPE (cos, sin) for every position 0..kQwenMaxPositions-1, shared
   // by all Qwen arenas of this context (created with the first one).
   float2* qwen_rope = nullptr;
@@ -479,6 +490,26 @@ qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* s
   return QXC_OK;
 }
 
+// Rows [0, result) of `seq` no running grid can be writing.
+int rows_settled(const qxc_ctx* ctx, const qxc_kv* kv, int seq) {
+  if (ctx->kvw_open) return 0;
+  if (ctx->kvw_arena != kv || (ctx->kvw_seq >= 0 && ctx->kvw_seq != seq)) return kv->desc.capacity;
+  return ctx->kvw_row;
+}
+
+// Record a grid that triggers its dependents only after its wait (or at its
+// end) and wrote rows >= row_lo of `seq` (-1: several) of kv (kv null: none).
+void note_rows_written(qxc_ctx* ctx, const qxc_kv* kv, int seq, int row_lo) {
+  ctx->kvw_open = false;
+  ctx->kvw_arena = kv;
+  ctx->kvw_seq = seq;
+  ctx->kvw_row = row_lo;
+}
+
+// Record a grid that may write rows and triggers its dependents before its
+// wait: until the next grid that waits first, any row may be in flight.
+void note_rows_open(qxc_ctx* ctx) { ctx->kvw_open = true; }
+
 qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer_begin, int layer_count,
                        DecodeParams* p) {
   memset(p, 0, sizeof(*p));
@@ -516,6 +547,21 @@ qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer
   // a one-wave grid lets the next grid (the merge, or the next call) get
   // resident while it runs
   p->early_trigger = one_wave ? 1 : 0;
+  // a single contiguous sequence may stream its settled rows before the wait
+  if (plan.tab.size() == 1 && !kv->paged()) p->pre_rows = rows_settled(ctx, kv, plan.tab[0].seq_id);
+  if (kv->desc.model == QXC_MODEL_GRANITE) {
+    // the CUDA-core kernels trigger at their start (measured faster for
+    // them) and stream nothing before their wait
+    note_rows_open(ctx);
+  } else {
+    // the tensor-core decode triggers after its wait: it is now the only
+    // grid that may still write rows (its new slots), or none
+    int lo = kv->desc.capacity;
+    for (const SeqInfo& si : plan.tab)
+      if (si.new_slot >= 0) lo = std::min(lo, si.new_slot);
+    if (lo < kv->desc.capacity) note_rows_written(ctx, kv, plan.tab.size() == 1 ? plan.tab[0].seq_id : -1, lo);
+    else note_rows_written(ctx, nullptr, -1, 0);
+  }
   return QXC_OK;
 }
 
@@ -1451,6 +1497,7 @@ qxc_status qxc_decode_verify(qxc_ctx* ctx, qxc_kv* kv, const qxc_verify_args* a)
   else if (kd == QXC_F16 && vd == QXC_F16) st = launch_append<Granite, __half, __half>(ctx, ap, grid);
   else st = launch_append<Granite, __nv_bfloat16, __nv_bfloat16>(ctx, ap, grid);
   if (st != QXC_OK) return st;
+  note_rows_written(ctx, kv, a->seq, a->start);
   // 2. token t attends [0, start + t]
   if (kv->desc.model == QXC_MODEL_GRANITE && a->tokens >= 2 && a->tokens <= GraniteVerify4::NTOK &&
       !(a->flags & QXC_VERIFY_PER_TOKEN)) {
@@ -1909,6 +1956,7 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
   p.trace = tr.buf;
   qx_prefill_rope_kernel<<<(a->length + kRopePositions - 1) / kRopePositions, 256, 0, ctx->stream>>>(p);
   QXC_CUDA(ctx, cudaGetLastError());
+  note_rows_written(ctx, kv, a->seq, 0);
   // the attention grid is a programmatic dependent of the RoPE grid: its CTAs
   // initialise barriers and TMEM while the RoPE grid drains, and wait for it
   // (griddepcontrol.wait) before the first TMA load

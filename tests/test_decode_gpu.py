@@ -327,6 +327,46 @@ def test_qwen_config3_full_length(gpu_ctx, oracle):
     assert np.array_equal(gk.reshape(-1), kr)
 
 
+@pytest.mark.parametrize("alternate", [False, True])
+def test_qwen_back_to_back_steps(gpu_ctx, oracle, alternate):
+    """Decode steps queued back to back with no host sync. Each step's grid
+    streams the rows that no running grid can still write before its
+    griddepcontrol.wait. On one sequence, that excludes the row the previous
+    step appended. With two sequences in turn, it covers every tile, and the
+    new row is patched in after the copy."""
+    import torch
+    prefix, cap, steps = 1500, 1600, 6
+    nseq = 2 if alternate else 1
+    arena = KvArena(gpu_ctx, MODEL_QWEN3, 1, nseq, cap, BF16, BF16)
+    ref_caches = []
+    for sq in range(nseq):
+        _, _, _, kc, vc = qwen_case(0x7100 + sq, prefix, cap)
+        arena.write(sq, 0, 0, kc[:prefix], vc[:prefix])
+        arena.set_len(sq, prefix)
+        ref_caches.append((kc.copy(), vc.copy()))
+    ones = np.ones(128, np.float32)
+    dev = lambda a: torch.from_numpy(a.view(np.int16).reshape(1, -1)).cuda()
+    outs, refs = [], []
+    pos = [prefix] * nseq
+    for i in range(steps):
+        sq = i % nseq
+        q, k, v, _, _ = qwen_case(0x7200 + i, 0, 1)
+        okc, ovc = ref_caches[sq]
+        _, _, ref, _ = oracle.qwen_decode(q, k, v, ones, ones, okc, ovc, pos[sq], BF16, threads=8)
+        out = torch.zeros(1, 4096, device="cuda")
+        arena.decode(dev(q), dev(k), dev(v), out, [pos[sq]], seq_ids=[sq], split=128)
+        outs.append(out)
+        refs.append(ref)
+        pos[sq] += 1
+    gpu_ctx.sync()
+    for i in range(steps):
+        assert normwise(outs[i].cpu().numpy()[0], refs[i]) <= 2e-3, i
+    for sq in range(nseq):
+        gk, gv = arena.read(sq, 0, 0, pos[sq])
+        assert np.array_equal(gk.reshape(pos[sq], -1), ref_caches[sq][0][:pos[sq]].reshape(pos[sq], -1))
+        assert np.array_equal(gv.reshape(pos[sq], -1), ref_caches[sq][1][:pos[sq]].reshape(pos[sq], -1))
+
+
 # ---- KV-length split partials + LSE merge ---------------------------------------------
 @pytest.mark.parametrize("model", [MODEL_GRANITE, MODEL_QWEN3])
 @pytest.mark.parametrize("shards", [2, 3])

@@ -25,7 +25,9 @@ def position_of(x: np.float32) -> int:
     """Rust's saturating `value as u32` (and PTX cvt.rzi.u32.f32)."""
     if math.isnan(x) or x <= 0:
         return 0
-    return int(min(math.floor(float(x)), 0xFFFFFFFF))
+    if x >= 4294967295.0:
+        return 0xFFFFFFFF
+    return int(math.floor(float(x)))
 
 
 def expected(oracle, inputs):
