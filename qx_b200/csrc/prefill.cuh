@@ -62,6 +62,7 @@ struct PrefillParams {
   int out_dtype;
   int length;
   int nqb;  // query blocks of 64 positions
+  int early_trigger;  // the RoPE grid is resident all at once: let the attention grid launch at its start
   const float2* rope;  // pinned (sin, cos) [4096 positions][32 pairs]
   unsigned* err;
   unsigned long long* trace;  // stage timeline (diagnostics), or null
@@ -90,6 +91,10 @@ __global__ void __launch_bounds__(256) qx_prefill_rope_kernel(const __grid_const
   constexpr int ITEMS = kRopePositions * 160;
   constexpr int PER_THREAD = (ITEMS + 255) / 256;
   __shared__ float s_sin[kRopePositions][32], s_cos[kRopePositions][32];
+  // With every RoPE CTA resident at once, the attention grid may launch now:
+  // its CTAs take each SM as its RoPE CTAs drain and wait for this grid in
+  // griddepcontrol.wait (L = 2048: 31.4 -> 30.9 us per call; 512: 13.1 -> 12.5).
+  if (p.early_trigger) pdl_launch_dependents();
   const int tid = threadIdx.x;
   const int pos0 = blockIdx.x * kRopePositions;
   uint4 lo[PER_THREAD], hi[PER_THREAD];
@@ -144,9 +149,9 @@ __global__ void __launch_bounds__(256) qx_prefill_rope_kernel(const __grid_const
       reinterpret_cast<uint4*>(p.v_cache + (long long)pos * 512)[w - 96] = lo[k];
     }
   }
-  // Only now may the attention grid start: its CTAs fill every SM's
-  // registers, so an earlier start would starve the remaining RoPE CTAs.
-  pdl_launch_dependents();
+  // Otherwise only now: the attention CTAs fill every SM's registers, so an
+  // earlier start would starve the RoPE CTAs not yet resident.
+  if (!p.early_trigger) pdl_launch_dependents();
 }
 
 struct PrefillCfg {

@@ -1952,9 +1952,18 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
                                        PrefillCfg::SMEM));
     configured |= bit;
   }
+  const int rope_grid = (a->length + kRopePositions - 1) / kRopePositions;
+  {
+    static int rope_slots[64] = {};  // resident RoPE CTAs per SM, by device
+    int& per_sm = rope_slots[ctx->device & 63];
+    if (!per_sm && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qx_prefill_rope_kernel, 256, 0) !=
+                        cudaSuccess || per_sm < 1))
+      per_sm = 1;
+    p.early_trigger = rope_grid <= per_sm * ctx->sm_count ? 1 : 0;
+  }
   TraceRun tr(ctx, "prefill", (size_t)nqb * 8 * 3);  // softmax timeline, then the two MMA issuers'
   p.trace = tr.buf;
-  qx_prefill_rope_kernel<<<(a->length + kRopePositions - 1) / kRopePositions, 256, 0, ctx->stream>>>(p);
+  qx_prefill_rope_kernel<<<rope_grid, 256, 0, ctx->stream>>>(p);
   QXC_CUDA(ctx, cudaGetLastError());
   note_rows_written(ctx, kv, a->seq, 0);
   // the attention grid is a programmatic dependent of the RoPE grid: its CTAs
