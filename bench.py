@@ -36,6 +36,9 @@ sys.path.insert(0, ROOT)
 LAYERS = 24
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
+# nominal B200 peaks, the denominators the north star quotes beside the measured ones
+NOMINAL_HBM_GBS = 8000.0
+NOMINAL_BF16_TFLOPS = 2250.0
 
 
 def hbm_peak():
@@ -285,6 +288,7 @@ def run_config1(args, world, rank, local):
         "hbm_gbs": achieved_gbs,
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                      "frac": achieved_gbs / peak, "peak_kind": peak_kind,
+                     "frac_of_nominal": achieved_gbs / NOMINAL_HBM_GBS,
                      "traffic": traffic["bytes_per_launch"] if traffic else None,
                      "kernel": "qx_decode_kernel<Granite,float,float>",
                      "algorithmic_bytes_per_launch": avg_bytes, "avg_launch_us": avg_kernel_s * 1e6},
@@ -385,7 +389,7 @@ def hbm_roofline(bytes_per_launch, per_ms, kernel, workload=None):
     ach = bytes_per_launch / (float(np.mean(per_ms)) / 1e3) / 1e9
     tr = profile_traffic(workload) if workload else None
     return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": kind,
-            "traffic": (tr["dram_read"] + tr["dram_write"]) if tr else None, "kernel": kernel,
+            "frac_of_nominal": ach / NOMINAL_HBM_GBS, "traffic": (tr["dram_read"] + tr["dram_write"]) if tr else None, "kernel": kernel,
             "algorithmic_bytes_per_launch": bytes_per_launch, "avg_launch_us": float(np.mean(per_ms)) * 1e3}
 
 
@@ -527,7 +531,7 @@ def run_config2(args, world, rank, local):
                       "timing": "20 calls per CUDA graph replay",
                       "flops_per_step": flops}, clk, launches)
     line["roofline"] = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                        "peak_kind": kind,
+                        "peak_kind": kind, "frac_of_nominal": ach / NOMINAL_BF16_TFLOPS,
                         "traffic": (lambda t: t["dram_read"] + t["dram_write"] if t else None)(
                             profile_traffic(f"config2_l{L}")),
                         "kernel": "qx_prefill_rope_kernel + qx_prefill_attn_tc_kernel (timed together)",
