@@ -25,6 +25,18 @@
 // Prologue (RMSNorm with the reference's sequential sum, rotate-half RoPE
 // from the host cos/sin table, the appended row) and the split merge are
 // those of qx_decode_kernel (tools/qx-qwen-parity/src/main.rs:1170-1258).
+//
+// Granite with a 16-bit cache (group 2, head_dim 64) runs the same kernel
+// on a pair of adjacent kv heads as one 128-dim unit: the K tile holds head
+// 2u in dims 0-63 and head 2u+1 in dims 64-127, and Q^T is block-diagonal
+// (query heads 4u, 4u+1 nonzero in dims 0-63 only, 4u+2, 4u+3 in dims
+// 64-127 only), so one S^T MMA gives each query head its own kv head's
+// scores. O^T = V^T.P^T then holds every (dim, head) product; each head's
+// output is its own kv head's half of the dims and the rest is never read.
+// The prologue is Granite's: qx's pinned RoPE (granite_rotate) on q and k,
+// q rounded to the operand type for the MMA. This takes both contractions
+// off the CUDA cores for the bf16 / f16 Granite caches (configs 1-4 with
+// 16-bit KV); the fp32 cache stays on qx_decode_kernel.
 #pragma once
 #include <type_traits>
 
@@ -33,10 +45,24 @@
 
 namespace qx {
 
-template <typename KT>
+// One work unit's geometry. D: dims of a unit's K/V row (MMA K of S, M of
+// P.V); G: query heads per unit; UNITS: units per layer; HEAD_D: dims of
+// one head; KV_PER_UNIT: kv heads in a unit.
+struct TcQwen {
+  static constexpr bool GRANITE = false;
+  static constexpr int D = 128, G = 8, UNITS = 4, HQ = 32, HEAD_D = 128, KV_PER_UNIT = 1;
+  static constexpr float SCALE_LOG2 = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
+};
+struct TcGranitePair {
+  static constexpr bool GRANITE = true;
+  static constexpr int D = 128, G = 4, UNITS = 4, HQ = 16, HEAD_D = 64, KV_PER_UNIT = 2;
+  static constexpr float SCALE_LOG2 = 0.015625f * 1.4426950408889634f;  // 1/64 * log2(e)
+};
+
+template <typename KT, class TM = TcQwen>
 struct TcCfg {
   static constexpr int T = 128;  // cache rows per tile
-  static constexpr int D = 128, G = 8, HKV = 4, HQ = 32;
+  static constexpr int D = TM::D, G = TM::G, HKV = TM::UNITS, HQ = TM::HQ;
   static constexpr int NPAD = 16;        // MMA N (8 heads + 8 zero rows)
   static constexpr int BLK = T * 128;    // one 64-dim column block [128 rows][128 B]
   static constexpr int STAGE = 2 * BLK;  // K (or V) of one tile: 32 KB
@@ -65,9 +91,9 @@ struct TcCfg {
   static constexpr int PRE = 1;
 };
 
-template <typename KT>
+template <typename KT, class TM = TcQwen>
 __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_constant__ DecodeParams p) {
-  using C = TcCfg<KT>;
+  using C = TcCfg<KT, TM>;
   constexpr int D = C::D, G = C::G, HKV = C::HKV, HQ = C::HQ, T = C::T, NS = C::NS;
   extern __shared__ __align__(1024) unsigned char sm_raw[];
   unsigned char* sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
@@ -119,7 +145,7 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
 
   // Tile t of this CTA's split, K (lane 0) or V (lane 1): 4 boxes of
   // [64 rows][128 B] into ring stage t % NS, completing on its full barrier.
-  auto issue_tile = [&](int t, int seq_id, int layer, int h, int begin) {
+  auto issue_tile = [&](int t, int seq_id, int layer, int h, int begin, int end) {
     const CUtensorMap* map = lane == 0 ? &p.tmk : &p.tmv;
     uint64_t* full = lane == 0 ? kfull : vfull;
     unsigned char* ring = sm + (lane == 0 ? C::OFF_K : C::OFF_V);
@@ -127,10 +153,17 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
     mbar_arrive_expect_tx(&full[st], (uint32_t)C::STAGE);
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-      const int z = (int)kv_row(p.paging, p.capacity, p.layers, seq_id, layer, begin + t * T + half * 64);
+      // a box with no row of the split (the second half of a last tile of at
+      // most 64 rows) reads the fill value from outside the tensor instead of
+      // looking up a page past the sequence's block table
+      const int slot = begin + t * T + half * 64;
+      const int z = slot < end ? (int)kv_row(p.paging, p.capacity, p.layers, seq_id, layer, slot) : -128;
 #pragma unroll
-      for (int b = 0; b < 2; ++b)
-        tma_load_3d(ring + st * C::STAGE + b * C::BLK + half * 8192, map, b * 64, h, z, &full[st]);
+      for (int b = 0; b < 2; ++b) {
+        // column block b: dims 64b.. of the kv head (Qwen), or kv head 2h+b (Granite pair)
+        const int x = TM::KV_PER_UNIT == 1 ? b * 64 : 0, y = TM::KV_PER_UNIT == 1 ? h : 2 * h + b;
+        tma_load_3d(ring + st * C::STAGE + b * C::BLK + half * 8192, map, x, y, z, &full[st]);
+      }
     }
   };
   // The first C::PRE tiles, if all their rows lie below pre_rows, stream
@@ -148,7 +181,7 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
     const int n0 = (e0 - b0 + T - 1) / T;
     prefetch_tmap(lane == 0 ? &p.tmk : &p.tmv);
     while (npre < C::PRE && npre < n0 && min(b0 + (npre + 1) * T, e0) <= p.pre_rows) {
-      issue_tile(npre, s0.seq_id, p.layer_begin + l0, h0, b0);
+      issue_tile(npre, s0.seq_id, p.layer_begin + l0, h0, b0, e0);
       ++npre;
     }
   }
@@ -191,7 +224,7 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
       ok &= mbar_wait_bounded(loaded, 0, p.err);
       for (int t = npre; t < ntiles; ++t) {
         if (t >= NS) ok &= mbar_wait_bounded(&empty[t % NS], (uint32_t)(t / NS - 1) & 1u, p.err);
-        issue_tile(t, si.seq_id, layer, h, begin);
+        issue_tile(t, si.seq_id, layer, h, begin, end);
       }
       // no copy may still be landing when the CTA exits
       for (int t = ntiles > NS ? ntiles - NS : 0; t < ntiles; ++t)
@@ -246,75 +279,128 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
     if (!ok) s_flag[1] = 1;
   } else {
     // ---- consumers: prologue, one round of global loads --------------------
-    const long long qbase = (cu * HQ + (long long)h * G) * D;
-    const long long kvbase = (cu * HKV + h) * D;
-    const int pi = tid & 63;  // the rotation pair of every prologue item of this thread
-    // all of this thread's prologue inputs in flight at once: dim tid of the
-    // G query rows (and of the new key row), its RoPE pair, norm weights, new v
-    float qv[G], kn = 0.0f, vnew = 0.0f;
-    load_any_n<G>(p.q, qbase + tid, D, p.q_dtype, qv);
-    if (has_new) {
-      load_any_n<1>(p.k, kvbase + tid, 0, p.in_dtype, &kn);
-      load_any_n<1>(p.v, kvbase + tid, 0, p.in_dtype, &vnew);
-    }
-    const float2 cssn = p.rope_table[(long long)si.rope_pos * 64 + pi];
-    const float wq0 = p.q_norm ? p.q_norm[pi] : 1.0f, wq1 = p.q_norm ? p.q_norm[64 + pi] : 1.0f;
-    const float wk0 = p.k_norm ? p.k_norm[pi] : 1.0f, wk1 = p.k_norm ? p.k_norm[64 + pi] : 1.0f;
-#pragma unroll
-    for (int g = 0; g < G; ++g) raw[g * D + tid] = qv[g];
-    raw[G * D + tid] = kn;
-    {
-      // every load above has landed once its value is used
-      const float sink = cssn.x + wq0 + wq1 + wk0 + wk1 + vnew;
-      asm volatile("" ::"f"(sink));
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(loaded);
-    trace.mark();  // prologue loads landed
-    // zero the padding rows 8..15 of Q and of both P^T buffers (both column blocks)
-    for (int i = tid; i < 6 * 128; i += 128) {
-      const int blk = i >> 7, j = i & 127;  // blk 0,1: Q blocks; 2..5: P blocks
-      unsigned char* base = sm + (blk < 2 ? C::OFF_Q + blk * 2048 : C::OFF_P + (blk - 2) * 2048) + 1024;
-      reinterpret_cast<uint2*>(base)[j] = make_uint2(0u, 0u);
-    }
-    consumers_sync(128);
-    if (tid < G || (tid == G && has_new)) {
-      const float* row = raw + tid * D;
-      float sum = 0.0f;
-#pragma unroll
-      for (int i = 0; i < D; ++i) sum = __fadd_rn(sum, __fmul_rn(row[i], row[i]));
-      st_inv[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 128.0f), 1.0e-6f)));
-    }
-    consumers_sync(128);
-    trace.mark();  // RMS norms
+    const long long qbase = (cu * HQ + (long long)h * G) * TM::HEAD_D;
+    const long long kvbase = (cu * HKV + h) * D;  // the unit's new k/v row
     bool bad = false;
-    for (int idx = tid; idx < (G + 1) * 64; idx += 128) {
-      const int g = idx >> 6;
-      if (g == G && !has_new) break;
-      const bool is_q = g < G;
-      const float inv = st_inv[g];
-      const float x = raw[g * D + pi], y = raw[g * D + pi + 64];
-      const float left = __fmul_rn(__fmul_rn(x, inv), is_q ? wq0 : wk0);
-      const float right = __fmul_rn(__fmul_rn(y, inv), is_q ? wq1 : wk1);
-      const float a = __fsub_rn(__fmul_rn(left, cssn.x), __fmul_rn(right, cssn.y));
-      const float b = __fadd_rn(__fmul_rn(right, cssn.x), __fmul_rn(left, cssn.y));
-      bad |= !(isfinite(a) && isfinite(b));
-      const KT ka = Elem<KT>::from_f32(a), kb = Elem<KT>::from_f32(b);
-      if (is_q) {
-        // Q row g (K-major, 128-byte swizzle): dims pi and pi+64 in blocks 0 and 1
-        const int c = pi >> 3, off = (pi & 7) * 2;
-        *reinterpret_cast<KT*>(sm + C::OFF_Q + g * 128 + ((c ^ (g & 7)) << 4) + off) = ka;
-        *reinterpret_cast<KT*>(sm + C::OFF_Q + 2048 + g * 128 + ((c ^ (g & 7)) << 4) + off) = kb;
-        if (p.q_rot_out && last_split) {
-          p.q_rot_out[qbase + g * D + pi] = Elem<KT>::to_f32(ka);
-          p.q_rot_out[qbase + g * D + pi + 64] = Elem<KT>::to_f32(kb);
+    if constexpr (TM::GRANITE) {
+      // thread t: rotation pair i of query head slot j (and of kv head slot
+      // j < 2 of the new key); dim t of the new value row
+      const int j = tid >> 5, i = tid & 31;
+      const long long qa = qbase + j * 64 + i;
+      const float ql = load_any(p.q, qa, p.q_dtype), qr = load_any(p.q, qa + 32, p.q_dtype);
+      float kl = 0.0f, kr = 0.0f, vnew = 0.0f;
+      if (has_new) {
+        if (tid < 64) {
+          kl = load_any(p.k, kvbase + j * 64 + i, p.in_dtype);
+          kr = load_any(p.k, kvbase + j * 64 + i + 32, p.in_dtype);
         }
-      } else {
-        newk[pi] = ka;
-        newk[pi + 64] = kb;
+        vnew = load_any(p.v, kvbase + tid, p.in_dtype);
       }
+      {
+        const float sink = ql + qr + kl + kr + vnew;  // every load above has landed
+        asm volatile("" ::"f"(sink));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(loaded);
+      trace.mark();  // prologue loads landed
+      // Q^T is block-diagonal: zero all of it, and the padding rows G..15 of
+      // both P^T buffers (both column blocks)
+      for (int w = tid; w < 256 + 4 * (16 - G) * 8; w += 128) {
+        unsigned char* dst = w < 256 ? sm + C::OFF_Q + w * 16
+                                     : sm + C::OFF_P + ((w - 256) / ((16 - G) * 8)) * 2048 + G * 128 +
+                                           ((w - 256) % ((16 - G) * 8)) * 16;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      consumers_sync(128);
+      trace.mark();  // (no norms)
+      float sn = 0.f, cs = 0.f, a = 0.f, b = 0.f;
+      bool ok = granite_sin_cos((uint32_t)si.rope_pos, i, &sn, &cs) && granite_rotate(ql, qr, sn, cs, &a, &b);
+      bad |= !ok;
+      // query head slot j is row j of Q^T, in column block j >> 1 (its kv head's dims)
+      unsigned char* qrow = sm + C::OFF_Q + (j >> 1) * 2048 + j * 128;
+      *reinterpret_cast<KT*>(qrow + (((i >> 3) ^ j) << 4) + (i & 7) * 2) = Elem<KT>::from_f32(a);
+      *reinterpret_cast<KT*>(qrow + ((((i >> 3) + 4) ^ j) << 4) + (i & 7) * 2) = Elem<KT>::from_f32(b);
+      if (p.q_rot_out && last_split) {
+        p.q_rot_out[qa] = a;
+        p.q_rot_out[qa + 32] = b;
+      }
+      if (has_new) {
+        if (tid < 64) {
+          ok = granite_rotate(kl, kr, sn, cs, &a, &b);
+          bad |= !ok;
+          newk[j * 64 + i] = Elem<KT>::from_f32(a);
+          newk[j * 64 + i + 32] = Elem<KT>::from_f32(b);
+        }
+        newv[tid] = Elem<KT>::from_f32(vnew);
+      }
+    } else {
+      const int pi = tid & 63;  // the rotation pair of every prologue item of this thread
+      // all of this thread's prologue inputs in flight at once: dim tid of the
+      // G query rows (and of the new key row), its RoPE pair, norm weights, new v
+      float qv[G], kn = 0.0f, vnew = 0.0f;
+      load_any_n<G>(p.q, qbase + tid, D, p.q_dtype, qv);
+      if (has_new) {
+        load_any_n<1>(p.k, kvbase + tid, 0, p.in_dtype, &kn);
+        load_any_n<1>(p.v, kvbase + tid, 0, p.in_dtype, &vnew);
+      }
+      const float2 cssn = p.rope_table[(long long)si.rope_pos * 64 + pi];
+      const float wq0 = p.q_norm ? p.q_norm[pi] : 1.0f, wq1 = p.q_norm ? p.q_norm[64 + pi] : 1.0f;
+      const float wk0 = p.k_norm ? p.k_norm[pi] : 1.0f, wk1 = p.k_norm ? p.k_norm[64 + pi] : 1.0f;
+#pragma unroll
+      for (int g = 0; g < G; ++g) raw[g * D + tid] = qv[g];
+      raw[G * D + tid] = kn;
+      {
+        // every load above has landed once its value is used
+        const float sink = cssn.x + wq0 + wq1 + wk0 + wk1 + vnew;
+        asm volatile("" ::"f"(sink));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(loaded);
+      trace.mark();  // prologue loads landed
+      // zero the padding rows 8..15 of Q and of both P^T buffers (both column blocks)
+      for (int i = tid; i < 6 * 128; i += 128) {
+        const int blk = i >> 7, j = i & 127;  // blk 0,1: Q blocks; 2..5: P blocks
+        unsigned char* base = sm + (blk < 2 ? C::OFF_Q + blk * 2048 : C::OFF_P + (blk - 2) * 2048) + 1024;
+        reinterpret_cast<uint2*>(base)[j] = make_uint2(0u, 0u);
+      }
+      consumers_sync(128);
+      if (tid < G || (tid == G && has_new)) {
+        const float* row = raw + tid * D;
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < D; ++i) sum = __fadd_rn(sum, __fmul_rn(row[i], row[i]));
+        st_inv[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 128.0f), 1.0e-6f)));
+      }
+      consumers_sync(128);
+      trace.mark();  // RMS norms
+      for (int idx = tid; idx < (G + 1) * 64; idx += 128) {
+        const int g = idx >> 6;
+        if (g == G && !has_new) break;
+        const bool is_q = g < G;
+        const float inv = st_inv[g];
+        const float x = raw[g * D + pi], y = raw[g * D + pi + 64];
+        const float left = __fmul_rn(__fmul_rn(x, inv), is_q ? wq0 : wk0);
+        const float right = __fmul_rn(__fmul_rn(y, inv), is_q ? wq1 : wk1);
+        const float a = __fsub_rn(__fmul_rn(left, cssn.x), __fmul_rn(right, cssn.y));
+        const float b = __fadd_rn(__fmul_rn(right, cssn.x), __fmul_rn(left, cssn.y));
+        bad |= !(isfinite(a) && isfinite(b));
+        const KT ka = Elem<KT>::from_f32(a), kb = Elem<KT>::from_f32(b);
+        if (is_q) {
+          // Q row g (K-major, 128-byte swizzle): dims pi and pi+64 in blocks 0 and 1
+          const int c = pi >> 3, off = (pi & 7) * 2;
+          *reinterpret_cast<KT*>(sm + C::OFF_Q + g * 128 + ((c ^ (g & 7)) << 4) + off) = ka;
+          *reinterpret_cast<KT*>(sm + C::OFF_Q + 2048 + g * 128 + ((c ^ (g & 7)) << 4) + off) = kb;
+          if (p.q_rot_out && last_split) {
+            p.q_rot_out[qbase + g * D + pi] = Elem<KT>::to_f32(ka);
+            p.q_rot_out[qbase + g * D + pi + 64] = Elem<KT>::to_f32(kb);
+          }
+        } else {
+          newk[pi] = ka;
+          newk[pi + 64] = kb;
+        }
+      }
+      if (has_new) newv[tid] = Elem<KT>::from_f32(vnew);
     }
-    if (has_new) newv[tid] = Elem<KT>::from_f32(vnew);
     if (bad) flag_error(p.err, QX_ERR_BIT_NONFINITE);
     fence_proxy_async_shared();  // Q and the P padding are read by tcgen05.mma
     consumers_sync(128);
@@ -330,7 +416,7 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
 
     // ---- consumers: tiles ----------------------------------------------------
     const bool pinned = p.pinned_exp != 0;
-    constexpr float SCALE_LOG2 = 0.08838834764831845f * 1.4426950408889634f;  // 1/sqrt(128) * log2(e)
+    constexpr float SCALE_LOG2 = TM::SCALE_LOG2;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     unsigned char* kring = sm + C::OFF_K;
     unsigned char* vring = sm + C::OFF_V;
@@ -359,7 +445,7 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
       ok &= mbar_wait_bounded(&sfull[b], (uint32_t)(t >> 1) & 1u, p.err);
       __syncwarp();
       tc_fence_after();
-      float x[G];
+      float x[8];  // columns G..7 hold zero-padding scores
       tmem_ld8_sync(tbase + lane_base + 16 * b, x);
 #pragma unroll
       for (int g = 0; g < G; ++g) x[g] = tid < rows ? x[g] * SCALE_LOG2 : -INFINITY;
@@ -398,8 +484,8 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
           ok &= mbar_wait_bounded(&pdone[(t - 1) & 1], (uint32_t)((t - 1) >> 1) & 1u, p.err);
           __syncwarp();
           tc_fence_after();
-          float o[G];
-          tmem_ld8_sync(tbase + lane_base + 32, o);  // thread tid = dim tid, 8 heads
+          float o[8];
+          tmem_ld8_sync(tbase + lane_base + 32, o);  // thread tid = dim tid of the unit, 8 columns
 #pragma unroll
           for (int g = 0; g < G; ++g) o[g] *= alpha[g];
           tmem_st8(tbase + lane_base + 32, o);
@@ -437,7 +523,7 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
     ok &= mbar_wait_bounded(&pdone[(ntiles - 1) & 1], (uint32_t)((ntiles - 1) >> 1) & 1u, p.err);
     __syncwarp();
     tc_fence_after();
-    float O[G];
+    float O[8];
     tmem_ld8_sync(tbase + lane_base + 32, O);
     // the row-sum partials of the four warps
 #pragma unroll
@@ -461,8 +547,30 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
     }
     if (s_flag[1]) return;
     trace.mark();  // tiles done
-    finish_outputs<G, D, HKV, HQ, G>(p, O, Mg, Lg, nsplit, s, cu, h, tid, warp, lane, pinned,
-                                     reinterpret_cast<float*>(sm + C::OFF_K), stat, s_flag);
+    if constexpr (TM::GRANITE) {
+      // Lane tid of O^T holds dim tid & 63 of kv head slot a = tid >> 6 for
+      // query head slots 2a and 2a+1 (its own kv head's heads; the other
+      // columns are cross products). finish_outputs wants thread tid to hold
+      // dim tid & 63 of heads a and a + 2: trade through shared memory.
+      float* xs = raw;  // [G][64]
+      const int a = tid >> 6, d = tid & 63;
+      xs[(2 * a) * 64 + d] = a ? O[2] : O[0];
+      xs[(2 * a + 1) * 64 + d] = a ? O[3] : O[1];
+      consumers_sync(128);
+      float O2[2], M2[2], L2[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int g = a + 2 * k;
+        O2[k] = xs[g * 64 + d];
+        M2[k] = a ? Mg[1 + 2 * k] : Mg[2 * k];
+        L2[k] = a ? Lg[1 + 2 * k] : Lg[2 * k];
+      }
+      finish_outputs<G, TM::HEAD_D, HKV, HQ, 2>(p, O2, M2, L2, nsplit, s, cu, h, tid, warp, lane, pinned,
+                                                reinterpret_cast<float*>(sm + C::OFF_K), stat, s_flag);
+    } else {
+      finish_outputs<G, D, HKV, HQ, G>(p, O, Mg, Lg, nsplit, s, cu, h, tid, warp, lane, pinned,
+                                       reinterpret_cast<float*>(sm + C::OFF_K), stat, s_flag);
+    }
     trace.mark();  // outputs (or partials) written
     return;
   }

@@ -227,19 +227,36 @@ int blocks_per_sm() {
   return n > 0 ? n : 1;
 }
 
-template <typename KT>
+template <typename KT, class TM>
 int tc_blocks_per_sm() {
-  using C = TcCfg<KT>;
-  cudaFuncSetAttribute(qx_decode_tc_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  using C = TcCfg<KT, TM>;
+  cudaFuncSetAttribute(qx_decode_tc_kernel<KT, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   int n = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qx_decode_tc_kernel<KT>, C::NT, C::SMEM) != cudaSuccess) n = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qx_decode_tc_kernel<KT, TM>, C::NT, C::SMEM) != cudaSuccess)
+    n = 1;
   return n > 0 ? n : 1;
 }
+
+// A Granite arena whose keys and values share one 16-bit type decodes on the
+// tensor cores, a pair of kv heads per work unit (TcGranitePair).
+bool granite_pair_tc(const qxc_kv* kv) {
+  const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
+  return kv->desc.model == QXC_MODEL_GRANITE && kd == vd && (kd == QXC_BF16 || kd == QXC_F16);
+}
+
+// The decode kernel's grid runs on tcgen05 (Qwen, 16-bit Granite).
+bool decode_on_tc(const qxc_kv* kv) { return kv->desc.model == QXC_MODEL_QWEN3 || granite_pair_tc(kv); }
+
+// Work units per layer of the decode kernels: kv heads, or kv-head pairs.
+int decode_units(const qxc_kv* kv) { return granite_pair_tc(kv) ? kv->hkv / 2 : kv->hkv; }
 
 int decode_blocks_per_sm(const qxc_kv* kv) {
   const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
   if (kv->desc.model == QXC_MODEL_QWEN3)
-    return kd == QXC_BF16 ? tc_blocks_per_sm<__nv_bfloat16>() : tc_blocks_per_sm<__half>();
+    return kd == QXC_BF16 ? tc_blocks_per_sm<__nv_bfloat16, TcQwen>() : tc_blocks_per_sm<__half, TcQwen>();
+  if (granite_pair_tc(kv))
+    return kd == QXC_BF16 ? tc_blocks_per_sm<__nv_bfloat16, TcGranitePair>()
+                          : tc_blocks_per_sm<__half, TcGranitePair>();
   if (kd == QXC_F32 && vd == QXC_F32) return blocks_per_sm<Granite, float, float>();
   if (kd == QXC_F32 && vd == QXC_F16) return blocks_per_sm<Granite, float, __half>();
   if (kd == QXC_F16 && vd == QXC_F32) return blocks_per_sm<Granite, __half, float>();
@@ -247,13 +264,16 @@ int decode_blocks_per_sm(const qxc_kv* kv) {
   return blocks_per_sm<Granite, __nv_bfloat16, __nv_bfloat16>();
 }
 
-// Cache rows per pipeline tile: 128 for the tensor-core Qwen kernel, else 64.
-int decode_tile(const qxc_kv* kv) { return kv->desc.model == QXC_MODEL_QWEN3 ? 128 : 64; }
+// Cache rows per pipeline tile: 128 for the tensor-core kernels, else 64.
+int decode_tile(const qxc_kv* kv) { return decode_on_tc(kv) ? 128 : 64; }
+
+// A split must be a multiple of this many rows: 64 for Granite (the
+// tensor-core kernel masks the rest of a 128-row tile), 128 for Qwen.
+int split_unit(const qxc_kv* kv) { return kv->desc.model == QXC_MODEL_QWEN3 ? 128 : 64; }
 
 int decode_max_splits(const qxc_kv* kv) {
   const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
-  if (kv->desc.model == QXC_MODEL_QWEN3)
-    return kd == QXC_BF16 ? TcCfg<__nv_bfloat16>::MAX_SPLITS : TcCfg<__half>::MAX_SPLITS;
+  if (decode_on_tc(kv)) return TcCfg<__nv_bfloat16>::MAX_SPLITS;
   if (kd == QXC_F32 && vd == QXC_F32) return DecodeCfg<Granite, float, float>::MAX_SPLITS;
   if (kd == QXC_F32 && vd == QXC_F16) return DecodeCfg<Granite, float, __half>::MAX_SPLITS;
   if (kd == QXC_F16 && vd == QXC_F32) return DecodeCfg<Granite, __half, float>::MAX_SPLITS;
@@ -354,16 +374,17 @@ qxc_status launch_typed(qxc_ctx* ctx, const DecodeParams& p, int items) {
   return QXC_OK;
 }
 
-template <typename KT>
+template <typename KT, class TM>
 qxc_status launch_tc(qxc_ctx* ctx, const DecodeParams& p, int items) {
-  using C = TcCfg<KT>;
+  using C = TcCfg<KT, TM>;
   static unsigned long long configured = 0;
   const unsigned long long bit = 1ull << (ctx->device & 63);
   if (!(configured & bit)) {
-    QXC_CUDA(ctx, cudaFuncSetAttribute(qx_decode_tc_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    QXC_CUDA(ctx, cudaFuncSetAttribute(qx_decode_tc_kernel<KT, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM));
     configured |= bit;
   }
-  QXC_CUDA(ctx, launch_pdl(ctx, qx_decode_tc_kernel<KT>, items, C::NT, C::SMEM, p));
+  QXC_CUDA(ctx, launch_pdl(ctx, qx_decode_tc_kernel<KT, TM>, items, C::NT, C::SMEM, p));
   ctx->launches++;
   return QXC_OK;
 }
@@ -379,6 +400,8 @@ qxc_status launch_split_merge(qxc_ctx* ctx, const qxc_kv* kv, const DecodeParams
   const int grid = p.n_seq * p.layer_count * kv->hq * (kv->d / 32);
   if (kv->desc.model == QXC_MODEL_QWEN3)
     QXC_CUDA(ctx, launch_pdl(ctx, qx_split_merge_kernel<8, 128, 4, 32>, grid, 128, 0, p));
+  else if (granite_pair_tc(kv))
+    QXC_CUDA(ctx, launch_pdl(ctx, qx_split_merge_kernel<4, 64, 4, 16>, grid, 128, 0, p));
   else
     QXC_CUDA(ctx, launch_pdl(ctx, qx_split_merge_kernel<2, 64, 8, 16>, grid, 128, 0, p));
   ctx->launches++;
@@ -403,8 +426,12 @@ qxc_status launch_decode_kernel(qxc_ctx* ctx, const qxc_kv* kv, const DecodePara
   const int kd = kv->desc.key_dtype, vd = kv->desc.value_dtype;
   if (kv->desc.model == QXC_MODEL_QWEN3) {
     // group-8 attention runs on the tensor cores (decode_tc.cuh)
-    if (kd == QXC_BF16) return launch_tc<__nv_bfloat16>(ctx, p, items);
-    return launch_tc<__half>(ctx, p, items);
+    if (kd == QXC_BF16) return launch_tc<__nv_bfloat16, TcQwen>(ctx, p, items);
+    return launch_tc<__half, TcQwen>(ctx, p, items);
+  }
+  if (granite_pair_tc(kv)) {
+    if (kd == QXC_BF16) return launch_tc<__nv_bfloat16, TcGranitePair>(ctx, p, items);
+    return launch_tc<__half, TcGranitePair>(ctx, p, items);
   }
   if (kd == QXC_F32 && vd == QXC_F32) return launch_typed<Granite, float, float>(ctx, p, items);
   if (kd == QXC_F32 && vd == QXC_F16) return launch_typed<Granite, float, __half>(ctx, p, items);
@@ -444,12 +471,18 @@ struct CallPlan {
   std::vector<SeqInfo> tab;
   int items = 0;
   int chunk = 0;
+  int units = 0;  // work units per layer (kv heads, or kv-head pairs)
 };
 
 // Build the work decomposition of one call. `attend[i]`, `new_slot[i]`,
 // `rope_pos[i]` per sequence entry.
+// `units`: work units per layer of the kernel that will run (0: the decode
+// kernels' decode_units).
 qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* seq_ids, const int* attend,
-                     const int* new_slot, const int* rope_pos, int layer_count, int split, CallPlan* out) {
+                     const int* new_slot, const int* rope_pos, int layer_count, int split, CallPlan* out,
+                     int units = 0) {
+  if (units == 0) units = decode_units(kv);
+  out->units = units;
   int chunk = split;
   if (chunk == 0) {
     static int cached_slots[64][8] = {};  // [device][arena type] resident CTAs on the GPU
@@ -459,7 +492,7 @@ qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* s
                                                        : (kd == QXC_F16 ? 2 : 0) + (vd == QXC_F16 ? 1 : 0);
     int& slots = cached_slots[ctx->device & 63][type];
     if (!slots) slots = ctx->sm_count * decode_blocks_per_sm(kv);
-    chunk = auto_chunk(slots, attend, seq_count, layer_count * kv->hkv, decode_max_splits(kv), decode_tile(kv));
+    chunk = auto_chunk(slots, attend, seq_count, layer_count * units, decode_max_splits(kv), decode_tile(kv));
   }
   {
     int max_attend = 1;
@@ -468,8 +501,8 @@ qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* s
       return fail(ctx, QXC_ERR_INVALID_ARG, "split %d gives %d splits; at most %d fit the merge", chunk,
                   (max_attend + chunk - 1) / chunk, decode_max_splits(kv));
   }
-  if (chunk <= 0 || chunk % decode_tile(kv) != 0)
-    return fail(ctx, QXC_ERR_INVALID_ARG, "split %d must be a positive multiple of %d", split, decode_tile(kv));
+  if (chunk <= 0 || chunk % split_unit(kv) != 0)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "split %d must be a positive multiple of %d", split, split_unit(kv));
   out->chunk = chunk;
   ctx->last_split = chunk;
   out->tab.resize(seq_count);
@@ -483,7 +516,7 @@ qxc_status plan_call(qxc_ctx* ctx, const qxc_kv* kv, int seq_count, const int* s
     s.item_begin = (int)items;
     s.pad[0] = s.pad[1] = s.pad[2] = 0;
     const long long nsplit = (attend[i] + chunk - 1) / chunk;
-    items += nsplit * layer_count * kv->hkv;
+    items += nsplit * layer_count * units;
   }
   if (items > 0x7fffffffLL) return fail(ctx, QXC_ERR_INVALID_ARG, "too much work in one call");
   out->items = (int)items;
@@ -533,10 +566,10 @@ qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer
     qxc_status st = upload_seq_table(ctx, plan.tab, &p->seq_table);
     if (st != QXC_OK) return st;
   }
-  const int G = kv->hq / kv->hkv;
+  const int G = kv->hq / plan.units;
   qxc_status st = grow(ctx, &ctx->partials, &ctx->partials_cap, (size_t)plan.items * G * (kv->d + 2), false);
   if (st != QXC_OK) return st;
-  st = grow(ctx, &ctx->tickets, &ctx->tickets_cap, (size_t)plan.tab.size() * layer_count * kv->hkv, true);
+  st = grow(ctx, &ctx->tickets, &ctx->tickets_cap, (size_t)plan.tab.size() * layer_count * plan.units, true);
   if (st != QXC_OK) return st;
   p->partials = ctx->partials;
   p->tickets = ctx->tickets;
@@ -549,7 +582,7 @@ qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer
   p->early_trigger = one_wave ? 1 : 0;
   // a single contiguous sequence may stream its settled rows before the wait
   if (plan.tab.size() == 1 && !kv->paged()) p->pre_rows = rows_settled(ctx, kv, plan.tab[0].seq_id);
-  if (kv->desc.model == QXC_MODEL_GRANITE) {
+  if (!decode_on_tc(kv)) {
     // the CUDA-core kernels trigger at their start (measured faster for
     // them) and stream nothing before their wait
     note_rows_open(ctx);
@@ -852,11 +885,12 @@ qxc_status launch_verify_typed(qxc_ctx* ctx, qxc_kv* kv, const qxc_verify_args* 
     return fail(ctx, QXC_ERR_INVALID_ARG, "split %d gives %d splits; at most %d fit the merge", split,
                 (attend + split - 1) / split, C::MAX_SPLITS);
   CallPlan plan;
-  qxc_status st = plan_call(ctx, kv, 1, &seq, &attend, &none, &rope, a->layer_count, split, &plan);
+  qxc_status st = plan_call(ctx, kv, 1, &seq, &attend, &none, &rope, a->layer_count, split, &plan, kv->hkv);
   if (st != QXC_OK) return st;
   DecodeParams p;
   st = fill_params(ctx, kv, plan, a->layer_begin, a->layer_count, &p);
   if (st != QXC_OK) return st;
+  note_rows_open(ctx);  // the verify kernel triggers its dependents at its start
   st = grow(ctx, &ctx->partials, &ctx->partials_cap, (size_t)plan.items * C::G * (C::D + 2), false);
   if (st != QXC_OK) return st;
   p.partials = ctx->partials;
