@@ -83,6 +83,37 @@ def test_kv_precisions(gpu_ctx, oracle, kd, vd):
     assert np.array_equal(gk, oc.keys[:L]) and np.array_equal(gv, oc.values[:L])
 
 
+@pytest.mark.parametrize("length", [1, 63, 64, 65, 127, 128, 129, 200, 1000, 4096])
+@pytest.mark.parametrize("split", [0, 64, 192, 4096])
+@pytest.mark.parametrize("kv", [BF16, F16])
+def test_edge_lengths_16bit_tensor_core(gpu_ctx, oracle, length, split, kv):
+    """Granite with a 16-bit cache decodes on tcgen05, a kv-head pair per
+    work unit. Splits of 64 rows leave a last tile of at most 64 rows; 4096
+    keeps one split; 64 at length 4096 gives 64 splits and the separate
+    merge kernel. The new key row is bit-exact, and so is the rotated query
+    (f32, before the operand rounding)."""
+    import torch
+    cap = max(length, 64)
+    q, k, v, kc, vc = granite_inputs(0x1800 + length + 7 * split, length - 1, cap)
+    oc = oracle_cache(oracle, cap, kv, kv, kc, vc)
+    st, ref = oracle.granite_attention_decode(q, k, v, length - 1, oc)
+    assert st == 0
+    arena = gpu_arena(gpu_ctx, cap, kv, kv, kc, vc)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32).reshape(1, -1)).cuda()
+    out = torch.zeros(1, 1024, device="cuda")
+    qrot = torch.zeros(1, 1024, device="cuda")
+    arena.decode(dev(q), dev(k), dev(v), out, [length - 1], split=split, q_rot_out=qrot)
+    gpu_ctx.sync()
+    assert normwise(out.cpu().numpy()[0], ref) <= 2e-2, (length, split)
+    assert normwise(out.cpu().numpy()[0], ref) <= 4e-3, (length, split)  # observed margin
+    gk, gv = arena.read(0, 0, length - 1, 1)
+    assert np.array_equal(gk.reshape(-1), oc.keys[length - 1].reshape(-1))
+    assert np.array_equal(gv.reshape(-1), oc.values[length - 1].reshape(-1))
+    qr = np.ascontiguousarray(q, np.float32).copy()
+    assert oracle.lib().qxo_rotate_heads(oracle._fp(qr), 16, length - 1) == 0
+    assert np.array_equal(qrot.cpu().numpy()[0].view(np.uint32), qr.view(np.uint32))
+
+
 def test_sequential_steps_keep_cache_bit_exact(gpu_ctx, oracle):
     """Eight consecutive appends through the V1 mirror (KvCache / granite_attention_decode)."""
     cache = KvCache(64, gpu_ctx)
