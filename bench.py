@@ -952,7 +952,7 @@ def run_config4(args, world, rank, local):
     from qx_b200.distributed import lpt_shard, sequence_kv_bytes
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    lengths = [int(x) for x in syn.uniform_int(0x51580400, 256, 128, 4096)]
+    lengths = [int(x) for x in syn.uniform_int(0x51580400, 256, 128, 4096)][:args.c4_sequences]
     assignment, _ = lpt_shard([sequence_kv_bytes(L) for L in lengths], world)
     mine = assignment[rank]
     n = len(mine)
@@ -1003,18 +1003,20 @@ def run_config4(args, world, rank, local):
     K, W = args.steps, args.warmup
     total, per, clk, launches = timed_steps(step, K, W, stream, world, dev, local, ctx)
     my_bytes = sum(LAYERS * (2 * lengths[i] * 8 * 64 * 2 + 4 * 64 * (2 * 16 + 2 * 8)) for i in mine)
-    line = base_line("multi-sequence Granite decode tok/s (256 sequences x 24 layers)", 256 * K / (total / 1e3),
+    nseq = len(lengths)
+    line = base_line("multi-sequence Granite decode tok/s (256 sequences x 24 layers)", nseq * K / (total / 1e3),
                      "tok/s", world, K, W, total, True, "strong", "f32 q/k/v, bf16 KV",
-                     {"workload": "config4: 256 Granite sequences, lengths U{128..4096} (seed 0x51580400), "
+                     {"workload": f"config4: {nseq} Granite sequences, lengths U{{128..4096}} (seed 0x51580400), "
                                   "24 layers, bf16 KV, one decode step each",
-                      "l2": "26.6 GB of KV per step",
+                      "l2": f"{my_bytes / 1e9:.1f} GB of KV per step",
                       "parallelism": f"sequences sharded x{world} by LPT on KV bytes, no collective"},
                      clk, launches)
     line["config"]["split"] = ctx.last_split
     line["config"]["kv_arena_bytes_per_rank"] = int(kv_bytes)
     if page:
         line["config"]["workload"] += f"; paged arena, {page}-row pages, pool sized to the batch"
-    line["roofline"] = hbm_roofline(my_bytes, per, "qx_decode_kernel<Granite,bf16,bf16>")
+    line["roofline"] = hbm_roofline(my_bytes, per, "qx_decode_tc_kernel<bf16,TcGranitePair>",
+                                    None if nseq != 256 else ("config4_paged" if page else "config4"))
     arena.close()
     ctx.close()
     return line
@@ -1100,6 +1102,8 @@ def main():
                          "exchange kernel (kernel), or by an NCCL all-gather (nccl)")
     ap.add_argument("--prefill-len", type=int, default=2048, help="config2 prompt length (512 or 2048)")
     ap.add_argument("--qwen-context", type=int, default=32768, help="config3 KV length")
+    ap.add_argument("--c4-sequences", type=int, default=256,
+                    help="config4: the first N of its 256 sequences (a smaller case of the same kernel, to profile)")
     ap.add_argument("--native-exp", action="store_true", help="hardware exp2 instead of qx's pinned exp_f32")
     ap.add_argument("--e2e-steps", type=int, default=640)
     ap.add_argument("--cpu-steps", type=int, default=16)
