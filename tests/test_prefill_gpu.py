@@ -24,7 +24,7 @@ def run_prefill(ctx, L, seed):
     return q, k, v, arena, out.cpu().numpy()
 
 
-@pytest.mark.parametrize("L", [1, 63, 64, 65, 200, 512])
+@pytest.mark.parametrize("L", [1, 63, 64, 65, 128, 129, 200, 512, 1000])
 def test_prefill_matches_iterated_decode(gpu_ctx, oracle, L):
     q, k, v, arena, got = run_prefill(gpu_ctx, L, syn.seed_for(2) + L)
     st, kc, vc, ref = oracle.granite_prefill(q, k, v, oracle.BF16, oracle.BF16, threads=8)
@@ -44,6 +44,32 @@ def test_prefill_2048(gpu_ctx, oracle):
     assert normwise(got, ref) <= 2e-2
     gk, _ = arena.read(0, 0, 0, L)
     assert np.array_equal(gk, kc)
+
+
+def test_prefills_back_to_back(gpu_ctx, oracle):
+    """Three prompts queued with no host sync between them, into three
+    sequences of one arena (the RoPE grid of each may start its attention
+    grid early, and reuses the context's rotated-query scratch): each must
+    match the oracle."""
+    import torch
+    lengths = [700, 300, 700]
+    arena = KvArena(gpu_ctx, MODEL_GRANITE, 1, 3, 768, BF16, BF16)
+    dev = lambda a: torch.from_numpy(a.view(np.int16)).cuda()
+    cases = []
+    for s_, L in enumerate(lengths):
+        q = syn.to_bf16_bits(syn.normal(0x5100 + s_, (L, 16, 64), 0.5))
+        k = syn.to_bf16_bits(syn.normal(0x5200 + s_, (L, 8, 64), 0.5))
+        v = syn.to_bf16_bits(syn.normal(0x5300 + s_, (L, 8, 64), 0.5))
+        out = torch.zeros(L, 16, 64, device="cuda")
+        arena.prefill(dev(q), dev(k), dev(v), out, L, seq=s_)
+        cases.append((q, k, v, out))
+    gpu_ctx.sync()
+    for s_, (q, k, v, out) in enumerate(cases):
+        st, kc, vc, ref = oracle.granite_prefill(q, k, v, oracle.BF16, oracle.BF16, threads=8)
+        assert st == 0
+        assert normwise(out.cpu().numpy(), ref) <= 2e-2, s_
+        gk, gv = arena.read(s_, 0, 0, lengths[s_])
+        assert np.array_equal(gk, kc) and np.array_equal(gv, vc)
 
 
 def test_decode_continues_after_prefill(gpu_ctx, oracle):
