@@ -290,16 +290,16 @@ int auto_chunk(int slots, const int* attend, int n, int units_per_seq, int max_s
   int max_attend = 1;
   for (int i = 0; i < n; ++i) max_attend = std::max(max_attend, attend[i]);
   const int top = ((max_attend + tile - 1) / tile) * tile;
-  // A batch whose unsplit work already fills every CTA slot several times
+  // A batch whose unsplit work already fills every CTA slot a few times
   // over gains nothing from splitting; each extra CTA only adds its fixed
-  // cost (config 4 on the tensor-core kernel: 48.1k tok/s at splits of 1024
-  // rows, 62.1k unsplit). Unsplit when the work per slot is at least four
-  // times the longest item.
+  // cost (the tensor-core kernel on config 4: 48.1k tok/s at splits of 1024
+  // rows, 62.1k unsplit; its first 8 sequences: 45.1k and 54.4k). Unsplit
+  // when the work per slot is at least twice the longest item.
   {
     double work = 0.0;
     for (int i = 0; i < n; ++i) work += (double)units_per_seq * ((double)(attend[i] + tile - 1) / tile + 3.0);
     const double longest = (double)top / tile + 3.0;
-    if (work / slots >= 4.0 * longest && (max_attend + top - 1) / top <= max_splits) return top;
+    if (work / slots >= 2.0 * longest && (max_attend + top - 1) / top <= max_splits) return top;
   }
   double best = 1e300;
   int best_c = top;
