@@ -308,8 +308,10 @@ int auto_chunk(int slots, const int* attend, int n, int units_per_seq, int max_s
     long long items = 0;
     for (int i = 0; i < n; ++i) items += (long long)units_per_seq * ((attend[i] + c - 1) / c);
     const long long waves = (items + slots - 1) / slots;
-    // + the last CTA's merge, which grows with the split count
-    const double cost = (double)waves * ((double)c / tile + 3.0) * tile / 64.0 + 0.05 * ((max_attend + c - 1) / c);
+    // + the merge, which grows with the split count (weighted so that the
+    // measured optima stay chosen: config 1 at 2048 rows, config 3 at 896,
+    // the Q4 layer's single-layer decode at 256 rather than 128)
+    const double cost = (double)waves * ((double)c / tile + 3.0) * tile / 64.0 + 0.2 * ((max_attend + c - 1) / c);
     if (cost < best - 1e-9) {
       best = cost;
       best_c = c;
