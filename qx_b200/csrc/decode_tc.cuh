@@ -35,8 +35,8 @@
 // output is its own kv head's half of the dims and the rest is never read.
 // The prologue is Granite's: qx's pinned RoPE (granite_rotate) on q and k,
 // q rounded to the operand type for the MMA. This takes both contractions
-// off the CUDA cores for the bf16 / f16 Granite caches (configs 1-4 with
-// 16-bit KV); the fp32 cache stays on qx_decode_kernel.
+// off the CUDA cores for every Granite cache whose keys and values are both
+// bf16 or both f16; fp32 and mixed caches stay on qx_decode_kernel.
 #pragma once
 #include <type_traits>
 
