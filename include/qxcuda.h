@@ -84,6 +84,14 @@ const char* qxc_last_error(const qxc_ctx* ctx);
 uint64_t qxc_launch_count(const qxc_ctx* ctx);
 /* Cache positions per split chosen by the last decode call on this context. */
 int32_t qxc_last_split(const qxc_ctx* ctx);
+/* (new; host only, no device) The automatic split the decode calls choose:
+ * cache rows per split for `n` sequences of attend[i] rows, `units` work
+ * units per sequence (layers x kv heads, or kv-head pairs on the 16-bit
+ * Granite path), `slots` CTAs resident on the GPU at once, at most
+ * `max_splits` splits, `tile` rows per pipeline tile (64 on the CUDA-core
+ * kernels, 128 on the tensor-core ones). 0 on a bad argument. */
+int32_t qxc_auto_split(int32_t slots, const int32_t* attend, int32_t n, int32_t units, int32_t max_splits,
+                       int32_t tile);
 
 /* ---- KV cache arena ---------------------------------------------------- */
 typedef struct qxc_kv_desc {

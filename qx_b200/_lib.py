@@ -115,6 +115,7 @@ def load() -> C.CDLL:
         "qxc_last_error": (C.c_char_p, [vp]),
         "qxc_launch_count": (C.c_uint64, [vp]),
         "qxc_last_split": (C.c_int32, [vp]),
+        "qxc_auto_split": (C.c_int32, [C.c_int32, C.POINTER(C.c_int32), C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
         "qxc_kv_bytes": (C.c_int, [C.POINTER(KvDesc), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
         "qxc_kv_create": (C.c_int, [vp, C.POINTER(KvDesc), pp]),
         "qxc_kv_create_paged": (C.c_int, [vp, C.POINTER(KvDesc), C.POINTER(KvPaging), pp]),

@@ -1036,6 +1036,14 @@ uint64_t qxc_launch_count(const qxc_ctx* ctx) { return ctx ? ctx->launches : 0; 
 
 int32_t qxc_last_split(const qxc_ctx* ctx) { return ctx ? ctx->last_split : 0; }
 
+int32_t qxc_auto_split(int32_t slots, const int32_t* attend, int32_t n, int32_t units, int32_t max_splits,
+                       int32_t tile) {
+  if (slots < 1 || !attend || n < 1 || units < 1 || max_splits < 1 || tile < 1) return 0;
+  for (int i = 0; i < n; ++i)
+    if (attend[i] < 1) return 0;
+  return auto_chunk(slots, attend, n, units, max_splits, tile);
+}
+
 // ---- KV arena ---------------------------------------------------------------
 qxc_status qxc_kv_bytes(const qxc_kv_desc* d, size_t* key_bytes, size_t* value_bytes) {
   qxc_status st = check_desc(nullptr, d);

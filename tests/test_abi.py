@@ -68,3 +68,39 @@ def test_null_arguments_are_rejected_without_a_gpu():
     assert lib.qxc_init(0, None) == _lib.ERR_INVALID_ARG
     assert lib.qxc_sync(None) == _lib.ERR_INVALID_ARG
     assert lib.qxc_decode(None, None, None) == _lib.ERR_INVALID_ARG
+
+
+def _auto_split(slots, attend, units, max_splits, tile):
+    lib = _lib.load()
+    a = (C.c_int32 * len(attend))(*attend)
+    return lib.qxc_auto_split(slots, a, len(attend), units, max_splits, tile)
+
+
+def test_automatic_split_keeps_the_measured_optima():
+    """qxc_auto_split is the decode calls' own split choice (host only).
+    Each case pins a split that a sweep on a B200 found best: config 1 at
+    2048 rows (384 CTAs in one wave of 444 slots), config 3 at 896 (148 CTAs
+    for 148 slots), the Q4 layer's one-layer decode at 256, config 0 at 64."""
+    assert [_auto_split(444, [n], 24 * 8, 1024, 64) for n in (4033, 4064, 4096)] == [2048] * 3
+    assert _auto_split(148, [32768], 4, 1024, 128) == 896
+    assert _auto_split(444, [4064], 8, 1024, 64) == 256
+    assert _auto_split(444, [512], 8, 1024, 64) == 64
+
+
+def test_automatic_split_leaves_large_batches_unsplit():
+    """A batch whose unsplit work fills the slots at least twice per longest
+    item runs unsplit: config 4's 256 sequences and its first 8 (measured
+    62.1k and 54.4k tok/s unsplit against 48.1k and 45.1k split). Its first
+    4 still split."""
+    from qx_b200 import synthetic as syn
+    lengths = [int(x) for x in syn.uniform_int(0x51580400, 256, 128, 4096)]
+    top = lambda xs: -(-max(xs) // 128) * 128  # noqa: E731
+    assert _auto_split(148, lengths, 24 * 4, 1024, 128) == top(lengths)
+    assert _auto_split(148, lengths[:8], 24 * 4, 1024, 128) == top(lengths[:8])
+    assert _auto_split(148, lengths[:4], 24 * 4, 1024, 128) < top(lengths[:4])
+
+
+def test_automatic_split_rejects_bad_arguments():
+    assert _auto_split(0, [5], 1, 1, 64) == 0
+    assert _auto_split(148, [0], 1, 1, 64) == 0
+    assert _auto_split(148, [100], 0, 1, 64) == 0
