@@ -935,7 +935,8 @@ def run_verify(args, world, rank, local):
                      clk, launches)
     line["verify_steps_per_s"] = world * K / (total / 1e3)
     line["config"]["split"] = ctx.last_split
-    line["roofline"] = hbm_roofline(B, per, "qx_append_rows_kernel + qx_decode_kernel<Granite,float,float>")
+    line["roofline"] = hbm_roofline(B, per, "qx_append_rows_kernel + qx_verify_kernel<float,float> (timed together)",
+                                    "verify" if L == 4096 else None)
     arena.close()
     ctx.close()
     return line
