@@ -1017,7 +1017,7 @@ def run_config4(args, world, rank, local):
     if page:
         line["config"]["workload"] += f"; paged arena, {page}-row pages, pool sized to the batch"
     line["roofline"] = hbm_roofline(my_bytes, per, "qx_decode_tc_kernel<bf16,TcGranitePair>",
-                                    None if nseq != 256 else ("config4_paged" if page else "config4"))
+                                    None if nseq != 256 or world != 1 else ("config4_paged" if page else "config4"))
     arena.close()
     ctx.close()
     return line
