@@ -104,3 +104,12 @@ def test_automatic_split_rejects_bad_arguments():
     assert _auto_split(0, [5], 1, 1, 64) == 0
     assert _auto_split(148, [0], 1, 1, 64) == 0
     assert _auto_split(148, [100], 0, 1, 64) == 0
+
+
+def test_every_declared_entry_point_has_a_python_signature():
+    """The ctypes mirror declares argument and result types for every
+    function include/*.h declares, so no call goes through ctypes' default
+    int conversion of pointers and sizes."""
+    lib = _lib.load()
+    untyped = [n for n in _lib.header_symbols() if getattr(lib, n).argtypes is None]
+    assert untyped == []
