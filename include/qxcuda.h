@@ -6,7 +6,7 @@
  *
  * Plain C types only: device pointers are `void*`, sizes are integers,
  * errors are status codes plus a per-context message. A Rust `qx-cuda`
- * crate binds these symbols one-to-one.
+ * crate binds these symbols one-to-one through an `extern "C"` block.
  *
  * Reference interfaces replaced (paths within blasrodri/qx):
  *   crates/qx-runtime/src/lib.rs:350-432     KvCache (new/len/is_empty/reset/append)
@@ -405,8 +405,12 @@ qxc_status qxc_decode_partials(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args*
  * partials from qxc_decode_partials. The kernel stores the partials into every
  * rank's area with peer stores, each value paired with the step's tag in one
  * 8-byte store (no memory fence), waits until every rank's values of its query
- * head carry the tag (bounded: QXC_ERR_TIMEOUT at qxc_sync, after which the
- * groups must be re-created on every rank) and merges in rank order: the
+ * head carry the tag (bounded: QXC_ERR_TIMEOUT at qxc_sync) and merges in
+ * rank order. A timed-out exchange leaves the group failed for good: every
+ * later exchange on it (this call or qxc_decode_exchange) returns
+ * QXC_ERR_TIMEOUT, at the call once the failure has been recorded, else at
+ * qxc_sync without pushing or merging anything; destroy and re-create the
+ * groups on every rank to go on. The merged output: the
  * output equals qxc_lse_merge over the gathered partials, bit for bit, on
  * every rank. Every rank must issue the same sequence of exchange calls. */
 #define QXC_PEER_HANDLE_BYTES 64

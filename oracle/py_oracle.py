@@ -67,7 +67,8 @@ def lib():
         _lib.qxo_q4_quantize.argtypes = [fp, C.c_int, C.c_int, u8p, u16p]
         _lib.qxo_q4_mat_vec_simd32.argtypes = [u8p, u16p, C.c_int, C.c_int, fp, fp]
         _lib.qxo_granite_attention_layer.argtypes = [fp, fp, u8p, u16p, u8p, u16p, u8p, u16p, u8p, u16p, C.c_int,
-                                                     fp, fp, ip, C.c_int, fp, fp]
+                                                     fp, fp, ip, C.c_int, C.c_int, fp, fp]
+        _lib.qxo_cpu_rotate_heads.argtypes = [fp, C.c_int, C.c_uint32]
         _lib.qxo_blake3_single_chunk.argtypes = [vp, C.c_size_t, u8p]
         _lib.qxo_chunk_tree_hash.argtypes = [vp, C.c_size_t, C.c_char_p, C.c_char_p, u8p]
         _lib.qxo_kv_leaf_hash.argtypes = [C.c_uint16, C.c_uint32, vp, C.c_size_t, vp, C.c_size_t, u8p]
@@ -247,8 +248,10 @@ class Q4Matrix:
 
 
 def granite_attention_layer(hidden, input_norm, qp: Q4Matrix, kp: Q4Matrix, vp: Q4Matrix, op: Q4Matrix,
-                            position: int, cache: KvCache):
-    """(status 0 ok, hidden out [1024], attention [1024]) for one layer at `position`."""
+                            position: int, cache: KvCache, cpu_twin: bool = False):
+    """(status 0 ok, hidden out [1024], attention [1024]) for one layer at
+    `position`: the V2 GPU stage's arithmetic, or with cpu_twin the V2 CPU
+    twin CpuQ4Reference::step (no-fma RoPE, hierarchical attention, <= 512)."""
     h = np.ascontiguousarray(hidden, np.float32)
     w = np.ascontiguousarray(input_norm, np.float32)
     out = np.zeros(1024, np.float32)
@@ -256,7 +259,8 @@ def granite_attention_layer(hidden, input_norm, qp: Q4Matrix, kp: Q4Matrix, vp: 
     st = lib().qxo_granite_attention_layer(_fp(h), _fp(w), _u8(qp.codes), _u16(qp.scales), _u8(kp.codes),
                                            _u16(kp.scales), _u8(vp.codes), _u16(vp.scales), _u8(op.codes),
                                            _u16(op.scales), position, _fp(cache.keys), _fp(cache.values),
-                                           C.byref(cache.length), cache.max_context, _fp(out), _fp(att))
+                                           C.byref(cache.length), cache.max_context, int(bool(cpu_twin)), _fp(out),
+                                           _fp(att))
     return st, out, att
 
 

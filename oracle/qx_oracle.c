@@ -301,6 +301,27 @@ int qxo_rotate_heads(float* values, int heads, uint32_t position) {
   return QXO_OK;
 }
 
+/* cpu_rotate_heads, crates/qx-runtime-v2/src/lib.rs:4957-4970: the V2 CPU
+ * twin's RoPE. Same sin/cos as rotate_heads, but the pair is rotated as
+ * left*cos - right*sin and left*sin + right*cos with every product and sum
+ * rounded on its own (no fma), so it differs from rotate_heads in the last
+ * bits. The reference expects a registered coordinate (a panic otherwise). */
+int qxo_cpu_rotate_heads(float* values, int heads, uint32_t position) {
+  for (int head = 0; head < heads; ++head) {
+    int start = head * G_HEAD_DIM;
+    for (int pair = 0; pair < G_HEAD_DIM / 2; ++pair) {
+      float s, c;
+      if (!qxo_granite_rope_sin_cos(position, (uint32_t)pair, &s, &c)) return QXO_ERR_NONFINITE;
+      const float left = values[start + pair];
+      const float right = values[start + G_HEAD_DIM / 2 + pair];
+      const float lc = left * c, rs = right * s, ls = left * s, rc = right * c;
+      values[start + pair] = lc - rs;
+      values[start + G_HEAD_DIM / 2 + pair] = ls + rc;
+    }
+  }
+  return QXO_OK;
+}
+
 /* Rust's f32::max: a NaN operand yields the other operand. */
 static inline float rust_max(float a, float b) {
   if (isnan(a)) return b;
@@ -309,21 +330,30 @@ static inline float rust_max(float a, float b) {
 }
 
 /* granite_attention_decode_with_profile, crates/qx-runtime/src/lib.rs:464-552
- * (KvCache::append :382-405 inlined). */
-int qxo_granite_attention_decode(const float* query_in, const float* key_in,
-                                 const float* value, int position, void* keys,
-                                 void* values, int key_dtype, int value_dtype,
-                                 int* length, int max_context, int hierarchical,
-                                 float* output) {
+ * (KvCache::append :382-405 inlined). With cpu_twin the query and key are
+ * rotated by cpu_rotate_heads instead of apply_granite_rope: with
+ * hierarchical set, that is the V2 CPU twin CpuQ4Cache::attend
+ * (crates/qx-runtime-v2/src/lib.rs:4791-4863), whose scores, pinned exp,
+ * 256-thread / reduce_simd32 sum and 16 x 32 value chunks are the V1
+ * hierarchical variant's, in the same order. */
+static int granite_decode_impl(const float* query_in, const float* key_in, const float* value, int position,
+                               void* keys, void* values, int key_dtype, int value_dtype, int* length,
+                               int max_context, int hierarchical, int cpu_twin, float* output) {
   float query[G_HIDDEN];
   float key[G_KV_HEADS * G_HEAD_DIM];
   memcpy(query, query_in, sizeof(query));
   memcpy(key, key_in, sizeof(key));
   if (position < 0) return QXO_ERR_POSITION;
-  /* apply_granite_rope :434-442 */
-  if (qxo_rotate_heads(query, G_HEADS, (uint32_t)position) != QXO_OK ||
-      qxo_rotate_heads(key, G_KV_HEADS, (uint32_t)position) != QXO_OK)
+  if (cpu_twin) {
+    /* CpuQ4Reference::step, qx-runtime-v2 lib.rs:4691-4692 */
+    if (qxo_cpu_rotate_heads(query, G_HEADS, (uint32_t)position) != QXO_OK ||
+        qxo_cpu_rotate_heads(key, G_KV_HEADS, (uint32_t)position) != QXO_OK)
+      return QXO_ERR_NONFINITE;
+  } else if (qxo_rotate_heads(query, G_HEADS, (uint32_t)position) != QXO_OK ||
+             qxo_rotate_heads(key, G_KV_HEADS, (uint32_t)position) != QXO_OK) {
+    /* apply_granite_rope :434-442 */
     return QXO_ERR_NONFINITE;
+  }
   /* KvCache::append :382-405 */
   if (position != *length) return QXO_ERR_POSITION;
   if (position >= max_context) return QXO_ERR_POSITION;
@@ -408,6 +438,13 @@ int qxo_granite_attention_decode(const float* query_in, const float* key_in,
   free(scores);
   free(exponentials);
   return status;
+}
+
+int qxo_granite_attention_decode(const float* query_in, const float* key_in, const float* value, int position,
+                                 void* keys, void* values, int key_dtype, int value_dtype, int* length,
+                                 int max_context, int hierarchical, float* output) {
+  return granite_decode_impl(query_in, key_in, value, position, keys, values, key_dtype, value_dtype, length,
+                             max_context, hierarchical, 0, output);
 }
 
 typedef struct {
@@ -709,21 +746,33 @@ void qxo_q4_mat_vec_simd32(const uint8_t* codes, const uint16_t* scales, int row
   }
 }
 
+/* The attention sub-layer of a Granite layer with Q4 weights.
+ * cpu_twin = 0: the arithmetic of the V2 GPU stage encode_attention_layer
+ *   (crates/qx-runtime-v2/src/lib.rs:6916-6994): rms_norm, the Q4 q/k/v
+ *   mat-vecs, RoPE with the fma pair of the Metal kernel qx_v2_rope_kv
+ *   (kernels/v2_decode.metal:244-289, the same operations as V1's
+ *   rotate_heads), attention as V1's plain granite_attention_decode (valid
+ *   to 4096 positions), the Q4 o-projection and the fma residual. This is
+ *   what libqxcuda's qxc_attention_layer computes.
+ * cpu_twin = 1: CpuQ4Reference::step's attention part (lib.rs:4686-4706)
+ *   exactly: cpu_rotate_heads (no fma) and CpuQ4Cache::attend (hierarchical
+ *   sums, at most 512 positions; QXO_ERR_INVALID_ARG beyond, where the
+ *   reference's partials slice panics). */
 int qxo_granite_attention_layer(const float* hidden, const float* input_norm,
                                 const uint8_t* q_codes, const uint16_t* q_scales,
                                 const uint8_t* k_codes, const uint16_t* k_scales,
                                 const uint8_t* v_codes, const uint16_t* v_scales,
                                 const uint8_t* o_codes, const uint16_t* o_scales,
                                 int position, float* keys, float* values, int* length,
-                                int capacity, float* out, float* attention_out) {
+                                int capacity, int cpu_twin, float* out, float* attention_out) {
   float normalized[G_HIDDEN], q[G_HIDDEN], k[G_KV_HEADS * G_HEAD_DIM], v[G_KV_HEADS * G_HEAD_DIM];
   float attention[G_HIDDEN], projection[G_HIDDEN];
   if (!qxo_rms_norm_simd(hidden, input_norm, normalized)) return QXO_ERR_NONFINITE;
   qxo_q4_mat_vec_simd32(q_codes, q_scales, G_HIDDEN, G_HIDDEN, normalized, q);
   qxo_q4_mat_vec_simd32(k_codes, k_scales, G_KV_HEADS * G_HEAD_DIM, G_HIDDEN, normalized, k);
   qxo_q4_mat_vec_simd32(v_codes, v_scales, G_KV_HEADS * G_HEAD_DIM, G_HIDDEN, normalized, v);
-  const int st = qxo_granite_attention_decode(q, k, v, position, keys, values, QXO_F32, QXO_F32, length,
-                                              capacity, 0, attention);
+  const int st = granite_decode_impl(q, k, v, position, keys, values, QXO_F32, QXO_F32, length, capacity,
+                                     cpu_twin ? 1 : 0, cpu_twin ? 1 : 0, attention);
   if (st != QXO_OK) return st;
   if (attention_out) memcpy(attention_out, attention, sizeof(attention));
   qxo_q4_mat_vec_simd32(o_codes, o_scales, G_HIDDEN, G_HIDDEN, attention, projection);

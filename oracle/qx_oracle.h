@@ -65,6 +65,9 @@ float qxo_f16_to_f32(uint16_t h);
 /* rotate_heads (:2439-2453) on `heads` heads of 64 values, in place.
  * Returns QXO_ERR_NONFINITE where the reference panics. */
 int qxo_rotate_heads(float* values, int heads, uint32_t position);
+/* cpu_rotate_heads (qx-runtime-v2 lib.rs:4957-4970), the V2 CPU twin's
+ * RoPE: the same sin/cos, each product and sum rounded separately (no fma). */
+int qxo_cpu_rotate_heads(float* values, int heads, uint32_t position);
 
 /* granite_attention_decode[_simd] (:444-552) on one KvCache.
  * keys/values: [max_context][8][64] of key_dtype / value_dtype elements
@@ -129,9 +132,13 @@ void qxo_q4_quantize(const float* src, int rows, int cols, uint8_t* codes, uint1
 void qxo_q4_mat_vec_simd32(const uint8_t* codes, const uint16_t* scales, int rows, int cols,
                            const float* input, float* out);
 /* One attention sub-layer: normalized = rms_norm(hidden, input_norm);
- * q/k/v = Q4 mat-vecs; attention = granite_attention_decode at `position`
- * on `cache`; out[i] = fma(RESIDUAL_MULTIPLIER = 0.22, o_proj(attention)[i],
- * hidden[i]). Weights as qxo_q4_quantize writes them; attention_out
+ * q/k/v = Q4 mat-vecs; RoPE; attention at `position` on `cache`;
+ * out[i] = fma(RESIDUAL_MULTIPLIER = 0.22, o_proj(attention)[i], hidden[i]).
+ * cpu_twin = 0 follows the V2 GPU stage (qx-runtime-v2 lib.rs:6916-6994:
+ * the Metal fma RoPE, i.e. rotate_heads, and V1's plain attention);
+ * cpu_twin = 1 follows the V2 CPU twin CpuQ4Reference::step exactly
+ * (lib.rs:4686-4706: cpu_rotate_heads, CpuQ4Cache::attend, <= 512
+ * positions). Weights as qxo_q4_quantize writes them; attention_out
  * (optional, [1024]) receives the attention output. Returns QXO_OK or
  * the decode's error status. */
 int qxo_granite_attention_layer(const float* hidden, const float* input_norm,
@@ -140,7 +147,7 @@ int qxo_granite_attention_layer(const float* hidden, const float* input_norm,
                                 const uint8_t* v_codes, const uint16_t* v_scales,
                                 const uint8_t* o_codes, const uint16_t* o_scales,
                                 int position, float* keys, float* values, int* length,
-                                int capacity, float* out, float* attention_out);
+                                int capacity, int cpu_twin, float* out, float* attention_out);
 
 /* ---- KV-slot commitments (qx-commit state.rs:213-251 and :334-368) ---- */
 /* BLAKE3 (the blake3 crate 1.8.7, Cargo.lock:656-657; the published

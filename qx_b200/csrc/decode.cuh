@@ -130,6 +130,8 @@ struct DecodeParams {
   // rank's step counter per (query head, slice); see exchange.cuh
   uint2* xinbox[8];
   unsigned* xstep;
+  unsigned* xfailed;       // the peer group's failed word (device), see mark_peer_group_failed
+  unsigned* xfailed_host;  // and its pinned host copy
   int xrank, xworld;
   void* xout;  // final output [HQ][D]
   int xout_dtype;
@@ -901,6 +903,16 @@ __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_consta
     // peers' matching CTAs are running too.
     constexpr int S = D / 32, ROW = 34;
     const int slice = blk % S, dl = tid >> 2;
+    __shared__ float xml[16];  // m_r, l_r of up to 8 ranks
+    __shared__ int xok;
+    // an earlier exchange on this group timed out: push nothing (one thread
+    // reads the word, so the whole CTA takes one branch)
+    if (tid == 0) xok = peer_group_failed(p.xfailed) ? 0 : 1;
+    __syncthreads();
+    if (!xok) {
+      if (tid == 0) flag_error(p.err, QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER);
+      return;
+    }
     const long long qh = (long long)h * G + g;
     const int W = p.xworld;
     unsigned* stp = p.xstep + qh * S + slice;
@@ -914,10 +926,6 @@ __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_consta
         st_tagged(p.xinbox[r] + mine * ROW + 32, M, tag);
         st_tagged(p.xinbox[r] + mine * ROW + 33, L, tag);
       }
-    __shared__ float xml[16];  // m_r, l_r of up to 8 ranks
-    __shared__ int xok;
-    if (tid == 0) xok = 1;
-    __syncthreads();
     const uint2* in = p.xinbox[p.xrank] + ((long long)half * W * rows + qh * S + slice) * ROW;
     bool ok = true;
     float ov[8];
@@ -934,7 +942,8 @@ __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_consta
       xml[tid] = v;
     }
     if (!ok) {
-      flag_error(p.err, QX_ERR_BIT_TIMEOUT);
+      flag_error(p.err, QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER);
+      mark_peer_group_failed(p.xfailed, p.xfailed_host);
       xok = 0;
     }
     __syncthreads();

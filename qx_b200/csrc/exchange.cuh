@@ -25,7 +25,12 @@
 // current one.
 //
 // Waits are bounded (kMaxWaitNs of %globaltimer): a missing peer turns into
-// QX_ERR_BIT_TIMEOUT, and the CTA returns without merging.
+// QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER, and the CTA returns without merging
+// and marks the peer group failed. Every later exchange on a failed group
+// returns at once with the same error, before it pushes anything: the step
+// counters of the heads that timed out did not advance while the others'
+// did, so the tags no longer tell one step from the next (a slow peer's
+// next push carries the tag this rank still waits for).
 #pragma once
 #include "decode.cuh"
 
@@ -37,6 +42,8 @@ constexpr int kExchThreads = 128;
 struct ExchangeParams {
   uint2* inbox[kMaxPeers];  // every rank's inbox base (index = rank), this rank's own included
   unsigned* step;           // this rank's [HQ] step counters
+  unsigned* failed;         // this rank's group-failed word (device)
+  unsigned* failed_host;    // the same fact for the host (mapped pinned memory)
   int rank, world;
   int hq, d;                // query heads and head dim of the model (d <= kExchThreads)
   const float* partials;    // this rank's [HQ][D+2]
@@ -54,8 +61,6 @@ __global__ void __launch_bounds__(kExchThreads) qx_exchange_merge_kernel(const _
   const int h = blockIdx.x, tid = threadIdx.x;
   const int HQ = p.hq, D = p.d, W = p.world;
   StageTrace trace(p.trace, h, tid == 0);
-  if (tid == 0) s_ok = 1;
-  __syncthreads();
   trace.mark();  // resident
   // the next grid may get resident and set up meanwhile: this grid's CTAs
   // are all resident already (one per query head), and the next grid waits
@@ -63,6 +68,13 @@ __global__ void __launch_bounds__(kExchThreads) qx_exchange_merge_kernel(const _
   pdl_launch_dependents();
   pdl_wait();  // the partials come from the previous grid
   trace.mark();  // partials ready
+  // one thread reads the failed word, so the whole CTA takes one branch
+  if (tid == 0) s_ok = peer_group_failed(p.failed) ? 0 : 1;
+  __syncthreads();
+  if (!s_ok) {
+    if (tid == 0) flag_error(p.err, QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER);
+    return;
+  }
   const unsigned s = p.step[h], tag = s + 1u, half = s & 1u;
   // 1. push this rank's head-h partial into every rank's inbox [half][rank][h]
   const long long slot = (((long long)half * W + p.rank) * HQ + h) * (D + 2);
@@ -90,7 +102,8 @@ __global__ void __launch_bounds__(kExchThreads) qx_exchange_merge_kernel(const _
     ml[tid] = v;
   }
   if (!ok) {
-    flag_error(p.err, QX_ERR_BIT_TIMEOUT);
+    flag_error(p.err, QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER);
+    mark_peer_group_failed(p.failed, p.failed_host);
     s_ok = 0;
   }
   __syncthreads();

@@ -19,8 +19,13 @@
 // Rules that come with a shared static buffer:
 //  - The first call on each device does a one-time set-up with that device
 //    current: it looks up the array's device address (cudaGetSymbolAddress)
-//    and sets the kernel's shared-memory attribute. Make that first call
-//    before any stream capture on the device.
+//    and, per KV precision, sets the kernel's shared-memory attribute. Make
+//    that first call before any stream capture on the device. The set-up
+//    runs once per device even when several host threads call at once.
+//  - With split 0 the split comes from the wave model of qxc_decode
+//    (qxc_auto_split), limited to the splits whose partials fit the array
+//    (30 for one Granite layer). The merge of the splits always runs inside
+//    the decode kernel (the last CTA of each kv head), whatever their number.
 //  - All calls on a device share the one array and it keeps the last call's
 //    contents. The merge tickets that must start at zero are cleared by each
 //    call (an asynchronous memset on the caller's stream). Two calls whose
@@ -32,6 +37,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -45,15 +51,35 @@ namespace {
 
 constexpr size_t kStaticScratchBytes = 128 * 1024;
 constexpr size_t kTicketBytes = 256;  // 8 kv-head tickets, padded to the alignment
+constexpr size_t kPartialBytes = 2 * (64 + 2) * sizeof(float);  // one work item's (O, m, l) for 2 query heads
+// Splits of the one (sequence, layer) a call decodes that fit the array:
+// 8 kv-head work items per split.
+constexpr int kStaticMaxSplits = (int)((kStaticScratchBytes - kTicketBytes) / (8 * kPartialBytes));
 
 // The scratch: [0, kTicketBytes) merge tickets, then split partials.
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 constexpr int kMaxDevices = 64;
-std::mutex g_setup_mutex;
-void* g_scratch_addr[kMaxDevices] = {};
-int g_sm_count[kMaxDevices] = {};
-unsigned g_configured[kMaxDevices] = {};  // bit per (key, value) dtype pair
+constexpr int kPairs = 5;  // accepted (key, value) dtype pairs
+
+// One-time set-up, race-free when several host threads make their first
+// call at once: std::call_once per device (the scratch address, the SM
+// count) and per (device, dtype pair) (the kernel's shared-memory attribute
+// and its resident CTAs per SM). Each slot is written inside its call_once
+// and only read after it, which call_once orders.
+struct DeviceSetup {
+  std::once_flag once;
+  cudaError_t status = cudaSuccess;
+  void* scratch = nullptr;
+  int sm_count = 0;
+};
+struct KernelSetup {
+  std::once_flag once;
+  cudaError_t status = cudaSuccess;
+  int blocks_per_sm = 1;
+};
+DeviceSetup g_device[kMaxDevices];
+KernelSetup g_kernel[kMaxDevices][kPairs];
 
 qxc_status say(char* msg, size_t len, qxc_status st, const char* text) {
   if (msg && len) snprintf(msg, len, "%s", text);
@@ -62,16 +88,22 @@ qxc_status say(char* msg, size_t len, qxc_status st, const char* text) {
 
 size_t esize(int dt) { return dt == QXC_F32 ? 4 : 2; }
 
-qxc_status encode_map(CUtensorMap* map, void* base, int dtype, int capacity, char* msg, size_t len) {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
+  std::call_once(once, [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return say(msg, len, QXC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+qxc_status encode_map(CUtensorMap* map, void* base, int dtype, int capacity, char* msg, size_t len) {
+  const PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return say(msg, len, QXC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const size_t es = esize(dtype);
   const CUtensorMapDataType t = dtype == QXC_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                 : dtype == QXC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -86,17 +118,49 @@ qxc_status encode_map(CUtensorMap* map, void* base, int dtype, int capacity, cha
   return QXC_OK;
 }
 
+// The kernel's set-up on this device (with it current): shared-memory
+// attribute, then resident CTAs per SM for the split model.
 template <typename KT, typename VT>
-qxc_status launch(const DecodeParams& p, int items, int dev, unsigned bit, cudaStream_t stream, char* msg,
-                  size_t len) {
+const KernelSetup& kernel_setup(int dev, int pair) {
+  KernelSetup& k = g_kernel[dev][pair];
+  std::call_once(k.once, [&k] {
+    using C = DecodeCfg<Granite, KT, VT>;
+    k.status = cudaFuncSetAttribute(qx_decode_kernel<Granite, KT, VT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::SMEM);
+    int n = 1;
+    if (k.status == cudaSuccess)
+      k.status = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qx_decode_kernel<Granite, KT, VT>, C::NT, C::SMEM);
+    k.blocks_per_sm = n > 0 ? n : 1;
+  });
+  return k;
+}
+
+template <typename KT, typename VT>
+qxc_status launch(DecodeParams& p, int attend, int split, const DeviceSetup& ds, int dev, int pair,
+                  cudaStream_t stream, char* msg, size_t len) {
   using C = DecodeCfg<Granite, KT, VT>;
-  if (!(g_configured[dev] & bit)) {
-    std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (cudaFuncSetAttribute(qx_decode_kernel<Granite, KT, VT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::SMEM) != cudaSuccess)
-      return say(msg, len, QXC_ERR_CUDA, "cudaFuncSetAttribute failed");
-    g_configured[dev] |= bit;
+  const KernelSetup& ks = kernel_setup<KT, VT>(dev, pair);
+  if (ks.status != cudaSuccess) return say(msg, len, QXC_ERR_CUDA, cudaGetErrorString(ks.status));
+  const int max_splits = std::min(kStaticMaxSplits, C::MAX_SPLITS);
+  // the split: the same wave model qxc_decode uses (qxc_auto_split), over
+  // the splits that fit the array
+  int chunk = split;
+  if (chunk == 0) chunk = qxc_auto_split(ds.sm_count * ks.blocks_per_sm, &attend, 1, 8, max_splits, C::T);
+  if (chunk <= 0) return say(msg, len, QXC_ERR_INVALID_ARG, "no split fits the static scratch");
+  const int nsplit = (attend + chunk - 1) / chunk;
+  const int items = nsplit * 8;
+  const size_t need = kTicketBytes + (size_t)items * kPartialBytes;
+  if (need > kStaticScratchBytes) {
+    char buf[160];
+    snprintf(buf, sizeof(buf),
+             "split-KV scratch of %zu bytes exceeds the static scratch of %zu bytes; use a larger split",
+             need, kStaticScratchBytes);
+    return say(msg, len, QXC_ERR_INVALID_ARG, buf);
   }
+  p.chunk = chunk;
+  // Tickets must start at zero; the array keeps whatever the last call left.
+  if (cudaMemsetAsync(p.tickets, 0, kTicketBytes, stream) != cudaSuccess)
+    return say(msg, len, QXC_ERR_CUDA, "clearing the static scratch failed");
   qx_decode_kernel<Granite, KT, VT><<<items, C::NT, C::SMEM, stream>>>(p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return say(msg, len, QXC_ERR_CUDA, cudaGetErrorString(e));
@@ -135,41 +199,18 @@ extern "C" qxc_status qxc_granite_decode_static_scratch(const qxc_static_decode_
 
   // One-time set-up on this device (with it current): the device address of
   // the static scratch and the SM count used to size the split.
-  if (!g_scratch_addr[dev]) {
-    std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (!g_scratch_addr[dev]) {
-      void* ptr = nullptr;
-      const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
-      if (e != cudaSuccess) return say(msg, len, QXC_ERR_CUDA, cudaGetErrorString(e));
-      int sms = 148;
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      g_sm_count[dev] = sms;
-      g_scratch_addr[dev] = ptr;
-    }
-  }
+  DeviceSetup& ds = g_device[dev];
+  std::call_once(ds.once, [&ds, dev] {
+    void* ptr = nullptr;
+    ds.status = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    int sms = 0;
+    if (ds.status == cudaSuccess) ds.status = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    ds.scratch = ptr;
+    ds.sm_count = sms > 0 ? sms : 1;
+  });
+  if (ds.status != cudaSuccess) return say(msg, len, QXC_ERR_CUDA, cudaGetErrorString(ds.status));
 
-  // Work decomposition, as qxc_decode plans a single (sequence, layer).
   const int attend = a->position + 1;
-  int chunk = a->split;
-  if (chunk == 0) {
-    const long long target = (long long)g_sm_count[dev] * 8;
-    long long c = ((long long)attend * 8 + target - 1) / target;
-    c = c < 256 ? 256 : c;
-    c = ((c + 63) / 64) * 64;
-    const long long cap = ((attend + 63) / 64) * 64;
-    chunk = (int)(c < cap ? c : cap);
-  }
-  const int nsplit = (attend + chunk - 1) / chunk;
-  const int items = nsplit * 8;
-  const size_t need = kTicketBytes + (size_t)items * 2 * (64 + 2) * sizeof(float);
-  if (need > kStaticScratchBytes) {
-    char buf[160];
-    snprintf(buf, sizeof(buf),
-             "split-KV scratch of %zu bytes exceeds the static scratch of %zu bytes; use a larger split",
-             need, kStaticScratchBytes);
-    return say(msg, len, QXC_ERR_INVALID_ARG, buf);
-  }
-
   DecodeParams p;
   memset(&p, 0, sizeof(p));
   qxc_status st = encode_map(&p.tmk, a->key_cache, kd, a->capacity, msg, len);
@@ -189,7 +230,6 @@ extern "C" qxc_status qxc_granite_decode_static_scratch(const qxc_static_decode_
   p.single.new_slot = a->position;
   p.single.rope_pos = a->position;
   p.single.item_begin = 0;
-  p.chunk = chunk;
   p.q = a->q;
   p.k = a->k;
   p.v = a->v;
@@ -199,20 +239,16 @@ extern "C" qxc_status qxc_granite_decode_static_scratch(const qxc_static_decode_
   p.out_dtype = a->out_dtype;
   p.pinned_exp = (a->flags & QXC_DECODE_NATIVE_EXP) ? 0 : 1;
   p.emit_partials = 0;
-  unsigned char* scratch = static_cast<unsigned char*>(g_scratch_addr[dev]);
+  unsigned char* scratch = static_cast<unsigned char*>(ds.scratch);
   p.tickets = reinterpret_cast<int*>(scratch);
   p.partials = reinterpret_cast<float*>(scratch + kTicketBytes);
   p.err = a->device_error;
 
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
-  // Tickets must start at zero; the array keeps whatever the last call left.
-  if (cudaMemsetAsync(scratch, 0, kTicketBytes, stream) != cudaSuccess)
-    return say(msg, len, QXC_ERR_CUDA, "clearing the static scratch failed");
-
-  const unsigned bit = 1u << (kd * 3 + vd);
-  if (kd == QXC_F32 && vd == QXC_F32) return launch<float, float>(p, items, dev, bit, stream, msg, len);
-  if (kd == QXC_F32 && vd == QXC_F16) return launch<float, __half>(p, items, dev, bit, stream, msg, len);
-  if (kd == QXC_F16 && vd == QXC_F32) return launch<__half, float>(p, items, dev, bit, stream, msg, len);
-  if (kd == QXC_F16 && vd == QXC_F16) return launch<__half, __half>(p, items, dev, bit, stream, msg, len);
-  return launch<__nv_bfloat16, __nv_bfloat16>(p, items, dev, bit, stream, msg, len);
+  const int split = a->split;
+  if (kd == QXC_F32 && vd == QXC_F32) return launch<float, float>(p, attend, split, ds, dev, 0, stream, msg, len);
+  if (kd == QXC_F32 && vd == QXC_F16) return launch<float, __half>(p, attend, split, ds, dev, 1, stream, msg, len);
+  if (kd == QXC_F16 && vd == QXC_F32) return launch<__half, float>(p, attend, split, ds, dev, 2, stream, msg, len);
+  if (kd == QXC_F16 && vd == QXC_F16) return launch<__half, __half>(p, attend, split, ds, dev, 3, stream, msg, len);
+  return launch<__nv_bfloat16, __nv_bfloat16>(p, attend, split, ds, dev, 4, stream, msg, len);
 }

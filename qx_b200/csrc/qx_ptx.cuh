@@ -13,6 +13,24 @@ namespace qx {
 // Error-word bits (qxc_sync maps them to status codes).
 constexpr unsigned QX_ERR_BIT_NONFINITE = 0x1u;
 constexpr unsigned QX_ERR_BIT_TIMEOUT = 0x2u;
+// An exchange with peer ranks gave up (or found its peer group already
+// failed): qxc_sync reports QXC_ERR_TIMEOUT and names the peer group.
+constexpr unsigned QX_ERR_BIT_PEER = 0x4u;
+
+// A peer group that has seen a timed-out exchange is failed for good. Its
+// ranks' step counters no longer agree (the heads that timed out did not
+// advance, the others did), so a later exchange could take a peer's earlier
+// push, which carries the same tag, for the current one. The first CTA to
+// give up stores 1 into the group's device word (read by every later
+// exchange kernel before it pushes anything) and into its pinned host word
+// (read by the host before every later exchange call).
+__device__ __forceinline__ bool peer_group_failed(const unsigned* failed) {
+  return failed && *reinterpret_cast<const volatile unsigned*>(failed) != 0u;
+}
+__device__ __forceinline__ void mark_peer_group_failed(unsigned* failed, unsigned* failed_host) {
+  if (failed) *reinterpret_cast<volatile unsigned*>(failed) = 1u;
+  if (failed_host) *reinterpret_cast<volatile unsigned*>(failed_host) = 1u;
+}
 
 // Record a device-side error. The word lives in mapped pinned host memory;
 // a plain volatile store (no read-modify-write) is enough because the host

@@ -95,6 +95,12 @@ struct qxc_peer_group {
   size_t bytes = 0, off_xinbox = 0, off_step = 0;
   char* peer[kMaxPeers] = {};    // every rank's base as seen from this device
   bool opened[kMaxPeers] = {};   // opened through CUDA IPC (closed on destroy)
+  // Set (by the device) once an exchange on this group has timed out; from
+  // then on every exchange call on it fails (see mark_peer_group_failed).
+  unsigned* failed_host = nullptr;  // mapped pinned word
+  unsigned* failed_mapped = nullptr;  // its device address
+  unsigned* failed_dev() const { return reinterpret_cast<unsigned*>(base + off_step + 768); }
+  bool failed() const { return *reinterpret_cast<volatile unsigned*>(failed_host) != 0u; }
 };
 
 struct qxc_kv {
@@ -1024,6 +1030,10 @@ qxc_status qxc_sync(qxc_ctx* ctx) {
       cudaMemsetAsync(ctx->tickets, 0, ctx->tickets_cap * sizeof(int), ctx->stream);
       cudaStreamSynchronize(ctx->stream);
     }
+    if (e & QX_ERR_BIT_PEER)
+      return fail(ctx, QXC_ERR_TIMEOUT,
+                  "a bounded device-side wait gave up: an exchange with a peer rank timed out, and its peer group "
+                  "is failed (destroy and re-create the groups on every rank)");
     if (e & QX_ERR_BIT_TIMEOUT) return fail(ctx, QXC_ERR_TIMEOUT, "a bounded device-side wait gave up");
     return fail(ctx, QXC_ERR_NONFINITE, "non-finite value in RoPE or attention (the reference panics here)");
   }
@@ -1765,6 +1775,8 @@ static qxc_status decode_partials_impl(qxc_ctx* ctx, qxc_kv* kv, const qxc_parti
     p.external_merge = 1;
     for (int r = 0; r < g->world; ++r) p.xinbox[r] = reinterpret_cast<uint2*>(g->peer[r] + g->off_xinbox);
     p.xstep = reinterpret_cast<unsigned*>(g->base + g->off_step) + kExchHeads;
+    p.xfailed = g->failed_dev();
+    p.xfailed_host = g->failed_mapped;
     p.xrank = g->rank;
     p.xworld = g->world;
     p.xout = xout;
@@ -1799,6 +1811,12 @@ qxc_status qxc_lse_merge(qxc_ctx* ctx, int32_t model, int32_t n_parts, const flo
 
 // ---- exchange over NVLink (KV-length split across GPUs) --------------------------
 
+static qxc_status peer_group_failed_error(qxc_ctx* ctx) {
+  return fail(ctx, QXC_ERR_TIMEOUT,
+              "peer group failed: an earlier exchange on it timed out (destroy and re-create the groups on every "
+              "rank)");
+}
+
 qxc_status qxc_peer_group_create(qxc_ctx* ctx, int32_t rank, int32_t world, qxc_peer_group** out) {
   if (!ctx || !out) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
   *out = nullptr;
@@ -1814,16 +1832,27 @@ qxc_status qxc_peer_group_create(qxc_ctx* ctx, int32_t rank, int32_t world, qxc_
   const size_t xinbox = (size_t)2 * world * kExchHeads * 4 * 34 * sizeof(uint2);
   g->off_xinbox = (inbox + 255) / 256 * 256;
   g->off_step = g->off_xinbox + (xinbox + 255) / 256 * 256;
-  g->bytes = g->off_step + 1024;  // [32] exchange-kernel steps, then [32][4] split-merge steps
+  // [32] exchange-kernel steps, then [32][4] split-merge steps, then (at
+  // byte 768) the group-failed word
+  g->bytes = g->off_step + 1024;
   const size_t bytes = g->bytes;
-  cudaError_t e = cudaMalloc(&g->base, bytes);
+  cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&g->failed_host), sizeof(unsigned), cudaHostAllocMapped);
   if (e != cudaSuccess) {
+    delete g;
+    return fail(ctx, QXC_ERR_OUT_OF_MEMORY, "pinned group word: %s", cudaGetErrorString(e));
+  }
+  *g->failed_host = 0u;
+  e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&g->failed_mapped), g->failed_host, 0);
+  if (e == cudaSuccess) e = cudaMalloc(&g->base, bytes);
+  if (e != cudaSuccess) {
+    cudaFreeHost(g->failed_host);
     delete g;
     return fail(ctx, QXC_ERR_OUT_OF_MEMORY, "exchange area of %zu bytes: %s", bytes, cudaGetErrorString(e));
   }
   e = cudaMemset(g->base, 0, g->bytes);
   if (e != cudaSuccess) {
     cudaFree(g->base);
+    cudaFreeHost(g->failed_host);
     delete g;
     return fail(ctx, QXC_ERR_CUDA, "cudaMemset: %s", cudaGetErrorString(e));
   }
@@ -1839,6 +1868,7 @@ void qxc_peer_group_destroy(qxc_peer_group* g) {
   for (int r = 0; r < g->world; ++r)
     if (g->opened[r]) cudaIpcCloseMemHandle(g->peer[r]);
   cudaFree(g->base);
+  cudaFreeHost(g->failed_host);
   delete g;
 }
 
@@ -1904,6 +1934,7 @@ qxc_status qxc_exchange_merge(qxc_ctx* ctx, qxc_peer_group* g, int32_t model, co
   if (!valid_dtype(out_dtype)) return fail(ctx, QXC_ERR_INVALID_ARG, "unknown dtype");
   if (model != QXC_MODEL_QWEN3 && model != QXC_MODEL_GRANITE)
     return fail(ctx, QXC_ERR_INVALID_ARG, "unknown model %d", model);
+  if (g->failed()) return peer_group_failed_error(ctx);
   ExchangeParams p;
   memset(&p, 0, sizeof(p));
   for (int r = 0; r < g->world; ++r) {
@@ -1911,6 +1942,8 @@ qxc_status qxc_exchange_merge(qxc_ctx* ctx, qxc_peer_group* g, int32_t model, co
     p.inbox[r] = reinterpret_cast<uint2*>(g->peer[r]);
   }
   p.step = reinterpret_cast<unsigned*>(g->base + g->off_step);
+  p.failed = g->failed_dev();
+  p.failed_host = g->failed_mapped;
   p.rank = g->rank;
   p.world = g->world;
   p.hq = model == QXC_MODEL_QWEN3 ? 32 : 16;
@@ -1944,6 +1977,7 @@ qxc_status qxc_decode_exchange(qxc_ctx* ctx, qxc_kv* kv, const qxc_partial_args*
   if (!valid_dtype(out_dtype)) return fail(ctx, QXC_ERR_INVALID_ARG, "unknown dtype");
   for (int r = 0; r < g->world; ++r)
     if (!g->peer[r]) return fail(ctx, QXC_ERR_INVALID_ARG, "peer %d is not attached", r);
+  if (g->failed()) return peer_group_failed_error(ctx);
   if ((kv->desc.model == QXC_MODEL_QWEN3 ? 32 : 16) * (kv->d / 32) > ctx->sm_count * 8)
     return fail(ctx, QXC_ERR_UNSUPPORTED, "the merge grid must fit one wave");
   return decode_partials_impl(ctx, kv, a, g, out, out_dtype);

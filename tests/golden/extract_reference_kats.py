@@ -17,8 +17,9 @@ import os
 import re
 import sys
 
-REF = os.environ.get("QX_REFERENCE", "/root/reference")
 HERE = os.path.dirname(os.path.abspath(__file__))
+# the reference tree: the first argument, else $QX_REFERENCE
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QX_REFERENCE", "")
 
 
 def _hexes(text):
@@ -26,6 +27,8 @@ def _hexes(text):
 
 
 def main():
+    if not REF or not os.path.isdir(REF):
+        sys.exit("usage: extract_reference_kats.py <path of the blasrodri/qx tree> (or set QX_REFERENCE)")
     math_src = open(os.path.join(REF, "crates/qx-consensus-math/src/lib.rs")).read()
     lines = math_src.splitlines()
 

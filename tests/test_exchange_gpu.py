@@ -97,16 +97,21 @@ def test_fused_exchange_missing_peer_times_out(gpu_ctx):
     out = torch.zeros(4096, device="cuda")
     a.decode_exchange(conv(syn.normal(1, (1, 4096))), conv(syn.normal(2, (1, 512))), conv(syn.normal(3, (1, 512))),
                       out, 1999, append=True, group=g0, split=256)
-    with pytest.raises(QxError, match="bounded device-side wait"):
+    with pytest.raises(QxError, match="peer group is failed"):
         gpu_ctx.sync()
+    # the heads' step counters no longer agree: the group refuses further use
+    with pytest.raises(QxError, match="peer group failed"):
+        a.decode_exchange(conv(syn.normal(4, (1, 4096))), conv(syn.normal(5, (1, 512))),
+                          conv(syn.normal(6, (1, 512))), out, 2000, append=True, group=g0, split=256)
     g0.close()
     g1.close()
 
 
 def test_exchange_missing_peer_times_out(gpu_ctx):
     """Rank 0 of two, the second rank's area attached but never run: every
-    head's wait runs out (about a second), sync reports the timeout, and the
-    context keeps working."""
+    head's wait runs out (about a second), sync reports the timeout, the peer
+    group is failed from then on (an exchange already enqueued does nothing,
+    a later call is refused), and the context keeps working."""
     import torch
     g0, g1 = PeerGroup(gpu_ctx, 0, 2), PeerGroup(gpu_ctx, 1, 2)
     g0.set_peer(1, g1.base())
@@ -115,8 +120,16 @@ def test_exchange_missing_peer_times_out(gpu_ctx):
     parts[:, 129] = 1.0   # l
     out = torch.zeros(4096, device="cuda")
     g0.exchange_merge(MODEL_QWEN3, parts, out)
-    with pytest.raises(QxError, match="bounded device-side wait"):
+    # enqueued before the failure is known: its kernel finds the group failed
+    # and returns at once, pushing and merging nothing
+    out2 = torch.full((4096,), 7.0, device="cuda")
+    g0.exchange_merge(MODEL_QWEN3, parts, out2)
+    with pytest.raises(QxError, match="peer group is failed"):
         gpu_ctx.sync()
+    assert torch.all(out2 == 7.0)
+    # after the failure is recorded, the group refuses every exchange call
+    with pytest.raises(QxError, match="peer group failed"):
+        g0.exchange_merge(MODEL_QWEN3, parts, out)
     y = torch.zeros(4096, device="cuda")
     gpu_ctx.lse_merge(MODEL_QWEN3, 1, parts, y)
     gpu_ctx.sync()

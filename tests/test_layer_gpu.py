@@ -1,10 +1,20 @@
 """The attention sub-layer with Q4 projections (qxc_q4_mat_vec,
-qxc_attention_layer) against the oracle's restatement of the reference's CPU
-layer (qx-runtime-v2 CpuQ4Reference::step, lib.rs:4680-4706).
+qxc_attention_layer) against the oracle.
 
-The RMSNorm and Q4 mat-vec keep the reference's lane order, so q/k/v, the
-appended key row and the projections are bit-exact; the layer output, which
-passes through the attention, is within the fp32 gate (1e-5 normwise).
+qxc_attention_layer computes the V2 GPU stage (qx-runtime-v2
+encode_attention_layer, lib.rs:6916-6994): RMSNorm, Q4 q/k/v, the fma RoPE
+of the Metal kernel qx_v2_rope_kv (the same operations as V1's
+rotate_heads), attention, Q4 o-projection, fma residual. The oracle's
+default layer restates exactly that: the RMSNorm and Q4 mat-vec keep the
+reference's lane order, so q/k/v, the appended rows and the projections are
+bit-exact, and the outputs, which pass through the attention, are within the
+fp32 gate (1e-5 normwise).
+
+The V2 CPU twin CpuQ4Reference::step (lib.rs:4680-4706) rotates without fma
+(cpu_rotate_heads) and attends with hierarchical sums up to 512 positions;
+against it the value rows are bit-exact, the key rows differ in the RoPE's
+last bits, and the outputs stay within the same 1e-5 gate and the
+reference's own V2 gate (0.01 absolute, tools/qx-bench/src/main.rs:11064-11076).
 """
 import sys
 import os
@@ -129,3 +139,28 @@ def test_attention_layers_chained(gpu_ctx, oracle):
         gpu_ctx.sync()
         assert normwise(cur.cpu().numpy(), ref) <= 1e-5
     assert arena.len(0) == prefix + tokens
+
+
+def test_attention_layer_against_cpu_twin(gpu_ctx, oracle):
+    """qxc_attention_layer against the V2 CPU twin (CpuQ4Reference::step's
+    attention part), up to the twin's 512 positions."""
+    import torch
+    layers, prefix, cap = 1, 490, 512
+    W, dW, arena, caches = layer_setup(gpu_ctx, oracle, layers, prefix, cap)
+    twin = caches[0]
+    for t in range(cap - prefix):
+        h = syn.normal(0x8480 + t, (1024,))
+        st, ref, att_ref = oracle.granite_attention_layer(h, W[0]["norm"], W[0]["q"], W[0]["k"], W[0]["v"],
+                                                          W[0]["o"], prefix + t, twin, cpu_twin=True)
+        assert st == 0
+        out = torch.zeros(1024, device="cuda")
+        att = torch.zeros(1024, device="cuda")
+        arena.attention_layer(torch.from_numpy(h).cuda(), out, dW[0]["norm"], dW[0]["q"], dW[0]["k"], dW[0]["v"],
+                              dW[0]["o"], prefix + t, layer=0, attention_out=att)
+        gpu_ctx.sync()
+        a, o = att.cpu().numpy(), out.cpu().numpy()
+        assert normwise(a, att_ref) <= 1e-5 and normwise(o, ref) <= 1e-5, t
+        assert np.abs(a - att_ref).max() <= 0.01
+    gk, gv = arena.read(0, 0, 0, cap)
+    assert np.array_equal(gv.view(np.uint32), twin.values[:cap].view(np.uint32))
+    assert np.abs(gk - twin.keys[:cap]).max() <= 1e-5

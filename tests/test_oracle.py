@@ -7,6 +7,9 @@ import struct
 import numpy as np
 import pytest
 
+from helpers import normwise
+from qx_b200 import synthetic as syn
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 KATS = json.load(open(os.path.join(HERE, "golden", "consensus_math_kats.json")))
 
@@ -226,6 +229,64 @@ def test_attention_layer_oracle_composes_its_parts(oracle):
     o = W[3].mat_vec(att2)
     assert np.array_equal(out, (np.float32(0.22) * o.astype(np.float64) + h).astype(np.float32)) or \
         np.abs(out - (0.22 * o.astype(np.float64) + h)).max() <= 1e-6
+
+
+def test_cpu_rotate_heads_is_the_no_fma_pair(oracle):
+    """cpu_rotate_heads (qx-runtime-v2 lib.rs:4957-4970): left*cos - right*sin
+    and left*sin + right*cos, each product and sum rounded on its own (float32
+    numpy arithmetic rounds every operation), with the pinned sin/cos."""
+    import ctypes as C
+    x = syn.normal(0x9100, (24 * 64,))
+    for position in (0, 1, 7, 511, 4095):
+        got = x.copy()
+        assert oracle.lib().qxo_cpu_rotate_heads(oracle._fp(got), 24, position) == 0
+        s = np.zeros(32, np.float32)
+        c = np.zeros(32, np.float32)
+        for pair in range(32):
+            ss, cc = C.c_float(), C.c_float()
+            assert oracle.lib().qxo_granite_rope_sin_cos(position, pair, C.byref(ss), C.byref(cc)) == 1
+            s[pair], c[pair] = ss.value, cc.value
+        h = x.reshape(24, 64)
+        left, right = h[:, :32], h[:, 32:]
+        exp = np.concatenate([left * c - right * s, left * s + right * c], axis=1).reshape(-1)
+        assert np.array_equal(got.view(np.uint32), exp.view(np.uint32))
+        # rotate_heads (fma) differs from it in the last bits only
+        fma = x.copy()
+        assert oracle.lib().qxo_rotate_heads(oracle._fp(fma), 24, position) == 0
+        assert np.abs(fma - got).max() <= 4e-7 * np.abs(x).max() * 4
+
+
+def test_attention_layer_cpu_twin(oracle):
+    """The V2 CPU twin (CpuQ4Reference::step) against the V2 GPU stage's form:
+    the value rows are bit-identical (no RoPE on v), the key rows differ only
+    by the RoPE rounding, outputs agree within 1e-5 normwise over 40 steps;
+    the twin stops past 512 positions, as the reference's partials slice."""
+    rng = np.random.default_rng(11)
+    W = [oracle.Q4Matrix((rng.standard_normal(s) * 0.05).astype(np.float32))
+         for s in ((1024, 1024), (512, 1024), (512, 1024), (1024, 1024))]
+    norm = (1.0 + 0.1 * rng.standard_normal(1024)).astype(np.float32)
+    cap, prefix = 520, 470
+    kc = syn.normal(0x9200, (prefix, 8, 64))
+    vc = syn.normal(0x9201, (prefix, 8, 64))
+    gpu_form, twin = oracle.KvCache(cap), oracle.KvCache(cap)
+    for c in (gpu_form, twin):
+        c.keys[:prefix], c.values[:prefix] = kc, vc
+        c.length.value = prefix
+    worst = 0.0
+    for t in range(42):
+        h = syn.normal(0x9300 + t, (1024,))
+        st, out, att = oracle.granite_attention_layer(h, norm, *W, prefix + t, gpu_form)
+        st2, out2, att2 = oracle.granite_attention_layer(h, norm, *W, prefix + t, twin, cpu_twin=True)
+        assert st == 0 and st2 == 0
+        worst = max(worst, normwise(att2, att), normwise(out2, out))
+    assert worst <= 1e-5
+    n = prefix + 42
+    assert np.array_equal(twin.values[:n].view(np.uint32), gpu_form.values[:n].view(np.uint32))
+    assert not np.array_equal(twin.keys[prefix:n], gpu_form.keys[prefix:n])
+    assert np.abs(twin.keys[:n] - gpu_form.keys[:n]).max() <= 1e-5
+    # position 512 makes the twin attend over 513 rows: its 16 x 32 value chunks end at 512
+    st, _, _ = oracle.granite_attention_layer(syn.normal(1, (1024,)), norm, *W, n, twin, cpu_twin=True)
+    assert st == oracle.ERR_INVALID_ARG
 
 
 # ---- KV-slot commitments (qx-commit state.rs:213-251, :334-368) ----------------------
