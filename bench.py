@@ -10,11 +10,14 @@ reference's speculative rollback does), so every step reads ~400 MB of KV,
 far more than the 126 MB L2.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload config1|config0|config2|config3|config4|layer|commit|verify]
+                    [--workload config1|config0|config2|config3|config4|layer|commit|verify|sweep]
 
-Prints one JSON line on rank 0. N>1 runs under torchrun: one independent
-sequence (replica) per GPU, no collective on the data path ("weak" scaling),
-device time max-reduced over ranks. `--impl reference` times the CPU
+Prints one JSON line on rank 0 (`sweep`: one per context 512/2048/4096). N>1
+runs under torchrun: one independent sequence (replica) per GPU, no
+collective on the data path ("weak" scaling), device time max-reduced over
+ranks. The config-1 line also carries `sharded`: config 4 (256 sequences)
+sharded over the N ranks by LPT on KV bytes, with the one-GPU value of the
+same run and the efficiency against N times it. `--impl reference` times the CPU
 restatement of qx's GQA path (oracle/, the reference being Rust and not
 buildable here) with all host threads on the same workload.
 """
@@ -685,10 +688,15 @@ def run_config3(args, world, rank, local):
 
 def run_layer(args, world, rank, local):
     """The attention sub-layers of the Granite stack with Q4 weights (the
-    reference's encode_attention_layer: RMSNorm, Q4 q/k/v, RoPE + append +
-    attention, Q4 o-projection, residual), 24 layers per token, fp32 KV at
-    context --context, positions cycled over the last 64 like config 1.
-    Random Q4 codes and FP16 scales stand in for the .qx weights."""
+    reference's --v2-attention-stack: PreparedAttentionStack::encode runs
+    encode_attention_layer for each of the 24 layers, the hidden state
+    chained from layer to layer: RMSNorm, Q4 q/k/v, RoPE + append +
+    attention, Q4 o-projection, residual), fp32 KV at context --context,
+    positions cycled over the last 64 like config 1. One qxc_attention_stack
+    call per token (one persistent launch for all 24 layers); with
+    --layer-chain, qxc_attention_layer per layer instead (four launches per
+    layer, captured in a CUDA graph). Random Q4 codes and FP16 scales stand
+    in for the .qx weights."""
     import torch
     from qx_b200 import F32, MODEL_GRANITE, Context, KvArena, Q4Weights
     from qx_b200 import _lib
@@ -719,39 +727,69 @@ def run_layer(args, world, rank, local):
     stream.synchronize()
     arena.set_len(0, P)
 
-    def one(i):
-        pos = P + i % cycle
-        for l in range(LAYERS):
-            w = weights[l]
-            arena.attention_layer(hidden[l % 2], hidden[(l + 1) % 2], w["norm"], w["q"], w["k"], w["v"], w["o"],
-                                  pos, layer=l, flags=_lib.DECODE_NO_ADVANCE if l + 1 < LAYERS else 0,
-                                  split=args.split)
+    if args.layer_chain:
+        def one(i):
+            pos = P + i % cycle
+            for l in range(LAYERS):
+                w = weights[l]
+                arena.attention_layer(hidden[l % 2], hidden[(l + 1) % 2], w["norm"], w["q"], w["k"], w["v"],
+                                      w["o"], pos, layer=l, flags=_lib.DECODE_NO_ADVANCE if l + 1 < LAYERS else 0,
+                                      split=args.split)
 
-    # one step is 72 launches of a few microseconds each: capture a whole
-    # cycle of 64 tokens in a CUDA graph and replay it (the host cursor is
-    # rewound before each replay; the graph's kernels carry their positions)
-    with torch.cuda.stream(stream):
-        for i in range(3):
-            one(i)
-    stream.synchronize()
-    arena.rollback(0, P)
-    graph = torch.cuda.CUDAGraph()
-    n0 = ctx.launch_count
-    with torch.cuda.graph(graph, stream=stream):
-        for i in range(cycle):
-            one(i)
-    per_replay = ctx.launch_count - n0
-
-    def replay(i):
+        # one step is 72 launches of a few microseconds each: capture a whole
+        # cycle of 64 tokens in a CUDA graph and replay it (the host cursor is
+        # rewound before each replay; the graph's kernels carry their positions)
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                one(i)
+        stream.synchronize()
         arena.rollback(0, P)
-        graph.replay()
+        graph = torch.cuda.CUDAGraph()
+        n0 = ctx.launch_count
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(cycle):
+                one(i)
+        per_replay = ctx.launch_count - n0
 
-    K, W = max(1, args.steps // cycle), max(3, args.warmup // cycle)
-    with torch.cuda.stream(stream):
-        total, per, clk, _ = timed_steps(replay, K, W, stream, world, dev, local, ctx)
-    stream.synchronize()
-    per = [x / cycle for x in per]  # per token
-    steps = K * cycle
+        def replay(i):
+            arena.rollback(0, P)
+            graph.replay()
+
+        K, W = max(1, args.steps // cycle), max(3, args.warmup // cycle)
+        with torch.cuda.stream(stream):
+            total, per, clk, _ = timed_steps(replay, K, W, stream, world, dev, local, ctx)
+        stream.synchronize()
+        per = [x / cycle for x in per]  # per token
+        steps = K * cycle
+        launches = K * per_replay
+        kernel = "qx_q4_matvec_kernel + qx_decode_kernel<Granite,float,float> + qx_split_merge_kernel"
+        timing = "64 tokens per CUDA graph replay"
+    else:
+        import ctypes as C
+        # the call's arguments, built once per position (the host cost per
+        # token is then one ctypes call)
+        ws = (_lib.LayerWeights * LAYERS)()
+        for l, w in enumerate(weights):
+            ws[l] = _lib.LayerWeights(w["norm"].data_ptr(), w["q"].ref(), w["k"].ref(), w["v"].ref(), w["o"].ref())
+        sargs = [_lib.StackArgs(0, 0, LAYERS, P + j, hidden[0].data_ptr(), hidden[1].data_ptr(), ws, 0, args.split)
+                 for j in range(cycle)]
+        sptr = [C.byref(a) for a in sargs]
+        lib = ctx.lib
+
+        def one(i):
+            j = i % cycle
+            if j == 0 and i > 0:
+                arena.rollback(0, P)
+            st = lib.qxc_attention_stack(ctx.handle, arena.handle, sptr[j])
+            if st != 0:
+                raise RuntimeError(lib.qxc_last_error(ctx.handle).decode())
+
+        arena.rollback(0, P)
+        K, W = args.steps, args.warmup
+        total, per, clk, launches = timed_steps(one, K, W, stream, world, dev, local, ctx)
+        steps = K
+        kernel = "qx_attention_stack_kernel"
+        timing = "one qxc_attention_stack call (one launch) per token"
     kv = sum(granite_stack_bytes(P + j + 1) for j in range(cycle)) / cycle
     wbytes = LAYERS * (1024 + 512 + 512 + 1024) * (1024 // 2 + 1024 // 32 * 2)
     B = kv + wbytes + LAYERS * 2 * 1024 * 4 * 2
@@ -760,9 +798,9 @@ def run_layer(args, world, rank, local):
                      {"workload": f"Granite 24-layer attention sub-layers with Q4 q/k/v/o (random codes), fp32 KV, "
                                   f"context {L}, positions {P}..{L - 1} cycled, batch 1",
                       "l2": "inputs larger than L2: ~400 MB of KV and 42 MB of Q4 weights per token",
-                      "timing": "64 tokens per CUDA graph replay", "bytes_per_token": int(B)},
-                     clk, K * per_replay)
-    line["roofline"] = hbm_roofline(B, per, "qx_q4_matvec_kernel + qx_decode_kernel<Granite,float,float>")
+                      "timing": timing, "bytes_per_token": int(B), "split": ctx.last_split},
+                     clk, launches)
+    line["roofline"] = hbm_roofline(B, per, kernel, None if args.layer_chain or L != 4096 else "layer")
     arena.close()
     ctx.close()
     return line
@@ -942,27 +980,24 @@ def run_verify(args, world, rank, local):
     return line
 
 
-def run_config4(args, world, rank, local):
-    """Config 4: 256 independent Granite sequences, lengths U{128..4096}, bf16 KV,
-    one decode step through 24 layers; sequences sharded over ranks by LPT on KV bytes."""
+def config4_measure(args, local, lengths, mine, K, W, timing_world):
+    """Decode one step of sequences `mine` (indices into `lengths`) through
+    24 layers per timed step, bf16 KV; returns a dict of the measurement.
+    `timing_world` ranks take part in the barriers and the max-reduce of the
+    time (1: this rank alone)."""
     import ctypes as C
     import torch
     from qx_b200 import BF16, F32, MODEL_GRANITE, Context, KvArena
     from qx_b200 import _lib
-    from qx_b200 import synthetic as syn
-    from qx_b200.distributed import lpt_shard, sequence_kv_bytes
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    lengths = [int(x) for x in syn.uniform_int(0x51580400, 256, 128, 4096)][:args.c4_sequences]
-    assignment, _ = lpt_shard([sequence_kv_bytes(L) for L in lengths], world)
-    mine = assignment[rank]
     n = len(mine)
     ctx = Context(local)
     stream = torch.cuda.Stream(device=dev)
     ctx.set_stream(stream)
     page = args.paged
     g = torch.Generator(device=dev)
-    g.manual_seed(0x51580401 + rank)
+    g.manual_seed(0x51580401 + mine[0])
     if page:
         # a paged arena sized to the batch: each sequence maps ceil(L / page)
         # pages of the shared pool instead of a 4096-row cache per layer
@@ -1001,26 +1036,78 @@ def run_config4(args, world, rank, local):
         if st != 0:
             raise RuntimeError(lib.qxc_last_error(ctx.handle).decode())
 
-    K, W = args.steps, args.warmup
-    total, per, clk, launches = timed_steps(step, K, W, stream, world, dev, local, ctx)
+    total, per, clk, launches = timed_steps(step, K, W, stream, timing_world, dev, local, ctx)
     my_bytes = sum(LAYERS * (2 * lengths[i] * 8 * 64 * 2 + 4 * 64 * (2 * 16 + 2 * 8)) for i in mine)
+    res = {"total_ms": total, "per": per, "clocks": clk, "launches": launches, "bytes": my_bytes,
+           "split": ctx.last_split, "kv_arena_bytes": kv_bytes}
+    arena.close()
+    ctx.close()
+    return res
+
+
+def config4_lengths(args):
+    from qx_b200 import synthetic as syn
+    return [int(x) for x in syn.uniform_int(0x51580400, 256, 128, 4096)][:args.c4_sequences]
+
+
+def run_config4(args, world, rank, local):
+    """Config 4: 256 independent Granite sequences, lengths U{128..4096}, bf16 KV,
+    one decode step through 24 layers; sequences sharded over ranks by LPT on KV bytes."""
+    from qx_b200.distributed import lpt_shard, sequence_kv_bytes
+    lengths = config4_lengths(args)
+    assignment, _ = lpt_shard([sequence_kv_bytes(L) for L in lengths], world)
+    K, W = args.steps, args.warmup
+    r = config4_measure(args, local, lengths, assignment[rank], K, W, world)
+    total = r["total_ms"]
     nseq = len(lengths)
     line = base_line("multi-sequence Granite decode tok/s (256 sequences x 24 layers)", nseq * K / (total / 1e3),
                      "tok/s", world, K, W, total, True, "strong", "f32 q/k/v, bf16 KV",
                      {"workload": f"config4: {nseq} Granite sequences, lengths U{{128..4096}} (seed 0x51580400), "
                                   "24 layers, bf16 KV, one decode step each",
-                      "l2": f"{my_bytes / 1e9:.1f} GB of KV per step",
+                      "l2": f"{r['bytes'] / 1e9:.1f} GB of KV per step",
                       "parallelism": f"sequences sharded x{world} by LPT on KV bytes, no collective"},
-                     clk, launches)
-    line["config"]["split"] = ctx.last_split
-    line["config"]["kv_arena_bytes_per_rank"] = int(kv_bytes)
-    if page:
-        line["config"]["workload"] += f"; paged arena, {page}-row pages, pool sized to the batch"
-    line["roofline"] = hbm_roofline(my_bytes, per, "qx_decode_tc_kernel<bf16,TcGranitePair>",
-                                    None if nseq != 256 or world != 1 else ("config4_paged" if page else "config4"))
-    arena.close()
-    ctx.close()
+                     r["clocks"], r["launches"])
+    line["config"]["split"] = r["split"]
+    line["config"]["kv_arena_bytes_per_rank"] = int(r["kv_arena_bytes"])
+    if args.paged:
+        line["config"]["workload"] += f"; paged arena, {args.paged}-row pages, pool sized to the batch"
+    line["roofline"] = hbm_roofline(r["bytes"], r["per"], "qx_decode_tc_kernel<bf16,TcGranitePair>",
+                                    None if nseq != 256 or world != 1 else ("config4_paged" if args.paged else "config4"))
     return line
+
+
+def sharded_config4(args, world, rank, local):
+    """The path that shards (config 4), measured beside the config-1 headline:
+    the 256 sequences split over the ranks by LPT on KV bytes, each rank
+    timing its own shard (device time, max over ranks). At N > 1 rank 0 also
+    times all 256 sequences alone on its GPU first (the other ranks wait), so
+    the line carries the one-GPU value of the same run and the efficiency
+    value / (N x one-GPU value)."""
+    from qx_b200.distributed import lpt_shard, sequence_kv_bytes
+    lengths = config4_lengths(args)
+    K, W = args.steps, args.warmup
+    one = None
+    if world > 1:
+        barrier(world)
+        if rank == 0:
+            r1 = config4_measure(args, local, lengths, list(range(len(lengths))), K, W, 1)
+            one = len(lengths) * K / (r1["total_ms"] / 1e3)
+        barrier(world)
+    assignment, loads = lpt_shard([sequence_kv_bytes(L) for L in lengths], world)
+    r = config4_measure(args, local, lengths, assignment[rank], K, W, world)
+    value = len(lengths) * K / (r["total_ms"] / 1e3)
+    if one is None:
+        one = value
+    peak, kind = hbm_peak()
+    per_rank_gbs = r["bytes"] / (r["total_ms"] / K / 1e3) / 1e9
+    return {"workload": f"config4: {len(lengths)} Granite sequences x 24 layers, bf16 KV, lengths U{{128..4096}} "
+                        "(seed 0x51580400), sharded by LPT on KV bytes, no collective",
+            "metric": "multi-sequence Granite decode tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": K, "ms_per_step": r["total_ms"] / K, "scaling": "strong",
+            "one_gpu_value": one, "efficiency": value / (world * one),
+            "rank0_sequences": len(assignment[0]), "max_rank_kv_bytes": max(loads),
+            "rank0_hbm_frac": per_rank_gbs / peak, "peak_kind": kind, "split": r["split"],
+            "gpu_launches": r["launches"]}
 
 
 # ---------------------------------------------------------------------------------------
@@ -1094,7 +1181,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config1",
-                    choices=["config0", "config1", "config2", "config3", "config4", "layer", "commit", "verify"])
+                    choices=["config0", "config1", "config2", "config3", "config4", "layer", "commit", "verify",
+                             "sweep"])
+    ap.add_argument("--layer-chain", action="store_true",
+                    help="layer workload: qxc_attention_layer per layer (graph-captured) instead of qxc_attention_stack")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="config1: leave out the `sharded` object (config 4 sharded over the ranks)")
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--paged", type=int, default=0, help="config4: paged KV arena with this many rows per page")
@@ -1130,10 +1222,22 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     try:
+        if args.workload == "sweep":
+            # the reference's --v2-attention-sweep (tools/qx-bench/src/main.rs:8984-9080): one line per
+            # context, each with its algorithmic bytes, achieved GB/s and roofline
+            for L in (512, 2048, 4096):
+                args.context = L
+                line = run_config1(args, world, rank, local)
+                line["config"]["sweep"] = [512, 2048, 4096]
+                if rank == 0:
+                    print(json.dumps(line), flush=True)
+            return 0
         run = {"config0": run_config0, "config1": run_config1, "config2": run_config2, "config3": run_config3,
                "config4": run_config4, "layer": run_layer, "commit": run_commit,
                "verify": run_verify}[args.workload]
         line = run(args, world, rank, local)
+        if args.workload == "config1" and not args.no_sharded:
+            line["sharded"] = sharded_config4(args, world, rank, local)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

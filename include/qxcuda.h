@@ -299,6 +299,44 @@ typedef struct {
 
 qxc_status qxc_attention_layer(qxc_ctx* ctx, qxc_kv* kv, const qxc_layer_args* args);
 
+/* The attention sub-layers of `layer_count` consecutive layers for one token
+ * (PreparedAttentionStack::encode, qx-runtime-v2 lib.rs:1793-1821, which
+ * runs encode_attention_layer :6916-6994 for every layer, the hidden state
+ * passed from each layer to the next): for each layer in order,
+ * hidden = fma(0.22, o_proj(attention(RoPE(q, k, v of
+ * RMSNorm(hidden)))), hidden), appending the new token at `position` to every
+ * layer's cache. hidden_out receives the last layer's output; the
+ * intermediate states stay in the context. Same arithmetic and position
+ * rules as qxc_attention_layer. An fp32 contiguous arena on a GPU of at
+ * least 128 SMs with 16-byte aligned Q4 rows runs every layer in one
+ * persistent cooperative launch (up to 32 layers per launch), its KV stream
+ * overlapping the dependent steps; other arenas run qxc_attention_layer per
+ * layer. `layers` is a host array of layer_count weight sets (device
+ * pointers). The cursor advances by one unless QXC_DECODE_NO_ADVANCE.
+ * split: cached rows per attention item (a multiple of 64, at most 256, at
+ * most 16 items per kv head), or 0 for the library's choice. */
+typedef struct {
+  const float* input_norm;  /* [1024] */
+  qxc_q4_matrix q_proj;     /* 1024 x 1024 */
+  qxc_q4_matrix k_proj;     /* 512 x 1024 */
+  qxc_q4_matrix v_proj;     /* 512 x 1024 */
+  qxc_q4_matrix o_proj;     /* 1024 x 1024 */
+} qxc_layer_weights;
+
+typedef struct {
+  int32_t seq;
+  int32_t layer_begin;
+  int32_t layer_count;
+  int32_t position;
+  const float* hidden_in;   /* [1024] */
+  float* hidden_out;        /* [1024] */
+  const qxc_layer_weights* layers;  /* host [layer_count] */
+  int32_t flags;
+  int32_t split;
+} qxc_stack_args;
+
+qxc_status qxc_attention_stack(qxc_ctx* ctx, qxc_kv* kv, const qxc_stack_args* args);
+
 /* ---- commitments of KV slots and residual checkpoints (BLAKE3) ----------- */
 /* Replaces the reference's verification-hash stage
  * (GpuDecodeGraph::encode_verification_hashes, qx-metal lib.rs:9247-9330,

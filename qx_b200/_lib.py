@@ -71,6 +71,19 @@ class LayerArgs(C.Structure):
                 ("split", C.c_int32)]
 
 
+class LayerWeights(C.Structure):
+    """qxc_layer_weights (one layer's RMSNorm weight and Q4 q/k/v/o)."""
+    _fields_ = [("input_norm", C.c_void_p), ("q_proj", Q4Matrix), ("k_proj", Q4Matrix), ("v_proj", Q4Matrix),
+                ("o_proj", Q4Matrix)]
+
+
+class StackArgs(C.Structure):
+    """qxc_stack_args (the attention sub-layers of consecutive layers, one token)."""
+    _fields_ = [("seq", C.c_int32), ("layer_begin", C.c_int32), ("layer_count", C.c_int32),
+                ("position", C.c_int32), ("hidden_in", C.c_void_p), ("hidden_out", C.c_void_p),
+                ("layers", C.POINTER(LayerWeights)), ("flags", C.c_int32), ("split", C.c_int32)]
+
+
 class KvPaging(C.Structure):
     """qxc_kv_paging (paged arena: rows per page, physical pages per layer)."""
     _fields_ = [("page_size", C.c_int32), ("pool_pages", C.c_int32)]
@@ -144,6 +157,7 @@ def load() -> C.CDLL:
         "qxc_decode_verify": (C.c_int, [vp, vp, C.POINTER(VerifyArgs)]),
         "qxc_q4_mat_vec": (C.c_int, [vp, C.POINTER(Q4Matrix), vp, vp, vp]),
         "qxc_attention_layer": (C.c_int, [vp, vp, C.POINTER(LayerArgs)]),
+        "qxc_attention_stack": (C.c_int, [vp, vp, C.POINTER(StackArgs)]),
         "qxc_lse_merge": (C.c_int, [vp, i32, i32, vp, vp, i32]),
         "qxc_peer_group_create": (C.c_int, [vp, i32, i32, pp]),
         "qxc_peer_group_destroy": (None, [vp]),

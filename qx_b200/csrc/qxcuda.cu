@@ -30,6 +30,7 @@
 #include "commit.cuh"
 #include "pages.cuh"
 #include "exchange.cuh"
+#include "stack.cuh"
 
 using namespace qx;
 
@@ -74,6 +75,13 @@ struct qxc_ctx {
   float2* qwen_rope = nullptr;
   float2* granite_rope = nullptr;  // pinned (sin, cos) [4096][32], built on first prefill
   float* layer_scratch = nullptr;   // attention layer: q[1024] k[512] v[512] attention[1024]
+  // attention stack (stack.cuh): tagged exchange buffers hx [2][1024],
+  // qx [2048], px [128][132], ax [1024]; chain [2][1024] floats (between
+  // launches of > 32 layers); the abort word; the launch generation
+  uint2* stack_x = nullptr;
+  float* stack_chain = nullptr;
+  unsigned* stack_abort = nullptr;
+  unsigned stack_gen = 0;
   // prefill's rotated-query scratch (bf16 elements)
   unsigned short* prefill_q = nullptr;
   size_t prefill_q_cap = 0;
@@ -1005,6 +1013,9 @@ void qxc_destroy(qxc_ctx* ctx) {
   cudaFree(ctx->qwen_rope);
   cudaFree(ctx->granite_rope);
   cudaFree(ctx->layer_scratch);
+  cudaFree(ctx->stack_x);
+  cudaFree(ctx->stack_chain);
+  cudaFree(ctx->stack_abort);
   cudaFree(ctx->prefill_q);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -1028,6 +1039,11 @@ qxc_status qxc_sync(qxc_ctx* ctx) {
     // a kernel that stopped early may have left split tickets raised
     if (ctx->tickets) {
       cudaMemsetAsync(ctx->tickets, 0, ctx->tickets_cap * sizeof(int), ctx->stream);
+      cudaStreamSynchronize(ctx->stream);
+    }
+    // and a stack launch that gave up has raised its abort word
+    if (ctx->stack_abort) {
+      cudaMemsetAsync(ctx->stack_abort, 0, sizeof(unsigned), ctx->stream);
       cudaStreamSynchronize(ctx->stream);
     }
     if (e & QX_ERR_BIT_PEER)
@@ -1501,6 +1517,191 @@ qxc_status qxc_attention_layer(qxc_ctx* ctx, qxc_kv* kv, const qxc_layer_args* a
   o.residual = a->hidden_in;
   o.err = ctx->err_dev;
   return launch_matvec(ctx, o);
+}
+
+// ---- the attention sub-layers of a layer stack in one launch (stack.cuh) ------
+namespace {
+
+constexpr int kStackHx = 0, kStackQx = 2048, kStackPx = 4096;
+constexpr int kStackAx = kStackPx + 8 * kStackMaxSplits * kStackPartial;
+constexpr int kStackTagged = kStackAx + 1024;  // uint2 values
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Cached rows per attention item of a fused launch: the fewest rows (a
+// multiple of 64) that cover the attended rows with at most min(16, CTAs/8)
+// splits per kv head; 0 when that exceeds the 256 rows a CTA stages.
+int stack_chunk(int attend, int ctas, int split) {
+  const int max_splits = std::min(kStackMaxSplits, ctas / 8);
+  if (max_splits < 1) return 0;
+  int chunk = split;
+  if (chunk == 0) chunk = ((attend + max_splits - 1) / max_splits + 63) / 64 * 64;
+  if (chunk < 64 || chunk % 64 || chunk > kStackMaxTiles * kStackTileRows) return 0;
+  if ((attend + chunk - 1) / chunk > max_splits) return 0;
+  return chunk;
+}
+
+// The fused kernel applies to fp32 contiguous Granite arenas on a GPU whose
+// every SM takes one CTA (at least 128, so a CTA's q/k/v and o rows fit its
+// buffers) with 16-byte aligned Q4 rows.
+bool stack_fusable(qxc_ctx* ctx, const qxc_kv* kv, const qxc_stack_args* a, int chunk) {
+  if (kv->desc.key_dtype != QXC_F32 || kv->desc.value_dtype != QXC_F32 || kv->paged() || chunk == 0) return false;
+  if (ctx->sm_count < 128 || (2048 + ctx->sm_count - 1) / ctx->sm_count > kStackMaxQkvRows) return false;
+  int coop = 0;
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ctx->device);
+  if (!coop) return false;
+  for (int l = 0; l < a->layer_count; ++l) {
+    const qxc_layer_weights& w = a->layers[l];
+    for (const qxc_q4_matrix* m : {&w.q_proj, &w.k_proj, &w.v_proj, &w.o_proj})
+      if (!aligned16(m->codes) || !aligned16(m->scales)) return false;
+  }
+  return true;
+}
+
+qxc_status launch_stack(qxc_ctx* ctx, const StackParams& p) {
+  static unsigned long long configured = 0;
+  const unsigned long long bit = 1ull << (ctx->device & 63);
+  if (!(configured & bit)) {
+    QXC_CUDA(ctx, cudaFuncSetAttribute(qx_attention_stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       StackCfg::SMEM));
+    int per_sm = 0;
+    QXC_CUDA(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qx_attention_stack_kernel, kStackThreads,
+                                                                StackCfg::SMEM));
+    if (per_sm < 1) return fail(ctx, QXC_ERR_UNSUPPORTED, "the attention stack kernel does not fit an SM");
+    configured |= bit;
+  }
+  TraceRun tr(ctx, "stack", (size_t)ctx->sm_count);
+  StackParams q = p;
+  q.trace = tr.buf;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctx->sm_count);
+  cfg.blockDim = dim3(kStackThreads);
+  cfg.dynamicSmemBytes = StackCfg::SMEM;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: they wait on one another
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QXC_CUDA(ctx, cudaLaunchKernelEx(&cfg, qx_attention_stack_kernel, q));
+  ctx->launches++;
+  return QXC_OK;
+}
+
+}  // namespace
+
+qxc_status qxc_attention_stack(qxc_ctx* ctx, qxc_kv* kv, const qxc_stack_args* a) {
+  if (!ctx || !kv || !a) return fail(ctx, QXC_ERR_INVALID_ARG, "null argument");
+  if (kv->ctx != ctx) return fail(ctx, QXC_ERR_INVALID_ARG, "KV arena belongs to another context");
+  if (kv->desc.model != QXC_MODEL_GRANITE) return fail(ctx, QXC_ERR_UNSUPPORTED, "the Q4 layer is Granite's");
+  if (!a->hidden_in || !a->hidden_out || !a->layers) return fail(ctx, QXC_ERR_INVALID_ARG, "null tensor pointer");
+  qxc_status st = check_seq(ctx, kv, a->seq);
+  if (st != QXC_OK) return st;
+  if (a->layer_count < 1 || a->layer_begin < 0 || a->layer_begin + a->layer_count > kv->desc.layers)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "layers [%d, %d) outside the arena's %d layers", a->layer_begin,
+                a->layer_begin + a->layer_count, kv->desc.layers);
+  for (int l = 0; l < a->layer_count && st == QXC_OK; ++l) {
+    const qxc_layer_weights& w = a->layers[l];
+    if (!w.input_norm) return fail(ctx, QXC_ERR_INVALID_ARG, "layer %d: null input_norm", l);
+    st = check_q4(ctx, &w.q_proj, kHidden, kHidden, "q_proj");
+    if (st == QXC_OK) st = check_q4(ctx, &w.k_proj, 512, kHidden, "k_proj");
+    if (st == QXC_OK) st = check_q4(ctx, &w.v_proj, 512, kHidden, "v_proj");
+    if (st == QXC_OK) st = check_q4(ctx, &w.o_proj, kHidden, kHidden, "o_proj");
+  }
+  if (st != QXC_OK) return st;
+  // KvCache::append (qx-runtime lib.rs:385-398), checked before any launch
+  if (a->position != kv->len[a->seq])
+    return fail(ctx, QXC_ERR_POSITION, "KV position %d does not follow cache length %d", a->position,
+                kv->len[a->seq]);
+  if (a->position >= kv->desc.capacity)
+    return fail(ctx, QXC_ERR_POSITION, "KV position %d exceeds context %d", a->position, kv->desc.capacity);
+  if (a->split < 0 || a->split % 64 != 0)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "split %d must be 0 or a positive multiple of 64", a->split);
+  QXC_CUDA(ctx, cudaSetDevice(ctx->device));
+  if (!ctx->stack_x) {
+    // zeroed: tag 0 is never a launch's tag (those start at 65)
+    QXC_CUDA(ctx, cudaMalloc(&ctx->stack_x, kStackTagged * sizeof(uint2)));
+    QXC_CUDA(ctx, cudaMemsetAsync(ctx->stack_x, 0, kStackTagged * sizeof(uint2), ctx->stream));
+    QXC_CUDA(ctx, cudaMalloc(&ctx->stack_chain, 2048 * sizeof(float)));
+    QXC_CUDA(ctx, cudaMalloc(&ctx->stack_abort, sizeof(unsigned)));
+    QXC_CUDA(ctx, cudaMemsetAsync(ctx->stack_abort, 0, sizeof(unsigned), ctx->stream));
+  }
+  const int attend = a->position + 1;
+  const int chunk = stack_chunk(attend, ctx->sm_count, a->split);
+  if (a->split && !chunk)
+    return fail(ctx, QXC_ERR_INVALID_ARG, "split %d: at most %d splits of at most %d rows per kv head", a->split,
+                std::min(kStackMaxSplits, ctx->sm_count / 8), kStackMaxTiles * kStackTileRows);
+  if (!stack_fusable(ctx, kv, a, chunk)) {
+    // one qxc_attention_layer per layer, the hidden state through the chain buffers
+    float* chain = ctx->stack_chain;
+    for (int l = 0; l < a->layer_count; ++l) {
+      const qxc_layer_weights& w = a->layers[l];
+      qxc_layer_args la;
+      memset(&la, 0, sizeof(la));
+      la.seq = a->seq;
+      la.layer = a->layer_begin + l;
+      la.position = a->position;
+      la.hidden_in = l == 0 ? a->hidden_in : chain + ((l - 1) & 1) * 1024;
+      la.hidden_out = l == a->layer_count - 1 ? a->hidden_out : chain + (l & 1) * 1024;
+      la.input_norm = w.input_norm;
+      la.q_proj = w.q_proj;
+      la.k_proj = w.k_proj;
+      la.v_proj = w.v_proj;
+      la.o_proj = w.o_proj;
+      la.flags = (a->flags & ~QXC_DECODE_NO_ADVANCE) | QXC_DECODE_NO_ADVANCE;
+      st = qxc_attention_layer(ctx, kv, &la);
+      if (st != QXC_OK) return st;
+    }
+  } else {
+    StackParams p;
+    memset(&p, 0, sizeof(p));
+    p.tmk = kv->tmk;
+    p.tmv = kv->tmv;
+    p.k_region = kv->k_region;
+    p.v_region = kv->v_region;
+    p.capacity = kv->desc.capacity;
+    p.arena_layers = kv->desc.layers;
+    p.seq = a->seq;
+    p.position = a->position;
+    p.chunk = chunk;
+    p.nsplit = (attend + chunk - 1) / chunk;
+    p.hx = ctx->stack_x + kStackHx;
+    p.qx = ctx->stack_x + kStackQx;
+    p.px = ctx->stack_x + kStackPx;
+    p.ax = ctx->stack_x + kStackAx;
+    p.abort = ctx->stack_abort;
+    p.pinned_exp = (a->flags & QXC_DECODE_NATIVE_EXP) ? 0 : 1;
+    p.err = ctx->err_dev;
+    float* chain = ctx->stack_chain;
+    // at most kStackMaxLayers layers per launch; longer stacks chain launches
+    for (int l0 = 0, part = 0; l0 < a->layer_count; l0 += kStackMaxLayers, ++part) {
+      const int n = std::min(kStackMaxLayers, a->layer_count - l0);
+      p.layer_begin = a->layer_begin + l0;
+      p.n_layers = n;
+      p.hidden_in = l0 == 0 ? a->hidden_in : chain + ((part - 1) & 1) * 1024;
+      p.hidden_out = l0 + n == a->layer_count ? a->hidden_out : chain + (part & 1) * 1024;
+      for (int l = 0; l < n; ++l) {
+        const qxc_layer_weights& w = a->layers[l0 + l];
+        p.w[l].norm = w.input_norm;
+        const qxc_q4_matrix* m[4] = {&w.q_proj, &w.k_proj, &w.v_proj, &w.o_proj};
+        for (int j = 0; j < 4; ++j) {
+          p.w[l].codes[j] = m[j]->codes;
+          p.w[l].scales[j] = m[j]->scales;
+        }
+      }
+      // the launch's tags: gen * 64 + layer + 1, never 0 (gen wraps at 2^26)
+      ctx->stack_gen = (ctx->stack_gen + 1u) & 0x3ffffffu;
+      if (ctx->stack_gen == 0u) ctx->stack_gen = 1u;
+      p.gen = ctx->stack_gen;
+      st = launch_stack(ctx, p);
+      if (st != QXC_OK) return st;
+    }
+    // the kernel writes row `position` of every layer and waits for nothing
+    // after its end: later grids see complete rows
+    note_rows_written(ctx, nullptr, -1, 0);
+  }
+  if (!(a->flags & QXC_DECODE_NO_ADVANCE)) kv->len[a->seq] += 1;
+  return QXC_OK;
 }
 
 // ---- speculative verify ----------------------------------------------------

@@ -375,6 +375,19 @@ class KvArena:
                            q_proj.ref(), k_proj.ref(), v_proj.ref(), o_proj.ref(), _ptr(attention_out), flags, split)
         self.ctx.check(self.lib.qxc_attention_layer(self.ctx.handle, self.handle, C.byref(a)))
 
+    def attention_stack(self, hidden_in, hidden_out, layers, position: int, seq: int = 0, layer_begin: int = 0,
+                        flags: int = 0, split: int = 0) -> None:
+        """The attention sub-layers of len(layers) consecutive layers for one
+        token (qxc_attention_stack, PreparedAttentionStack::encode): each
+        entry of `layers` is a dict with "norm" (device [1024]) and "q", "k",
+        "v", "o" (Q4Weights); hidden_out receives the last layer's output."""
+        ws = (_lib.LayerWeights * len(layers))()
+        for i, w in enumerate(layers):
+            ws[i] = _lib.LayerWeights(_ptr(w["norm"]), w["q"].ref(), w["k"].ref(), w["v"].ref(), w["o"].ref())
+        a = _lib.StackArgs(seq, layer_begin, len(layers), position, _ptr(hidden_in), _ptr(hidden_out), ws, flags,
+                           split)
+        self.ctx.check(self.lib.qxc_attention_stack(self.ctx.handle, self.handle, C.byref(a)))
+
     def verification_hashes(self, token: int, residuals, residual_stride: int, checkpoint_interval: int, digests,
                             seq: int = 0) -> None:
         """Per-token commitments (qxc_verification_hashes): digests[p] = state
