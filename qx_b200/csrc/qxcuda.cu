@@ -76,12 +76,14 @@ struct qxc_ctx {
   float2* granite_rope = nullptr;  // pinned (sin, cos) [4096][32], built on first prefill
   float* layer_scratch = nullptr;   // attention layer: q[1024] k[512] v[512] attention[1024]
   // attention stack (stack.cuh): tagged exchange buffers hx [2][1024],
-  // qx [2048], px [128][132], ax [1024]; chain [2][1024] floats (between
-  // launches of > 32 layers); the abort word; the launch generation
+  // qx [2048], ax [1024]; split partials [128][132] floats and chain
+  // [2][1024] floats (between launches of > 32 layers); the words: [0] abort,
+  // [1..8] merge tickets; the launch generation
   uint2* stack_x = nullptr;
-  float* stack_chain = nullptr;
-  unsigned* stack_abort = nullptr;
+  float* stack_f = nullptr;
+  unsigned* stack_words = nullptr;
   unsigned stack_gen = 0;
+  unsigned stack_tickets = 0;  // every head's merge-ticket count after the launches so far
   // prefill's rotated-query scratch (bf16 elements)
   unsigned short* prefill_q = nullptr;
   size_t prefill_q_cap = 0;
@@ -1014,8 +1016,8 @@ void qxc_destroy(qxc_ctx* ctx) {
   cudaFree(ctx->granite_rope);
   cudaFree(ctx->layer_scratch);
   cudaFree(ctx->stack_x);
-  cudaFree(ctx->stack_chain);
-  cudaFree(ctx->stack_abort);
+  cudaFree(ctx->stack_f);
+  cudaFree(ctx->stack_words);
   cudaFree(ctx->prefill_q);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -1041,10 +1043,12 @@ qxc_status qxc_sync(qxc_ctx* ctx) {
       cudaMemsetAsync(ctx->tickets, 0, ctx->tickets_cap * sizeof(int), ctx->stream);
       cudaStreamSynchronize(ctx->stream);
     }
-    // and a stack launch that gave up has raised its abort word
-    if (ctx->stack_abort) {
-      cudaMemsetAsync(ctx->stack_abort, 0, sizeof(unsigned), ctx->stream);
+    // and a stack launch that gave up has raised its abort word and may
+    // have left merge tickets raised
+    if (ctx->stack_words) {
+      cudaMemsetAsync(ctx->stack_words, 0, 16 * sizeof(unsigned), ctx->stream);
       cudaStreamSynchronize(ctx->stream);
+      ctx->stack_tickets = 0;
     }
     if (e & QX_ERR_BIT_PEER)
       return fail(ctx, QXC_ERR_TIMEOUT,
@@ -1522,9 +1526,10 @@ qxc_status qxc_attention_layer(qxc_ctx* ctx, qxc_kv* kv, const qxc_layer_args* a
 // ---- the attention sub-layers of a layer stack in one launch (stack.cuh) ------
 namespace {
 
-constexpr int kStackHx = 0, kStackQx = 2048, kStackPx = 4096;
-constexpr int kStackAx = kStackPx + 8 * kStackMaxSplits * kStackPartial;
-constexpr int kStackTagged = kStackAx + 1024;  // uint2 values
+constexpr int kStackHx = 0, kStackQx = 2048, kStackAx = 4096, kStackPx = 5120;
+constexpr int kStackTagged = kStackPx + 8 * kStackMaxSplits * kStackPartial;  // uint2 values
+constexpr int kStackChain = 0;  // floats: the chain between launches
+constexpr int kStackFloats = 2048;
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -1622,9 +1627,9 @@ qxc_status qxc_attention_stack(qxc_ctx* ctx, qxc_kv* kv, const qxc_stack_args* a
     // zeroed: tag 0 is never a launch's tag (those start at 65)
     QXC_CUDA(ctx, cudaMalloc(&ctx->stack_x, kStackTagged * sizeof(uint2)));
     QXC_CUDA(ctx, cudaMemsetAsync(ctx->stack_x, 0, kStackTagged * sizeof(uint2), ctx->stream));
-    QXC_CUDA(ctx, cudaMalloc(&ctx->stack_chain, 2048 * sizeof(float)));
-    QXC_CUDA(ctx, cudaMalloc(&ctx->stack_abort, sizeof(unsigned)));
-    QXC_CUDA(ctx, cudaMemsetAsync(ctx->stack_abort, 0, sizeof(unsigned), ctx->stream));
+    QXC_CUDA(ctx, cudaMalloc(&ctx->stack_f, kStackFloats * sizeof(float)));
+    QXC_CUDA(ctx, cudaMalloc(&ctx->stack_words, 16 * sizeof(unsigned)));
+    QXC_CUDA(ctx, cudaMemsetAsync(ctx->stack_words, 0, 16 * sizeof(unsigned), ctx->stream));
   }
   const int attend = a->position + 1;
   const int chunk = stack_chunk(attend, ctx->sm_count, a->split);
@@ -1633,7 +1638,7 @@ qxc_status qxc_attention_stack(qxc_ctx* ctx, qxc_kv* kv, const qxc_stack_args* a
                 std::min(kStackMaxSplits, ctx->sm_count / 8), kStackMaxTiles * kStackTileRows);
   if (!stack_fusable(ctx, kv, a, chunk)) {
     // one qxc_attention_layer per layer, the hidden state through the chain buffers
-    float* chain = ctx->stack_chain;
+    float* chain = ctx->stack_f + kStackChain;
     for (int l = 0; l < a->layer_count; ++l) {
       const qxc_layer_weights& w = a->layers[l];
       qxc_layer_args la;
@@ -1667,12 +1672,13 @@ qxc_status qxc_attention_stack(qxc_ctx* ctx, qxc_kv* kv, const qxc_stack_args* a
     p.nsplit = (attend + chunk - 1) / chunk;
     p.hx = ctx->stack_x + kStackHx;
     p.qx = ctx->stack_x + kStackQx;
-    p.px = ctx->stack_x + kStackPx;
     p.ax = ctx->stack_x + kStackAx;
-    p.abort = ctx->stack_abort;
+    p.px = ctx->stack_x + kStackPx;
+    p.abort = ctx->stack_words;
+    p.tickets = ctx->stack_words + 1;
     p.pinned_exp = (a->flags & QXC_DECODE_NATIVE_EXP) ? 0 : 1;
     p.err = ctx->err_dev;
-    float* chain = ctx->stack_chain;
+    float* chain = ctx->stack_f + kStackChain;
     // at most kStackMaxLayers layers per launch; longer stacks chain launches
     for (int l0 = 0, part = 0; l0 < a->layer_count; l0 += kStackMaxLayers, ++part) {
       const int n = std::min(kStackMaxLayers, a->layer_count - l0);
@@ -1693,8 +1699,10 @@ qxc_status qxc_attention_stack(qxc_ctx* ctx, qxc_kv* kv, const qxc_stack_args* a
       ctx->stack_gen = (ctx->stack_gen + 1u) & 0x3ffffffu;
       if (ctx->stack_gen == 0u) ctx->stack_gen = 1u;
       p.gen = ctx->stack_gen;
+      p.ticket_base = ctx->stack_tickets;
       st = launch_stack(ctx, p);
       if (st != QXC_OK) return st;
+      ctx->stack_tickets += (unsigned)n * (unsigned)p.nsplit;  // (mod 2^32, as the kernel counts)
     }
     // the kernel writes row `position` of every layer and waits for nothing
     // after its end: later grids see complete rows

@@ -18,27 +18,36 @@
 //
 //   A  CTAs with q/k/v rows: RMSNorm of hidden(i) (each computes it, in the
 //      reference's order), then their contiguous slice of the 2048 q/k/v
-//      rows from Q4 weights staged in shared memory.
-//   B  CTAs with an attention item (kv head h, split s of the cache): RoPE
-//      of q (and, on the split holding the new slot, of k); the split's
-//      cache rows are already in shared memory (TMA, issued as soon as the
-//      previous layer's attention freed the buffers); append the new row;
-//      (m, l, O) of both query heads. The item of split 0 then merges its
-//      head's splits into 128 values of the attention vector.
+//      rows from Q4 weights staged in shared memory (bulk copies issued two
+//      layers ahead into a double buffer).
+//   B  CTAs with an attention item (kv head h, split s of the cache, at
+//      most 256 rows): every lane takes its row's key into registers while
+//      q is on its way; RoPE of q (and, on the split holding the new slot,
+//      of k); append the new row; (m, l, O) of both query heads. A ticket per
+//      kv head, counted up for good, elects the last of the head's items to
+//      finish, which merges the head's splits into 128 values of the
+//      attention vector.
 //   C  CTAs with o-projection rows: the attention vector, their rows of the
 //      o-projection and the residual: their part of hidden(i + 1).
+//
+// The next layer's cache rows (16.8 MB of fp32 KV at 4096 positions) are
+// prefetched from HBM into L2 as soon as a layer's attention is done and
+// copied on into shared memory (TMA) at the layer's end, so the HBM stream
+// runs under the dependent steps. Only L2-to-SM bytes, not HBM-to-SM ones,
+// then queue ahead of the hand-off loads on the same SM.
 //
 // Hand-offs carry no fence and no counter: every 32-bit value travels with a
 // 32-bit tag (this launch's generation and the layer) in one 8-byte store,
 // which a reader sees whole or not at all, and the reader polls the value
 // itself until its tag is the expected one: the poll is the load of the
-// data. A buffer is only rewritten (the next layer's tag) once every reader
-// of its current contents has passed a point the writer depends on, so a
-// reader never sees a later tag than the one it waits for. Every poll is
-// bounded: after kMaxWaitNs, or once another CTA has raised the shared abort
-// word, the CTA records QX_ERR_BIT_TIMEOUT, raises the word, waits (bounded)
-// for its own copies in flight and leaves; the host clears the word when it
-// reports the error.
+// data. (A fence here would wait behind the CTA's own bulk copies in
+// flight: microseconds.) A buffer is only rewritten (the next layer's tag)
+// once every reader of its current contents has passed a point the writer
+// depends on, so a reader never sees a later tag than the one it waits for.
+// Every poll is bounded: after kMaxWaitNs, or once another CTA has raised
+// the shared abort word, the CTA records QX_ERR_BIT_TIMEOUT, raises the
+// word, waits (bounded) for its own copies in flight and leaves; the host
+// clears the word (and the tickets) when it reports the error.
 //
 // Arithmetic: RMSNorm, q/k/v and the o-projection are bit-identical to the
 // reference's CPU routines (layer.cuh's order); RoPE is qx's pinned sin/cos
@@ -79,7 +88,9 @@ struct StackParams {
   // tagged exchange buffers ({value bits, tag})
   uint2* hx;              // [2][1024] hidden between layers
   uint2* qx;              // [2048] q, k, v
-  uint2* px;              // [8 * nsplit][kStackPartial] split partials
+  uint2* px;              // [8 * nsplit][kStackPartial] tagged split partials
+  unsigned* tickets;      // [8] per kv head: items done, counted up for good (never reset)
+  unsigned ticket_base;   // every head's ticket count when this launch starts
   uint2* ax;              // [1024] the merged attention vector
   unsigned* abort;        // raised by a CTA whose wait gave up
   int pinned_exp;
@@ -108,6 +119,7 @@ struct StackCfg {
   static constexpr int OFF_BAR = OFF_ROPE + 288;        // 3 mbarriers: KV, weights 0, weights 1
   static constexpr int SMEM = OFF_BAR + 32 + 1024;      // + slack to align the base to 1024
 };
+static_assert(StackCfg::SMEM <= 227 * 1024, "the stack kernel's shared memory must fit one SM");
 
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size a
 // multiple of 16), completing on `bar`'s transaction count.
@@ -115,6 +127,14 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_addr(dst)),
                "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
+// Prefetch of a TMA tile into L2 only (nothing lands in this CTA's shared
+// memory; plain, no multicast).
+__device__ __forceinline__ void tma_prefetch_3d(const void* tmap, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(tmap), "r"(x), "r"(y),
+               "r"(z)
                : "memory");
 }
 
@@ -276,7 +296,6 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
   const int begin = s * p.chunk, end = min(begin + p.chunk, attend);
   const int ntiles = has_item ? (end - begin + kStackTileRows - 1) / kStackTileRows : 0;
   const bool owner = has_item && p.position >= begin && p.position < end;
-  const bool merger = has_item && s == 0;
   if (!has_q && !has_o && !has_item) return;  // no part in any hand-off
 
   if (tid == 0) {
@@ -320,6 +339,18 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
       }
     }
     ++kv_issued;
+  };
+  auto prefetch_kv = [&](int i) {  // this item's rows of layer i into L2
+    if (!has_item) return;
+    const int layer = p.layer_begin + i;
+    for (int t = 0; t < ntiles; ++t) {
+      const int z = (int)(((long long)p.seq * p.arena_layers + layer) * p.capacity + begin + t * kStackTileRows);
+#pragma unroll
+      for (int bx = 0; bx < 2; ++bx) {
+        tma_prefetch_3d(&p.tmk, bx * 32, h, z);
+        tma_prefetch_3d(&p.tmv, bx * 32, h, z);
+      }
+    }
   };
   auto issue_w = [&](int i) {  // thread 0: this CTA's norm, q/k/v and o rows of layer i into buffer i & 1
     if (!has_q && !has_o) return;
@@ -445,6 +476,31 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
 
     // ---- B: the attention item --------------------------------------------------
     if (has_item) {
+      // the split's rows have been in shared memory since the previous layer
+      if (tid == 0) {
+        if (mbar_wait_bounded(bar_kv, (uint32_t)(kv_waited & 1), p.err)) ++kv_waited;
+        else stack_raise(p, poll);
+      }
+      if (__syncthreads_or(poll.failed)) {
+        ok = false;
+        break;
+      }
+      // each lane takes its row's key into registers while q is on its way
+      const int rr = warp * 32 + lane;
+      const bool valid = begin + rr < end;
+      const bool warp_rows = warp * 32 < end - begin;
+      float kreg[64];
+      if (warp_rows) {
+        const unsigned char* krow = ks + (rr >> 6) * C::TILE;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float4 kv4 = *reinterpret_cast<const float4*>(krow + stack_swz(rr & 63, c * 4));
+          kreg[4 * c] = kv4.x;
+          kreg[4 * c + 1] = kv4.y;
+          kreg[4 * c + 2] = kv4.z;
+          kreg[4 * c + 3] = kv4.w;
+        }
+      }
       bool bad = false;
       if (tid < 64) {
         // q heads 2h, 2h + 1: the pinned RoPE pair (rotate_heads' arithmetic)
@@ -471,10 +527,6 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
         newv[tid - 128] = stack_take(p, p.qx + 1536 + h * 64 + (tid - 128), tag, poll);
       }
       if (bad) flag_error(p.err, QX_ERR_BIT_NONFINITE);
-      if (tid == 0) {
-        if (mbar_wait_bounded(bar_kv, (uint32_t)(kv_waited & 1), p.err)) ++kv_waited;
-        else stack_raise(p, poll);
-      }
       if (__syncthreads_or(poll.failed)) {
         ok = false;
         break;
@@ -488,38 +540,39 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
         const int d = tid * 2;
         *reinterpret_cast<float2*>(kd + d) = make_float2(newk[d], newk[d + 1]);
         *reinterpret_cast<float2*>(vd + d) = make_float2(newv[d], newv[d + 1]);
-        const int rr = p.position - begin, t = rr >> 6, r = rr & 63;
+        const int nr = p.position - begin, t = nr >> 6, r = nr & 63;
         *reinterpret_cast<float2*>(ks + t * C::TILE + stack_swz(r, d)) = make_float2(newk[d], newk[d + 1]);
         *reinterpret_cast<float2*>(vs + t * C::TILE + stack_swz(r, d)) = make_float2(newv[d], newv[d + 1]);
       }
+      if (owner && begin + rr == p.position) {
+        // the lane of the new slot: its key is the rotated new one
+#pragma unroll
+        for (int c = 0; c < 64; ++c) kreg[c] = newk[c];
+      }
       __syncthreads();
       trace.mark();
-      // warp w scores rows [32w, 32w + 32) of the item, one row per lane
+      // warp w scores rows [32w, 32w + 32) of the item, one row per lane,
+      // the key from registers and q broadcast from shared memory
       {
-        const int rr = warp * 32 + lane;
-        const bool valid = begin + rr < end;
-        const int t = rr >> 6, r = rr & 63;
-        const unsigned char* krow = ks + t * C::TILE;
         float s0 = -INFINITY, s1 = -INFINITY;
-        if (warp * 32 < end - begin) {
-          float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+        if (warp_rows) {
+          float2 a0 = make_float2(0.f, 0.f), a0b = make_float2(0.f, 0.f);
+          float2 a1 = make_float2(0.f, 0.f), a1b = make_float2(0.f, 0.f);
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const float4 kv4 = *reinterpret_cast<const float4*>(krow + stack_swz(r, c * 4));
             const float4 q0 = *reinterpret_cast<const float4*>(qs + c * 4);
             const float4 q1 = *reinterpret_cast<const float4*>(qs + 64 + c * 4);
-            a0[0] = fmaf(q0.x, kv4.x, a0[0]);
-            a0[1] = fmaf(q0.y, kv4.y, a0[1]);
-            a0[2] = fmaf(q0.z, kv4.z, a0[2]);
-            a0[3] = fmaf(q0.w, kv4.w, a0[3]);
-            a1[0] = fmaf(q1.x, kv4.x, a1[0]);
-            a1[1] = fmaf(q1.y, kv4.y, a1[1]);
-            a1[2] = fmaf(q1.z, kv4.z, a1[2]);
-            a1[3] = fmaf(q1.w, kv4.w, a1[3]);
+            const float2 k01 = make_float2(kreg[4 * c], kreg[4 * c + 1]);
+            const float2 k23 = make_float2(kreg[4 * c + 2], kreg[4 * c + 3]);
+            a0 = __ffma2_rn(make_float2(q0.x, q0.y), k01, a0);
+            a0b = __ffma2_rn(make_float2(q0.z, q0.w), k23, a0b);
+            a1 = __ffma2_rn(make_float2(q1.x, q1.y), k01, a1);
+            a1b = __ffma2_rn(make_float2(q1.z, q1.w), k23, a1b);
           }
+          float a0v[4] = {a0.x, a0.y, a0b.x, a0b.y}, a1v[4] = {a1.x, a1.y, a1b.x, a1b.y};
           if (valid) {
-            s0 = ((a0[0] + a0[1]) + (a0[2] + a0[3])) * Granite::SCALE;
-            s1 = ((a1[0] + a1[1]) + (a1[2] + a1[3])) * Granite::SCALE;
+            s0 = ((a0v[0] + a0v[1]) + (a0v[2] + a0v[3])) * Granite::SCALE;
+            s1 = ((a1v[0] + a1v[1]) + (a1v[2] + a1v[3])) * Granite::SCALE;
           }
         }
         const float m0 = warp_max(s0), m1 = warp_max(s1);
@@ -536,10 +589,12 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
           const float pj1 = __shfl_sync(0xffffffffu, p1, j);
           const int rj = warp * 32 + j;
           const float2 v2 = *reinterpret_cast<const float2*>(vs + (rj >> 6) * C::TILE + stack_swz(rj & 63, d));
-          o00 = fmaf(pj0, v2.x, o00);
-          o01 = fmaf(pj0, v2.y, o01);
-          o10 = fmaf(pj1, v2.x, o10);
-          o11 = fmaf(pj1, v2.y, o11);
+          const float2 a = __ffma2_rn(make_float2(pj0, pj0), v2, make_float2(o00, o01));
+          const float2 c = __ffma2_rn(make_float2(pj1, pj1), v2, make_float2(o10, o11));
+          o00 = a.x;
+          o01 = a.y;
+          o10 = c.x;
+          o11 = c.y;
         }
         *reinterpret_cast<float2*>(wo + (warp * 2 + 0) * 64 + d) = make_float2(o00, o01);
         *reinterpret_cast<float2*>(wo + (warp * 2 + 1) * 64 + d) = make_float2(o10, o11);
@@ -581,26 +636,36 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
           st_tagged(part + 65, wml[50 + g], tag);
         }
       }
-      // the tiles have been free since the attention: the next layer's rows
-      // start loading (warp 7 has no part in the partial or the merge)
-      if (tid == kKvIssuer && i + 1 < n) issue_kv(i + 1);
+      // the next layer's rows start their way from HBM into L2 now; they
+      // move on into this CTA's shared memory at the end of the layer, so
+      // that the bulk of them does not queue ahead of the hand-off loads
+      if (tid == kKvIssuer && i + 1 < n) prefetch_kv(i + 1);
+      // the last of this head's items to finish merges them: a ticket,
+      // counted up for good, elects it (no fence: the partials carry their
+      // tags, and it polls them like any hand-off)
+      if (tid == 0) {
+        const unsigned t = atomicAdd(p.tickets + h, 1u);
+        const unsigned last = p.ticket_base + (unsigned)i * (unsigned)p.nsplit + (unsigned)p.nsplit - 1u;
+        red[9] = __int_as_float(t == last ? 1 : 0);
+      }
+      __syncthreads();
       trace.mark();
-      if (merger) {
+      if (__float_as_int(red[9])) {
         // this head's splits -> 128 values of the attention vector: thread
-        // (g, d) = (tid >> 6, tid & 63) of the first 128, every split's O[d]
-        // in flight at once; warp 4 takes every split's (m, l)
+        // (g, d) = (tid >> 6, tid & 63) of the first 128 loads every split's
+        // O[d] at once; warp 4 takes every split's (m, l)
+        const uint2* first = p.px + (long long)h * p.nsplit * kStackPartial;
         float v[kStackMaxSplits];
         const int g = (tid >> 6) & 1, d = tid & 63;
         if (tid < 128) {
-          stack_take_n<kStackMaxSplits>(p, p.px + (long long)b * kStackPartial + g * 66 + d, kStackPartial, p.nsplit,
-                                        tag, v, poll);
+          stack_take_n<kStackMaxSplits>(p, first + g * 66 + d, kStackPartial, p.nsplit, tag, v, poll);
         } else if (warp == 4) {
           // lane = (head g2, split sp) = (lane >> 4, lane & 15)
           const int g2 = lane >> 4, sp = lane & 15;
           float mm = -INFINITY, ll = 0.0f;
           if (sp < p.nsplit) {
             float ml[2];
-            stack_take_n<2>(p, p.px + (long long)(b + sp) * kStackPartial + g2 * 66 + 64, 1, 2, tag, ml, poll);
+            stack_take_n<2>(p, first + (long long)sp * kStackPartial + g2 * 66 + 64, 1, 2, tag, ml, poll);
             mm = poll.failed ? -INFINITY : ml[0];
             ll = ml[1];
           }
@@ -622,8 +687,8 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
           if (!isfinite(a)) flag_error(p.err, QX_ERR_BIT_NONFINITE);
           st_tagged(p.ax + h * 128 + tid, a, tag);
         }
-        trace.mark();
       }
+      trace.mark();
     }
 
     // ---- C: o-projection rows and the residual ------------------------------------
@@ -660,6 +725,9 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
     }
     __syncthreads();  // every warp is done with this layer's weights
     if (tid == 0 && i + 2 < n) issue_w(i + 2);  // their buffer takes layer i + 2's
+    // the next layer's rows (in L2 since the attention) into shared memory
+    if (tid == kKvIssuer && i + 1 < n) issue_kv(i + 1);
+
   }
 
   // ---- leave: copies in flight first (bounded) ---------------------------------------
