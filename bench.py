@@ -1214,6 +1214,10 @@ def main():
             print(json.dumps(line), flush=True)
         return 0
 
+    if world > 1:
+        # NCCL writes its log (its version line included, under NCCL_DEBUG)
+        # to stdout unless told otherwise: keep stdout for the one JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     import torch
     if world > 1:
         import datetime

@@ -167,6 +167,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, 
       : "memory");
 }
 
+// Prefetch of a TMA tile into L2 only: nothing lands in shared memory and
+// no barrier completes (a plain copy for this CTA). L2 stays coherent with later
+// writes, so any rows may be prefetched, settled or not.
+__device__ __forceinline__ void tma_prefetch_3d(const void* tmap, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(tmap), "r"(x), "r"(y),
+               "r"(z)
+               : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

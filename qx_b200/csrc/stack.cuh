@@ -130,14 +130,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
-// Prefetch of a TMA tile into L2 only (nothing lands in this CTA's shared
-// memory; plain, no multicast).
-__device__ __forceinline__ void tma_prefetch_3d(const void* tmap, int x, int y, int z) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(tmap), "r"(x), "r"(y),
-               "r"(z)
-               : "memory");
-}
-
 // Poll state of one thread: when it first had to wait, and how often.
 struct StackPoll {
   unsigned long long t0 = 0;

@@ -212,7 +212,7 @@ def test_exchange_two_gpus_one_process():
         c.close()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_exchange_torchrun_ranks(world):
     import torch
     if torch.cuda.device_count() < world:
