@@ -932,14 +932,12 @@ __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_consta
 #pragma unroll
     for (int r = 0; r < 8; ++r) ov[r] = 0.0f;
     if (tid < 32) {
-#pragma unroll
-      for (int r = 0; r < 8; ++r)
-        if (r < W && ok) ok = wait_tagged(in + r * rows * ROW + tid, tag, &ov[r]);
-    }
-    if (tid < 2 * W) {
+      // dim tid of every rank's slice, and lanes 0 .. 2W-1 also (m, l) of
+      // rank tid / 2, all polled together
       float v = 0.0f;
-      if (ok) ok = wait_tagged(in + (tid >> 1) * rows * ROW + 32 + (tid & 1), tag, &v);
-      xml[tid] = v;
+      const uint2* ml = tid < 2 * W ? in + (tid >> 1) * rows * ROW + 32 + (tid & 1) : nullptr;
+      ok = wait_tagged_n<8>(in + tid, rows * ROW, W, ml, tag, ov, &v);
+      if (tid < 2 * W) xml[tid] = v;
     }
     if (!ok) {
       flag_error(p.err, QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER);

@@ -91,15 +91,13 @@ __global__ void __launch_bounds__(kExchThreads) qx_exchange_merge_kernel(const _
   float o[kMaxPeers];
 #pragma unroll
   for (int r = 0; r < kMaxPeers; ++r) o[r] = 0.0f;
-  if (tid < D) {
-#pragma unroll
-    for (int r = 0; r < kMaxPeers; ++r)
-      if (r < W && ok) ok = wait_tagged(in + r * rs + tid, tag, &o[r]);
-  }
-  if (tid < 2 * W) {
+  {
+    // O[tid] of every rank (tid < D) and, on threads 0 .. 2W-1, (m, l) of
+    // rank tid / 2, all polled together
     float v = 0.0f;
-    if (ok) ok = wait_tagged(in + (tid >> 1) * rs + D + (tid & 1), tag, &v);
-    ml[tid] = v;
+    const uint2* mlp = tid < 2 * W ? in + (tid >> 1) * rs + D + (tid & 1) : nullptr;
+    ok = wait_tagged_n<kMaxPeers>(in + tid, rs, tid < D ? W : 0, mlp, tag, o, &v);
+    if (tid < 2 * W) ml[tid] = v;
   }
   if (!ok) {
     flag_error(p.err, QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER);

@@ -80,6 +80,31 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return x < -125.0f ? 0.0f : r;
 }
 
+// exp2_poly of two arguments with the packed f32 operations of sm_100 (one
+// instruction per pair for each add and FMA); bit-identical to two calls of
+// exp2_poly, since every packed lane rounds like its scalar twin and
+// xc - n is exact.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  const float2 xc = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
+  const float2 j = __fadd2_rn(xc, make_float2(12582912.0f, 12582912.0f));
+  const float2 n = __fadd2_rn(j, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), xc);
+  float2 p = __ffma2_rn(make_float2(0.05517132207751274f, 0.05517132207751274f), f,
+                        make_float2(0.24261054396629333f, 0.24261054396629333f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  p = __ffma2_rn(p, f, make_float2(0.9999281167984009f, 0.9999281167984009f));
+  const float rx = __int_as_float(__float_as_int(p.x) + (__float_as_int(j.x) << 23));
+  const float ry = __int_as_float(__float_as_int(p.y) + (__float_as_int(j.y) << 23));
+  return make_float2(x.x < -125.0f ? 0.0f : rx, x.y < -125.0f ? 0.0f : ry);
+}
+
+// max of three f32 values in one instruction (sm_100's three-input max)
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ float softmax_exp(float x, bool pinned) {
   return pinned ? pinned_exp(x) : native_exp(x);
 }

@@ -63,16 +63,40 @@ __device__ __forceinline__ uint2 ld_tagged(const uint2* p) {
   return v;
 }
 
-// Poll one tagged value until it carries `tag`; false after kMaxWaitNs.
-__device__ __forceinline__ bool wait_tagged(const uint2* p, unsigned tag, float* v) {
-  uint2 x = ld_tagged(p);
-  if (x.y != tag) {
-    const unsigned long long t0 = global_ns();
-    while ((x = ld_tagged(p)).y != tag) {
-      if (global_ns() - t0 > kMaxWaitNs) return false;
+// Poll `count` <= N tagged values p[k * stride] (and `extra`, if not null)
+// until every one carries `tag`. All loads are in flight together and only
+// the values still missing are loaded again, so waiting for N peers costs one
+// round trip after the last one arrived, not N. v[k] is 0 for k >= count.
+// False after kMaxWaitNs.
+template <int N>
+__device__ __forceinline__ bool wait_tagged_n(const uint2* p, long long stride, int count, const uint2* extra,
+                                              unsigned tag, float* v, float* vextra) {
+  uint2 x[N];
+#pragma unroll
+  for (int k = 0; k < N; ++k) x[k] = k < count ? ld_tagged(p + k * stride) : make_uint2(0u, tag);
+  uint2 e = extra ? ld_tagged(extra) : make_uint2(0u, tag);
+  unsigned long long t0 = 0;
+  for (unsigned spins = 0;; ++spins) {
+    bool all = e.y == tag;
+#pragma unroll
+    for (int k = 0; k < N; ++k) all &= x[k].y == tag;
+    if (all) break;
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+      if (x[k].y != tag) x[k] = ld_tagged(p + k * stride);
+    if (e.y != tag) e = ld_tagged(extra);
+    if ((spins & 15u) == 0u) {
+      const unsigned long long now = global_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kMaxWaitNs) {
+        return false;
+      }
     }
   }
-  *v = __uint_as_float(x.x);
+#pragma unroll
+  for (int k = 0; k < N; ++k) v[k] = __uint_as_float(x[k].x);
+  if (vextra) *vextra = __uint_as_float(e.x);
   return true;
 }
 

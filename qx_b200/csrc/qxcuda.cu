@@ -2259,6 +2259,15 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
       per_sm = 1;
     p.early_trigger = rope_grid <= per_sm * ctx->sm_count ? 1 : 0;
   }
+  // Query block qb attends qb + 1 key tiles. When one CTA per (block, kv
+  // head) leaves a second wave of at least half the SMs but pairs of blocks
+  // fit in one wave, CTA j takes blocks nqb-1-j/8 and j/8 (nqb + 1 tiles
+  // each). A smaller second wave costs less than a pair's item boundary
+  // (L = 1216, 19 blocks: 18.0 us unpaired against 20.5 us paired; L = 2048,
+  // 32 blocks: 28.0 against 27.5).
+  const int paired_grid = (nqb + 1) / 2 * 8;
+  p.paired = (2 * nqb * 8 >= 3 * ctx->sm_count && paired_grid <= ctx->sm_count) ? 1 : 0;
+  const int attn_grid = p.paired ? paired_grid : nqb * 8;
   TraceRun tr(ctx, "prefill", (size_t)nqb * 8 * 3);  // softmax timeline, then the two MMA issuers'
   p.trace = tr.buf;
   qx_prefill_rope_kernel<<<rope_grid, 256, 0, ctx->stream>>>(p);
@@ -2268,7 +2277,7 @@ qxc_status qxc_prefill(qxc_ctx* ctx, qxc_kv* kv, const qxc_prefill_args* a) {
   // initialise barriers and TMEM while the RoPE grid drains, and wait for it
   // (griddepcontrol.wait) before the first TMA load
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nqb * 8);
+  cfg.gridDim = dim3(attn_grid);
   cfg.blockDim = dim3(PrefillCfg::NT);
   cfg.dynamicSmemBytes = PrefillCfg::SMEM;
   cfg.stream = ctx->stream;

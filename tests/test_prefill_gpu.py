@@ -35,6 +35,38 @@ def test_prefill_matches_iterated_decode(gpu_ctx, oracle, L):
     assert arena.len(0) == L
 
 
+@pytest.mark.parametrize("L", [1153, 1800, 2047, 2300])
+def test_prefill_paired_blocks(gpu_ctx, oracle, L):
+    """Lengths around the paired grid on 148 SMs. 1153 (19 blocks): a second
+    wave of 4 CTAs, left unpaired. 1800 (29 blocks): paired, CTA j runs query
+    blocks 28-j and j of one kv head back to back, the middle block alone.
+    2047: paired, with a ragged last block. 2300 (36 blocks): the largest
+    paired grid."""
+    q, k, v, arena, got = run_prefill(gpu_ctx, L, syn.seed_for(2) + 7 * L)
+    st, kc, vc, ref = oracle.granite_prefill(q, k, v, oracle.BF16, oracle.BF16, threads=8)
+    assert st == 0
+    assert normwise(got, ref) <= 2e-2
+    gk, gv = arena.read(0, 0, 0, L)
+    assert np.array_equal(gk, kc) and np.array_equal(gv, vc)
+
+
+@pytest.mark.parametrize("L", [200, 2047])
+def test_prefill_bf16_output(gpu_ctx, oracle, L):
+    """The bf16 output rows (unpaired and paired grids) against the oracle."""
+    import torch
+    q = syn.to_bf16_bits(syn.normal(0x5200 + L, (L, 16, 64), 0.5))
+    k = syn.to_bf16_bits(syn.normal(0x5201 + L, (L, 8, 64), 0.5))
+    v = syn.to_bf16_bits(syn.normal(0x5202 + L, (L, 8, 64), 0.5))
+    arena = KvArena(gpu_ctx, MODEL_GRANITE, 1, 1, L, BF16, BF16)
+    dev = lambda a: torch.from_numpy(a.view(np.int16)).cuda()
+    out = torch.zeros(L, 16, 64, device="cuda", dtype=torch.bfloat16)
+    arena.prefill(dev(q), dev(k), dev(v), out, L, out_dtype=BF16)
+    gpu_ctx.sync()
+    st, _, _, ref = oracle.granite_prefill(q, k, v, oracle.BF16, oracle.BF16, threads=8)
+    assert st == 0
+    assert normwise(out.float().cpu().numpy(), ref) <= 2e-2
+
+
 @pytest.mark.slow
 def test_prefill_2048(gpu_ctx, oracle):
     L = 2048
