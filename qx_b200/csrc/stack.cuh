@@ -32,9 +32,11 @@
 //
 // The next layer's cache rows (16.8 MB of fp32 KV at 4096 positions) are
 // prefetched from HBM into L2 as soon as a layer's attention is done and
-// copied on into shared memory (TMA) at the layer's end, so the HBM stream
-// runs under the dependent steps. Only L2-to-SM bytes, not HBM-to-SM ones,
-// then queue ahead of the hand-off loads on the same SM.
+// copied on into shared memory (TMA) in two parts, a quarter at the layer's
+// end and the rest once the next hidden state has arrived, so the HBM
+// stream runs under the dependent steps. Only L2-to-SM bytes, not HBM-to-SM
+// ones, then queue ahead of the hand-off loads on the same SM, and few of
+// them ahead of the hidden-state poll.
 //
 // Hand-offs carry no fence and no counter: every 32-bit value travels with a
 // 32-bit tag (this launch's generation and the layer) in one 8-byte store,
@@ -317,20 +319,29 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
   int kv_issued = 0, kv_waited = 0;
   int w_issued[2] = {0, 0}, w_waited[2] = {0, 0};
 
-  auto issue_kv = [&](int i) {  // thread 0: this item's rows of layer i
+  // This item's rows of layer i into shared memory, in one barrier phase.
+  // part 0: every K and V tile. part 1 (issued at the end of layer i - 1):
+  // the first kStackEarlyKTiles K tiles, and the expected byte count of the
+  // whole phase. part 2 (issued once layer i's hidden state has arrived):
+  // the other K tiles and all V tiles. Each part's L2-to-shared bytes queue
+  // ahead of the hand-off loads the CTA issues next: a quarter of the rows
+  // ahead of the hidden-state poll, the rest beside the q/k/v mat-vec.
+  constexpr int kStackEarlyKTiles = 2;
+  auto issue_kv = [&](int i, int part) {
     if (!has_item) return;
     fence_proxy_async_shared();  // generic writes to the tiles (the appended row) before the async ones
     const int layer = p.layer_begin + i;
-    mbar_arrive_expect_tx(bar_kv, (uint32_t)(ntiles * 2 * C::TILE));
+    if (part != 2) mbar_arrive_expect_tx(bar_kv, (uint32_t)(ntiles * 2 * C::TILE));
     for (int t = 0; t < ntiles; ++t) {
       const int z = (int)(((long long)p.seq * p.arena_layers + layer) * p.capacity + begin + t * kStackTileRows);
+      const bool k_now = part == 0 || (part == 1) == (t < kStackEarlyKTiles);
 #pragma unroll
       for (int bx = 0; bx < 2; ++bx) {
-        tma_load_3d(ks + t * C::TILE + bx * C::BOX, &p.tmk, bx * 32, h, z, bar_kv);
-        tma_load_3d(vs + t * C::TILE + bx * C::BOX, &p.tmv, bx * 32, h, z, bar_kv);
+        if (k_now) tma_load_3d(ks + t * C::TILE + bx * C::BOX, &p.tmk, bx * 32, h, z, bar_kv);
+        if (part != 1) tma_load_3d(vs + t * C::TILE + bx * C::BOX, &p.tmv, bx * 32, h, z, bar_kv);
       }
     }
-    ++kv_issued;
+    if (part != 2) ++kv_issued;
   };
   auto prefetch_kv = [&](int i) {  // this item's rows of layer i into L2
     if (!has_item) return;
@@ -379,7 +390,7 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
     return true;
   };
 
-  if (tid == kKvIssuer) issue_kv(0);
+  if (tid == kKvIssuer) issue_kv(0, 0);
   if (tid == 0) {
     issue_w(0);
     if (n > 1) issue_w(1);
@@ -419,6 +430,7 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
         ok = false;
         break;
       }
+      if (tid == kKvIssuer && i > 0) issue_kv(i, 2);  // the rest of this layer's rows
       trace.mark();
       // cpu_rms_norm_simd: thread t sums x[t], x[t + 256], ... by fma; the
       // warps, then the 8 warp sums, reduce as reduce_simd32
@@ -468,7 +480,8 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
 
     // ---- B: the attention item --------------------------------------------------
     if (has_item) {
-      // the split's rows have been in shared memory since the previous layer
+      if (!has_q && tid == kKvIssuer && i > 0) issue_kv(i, 2);
+      // the split's rows, copied since the previous layer's end
       if (tid == 0) {
         if (mbar_wait_bounded(bar_kv, (uint32_t)(kv_waited & 1), p.err)) ++kv_waited;
         else stack_raise(p, poll);
@@ -629,8 +642,9 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
         }
       }
       // the next layer's rows start their way from HBM into L2 now; they
-      // move on into this CTA's shared memory at the end of the layer, so
-      // that the bulk of them does not queue ahead of the hand-off loads
+      // move on into this CTA's shared memory later (issue_kv's parts 1 and
+      // 2), so that the bulk of them does not queue ahead of the hand-off
+      // loads
       if (tid == kKvIssuer && i + 1 < n) prefetch_kv(i + 1);
       // the last of this head's items to finish merges them: a ticket,
       // counted up for good, elects it (no fence: the partials carry their
@@ -717,9 +731,8 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
     }
     __syncthreads();  // every warp is done with this layer's weights
     if (tid == 0 && i + 2 < n) issue_w(i + 2);  // their buffer takes layer i + 2's
-    // the next layer's rows (in L2 since the attention) into shared memory
-    if (tid == kKvIssuer && i + 1 < n) issue_kv(i + 1);
-
+    // the first of the next layer's rows (in L2 since the attention) into shared memory
+    if (tid == kKvIssuer && i + 1 < n) issue_kv(i + 1, 1);
   }
 
   // ---- leave: copies in flight first (bounded) ---------------------------------------
