@@ -113,6 +113,12 @@ struct DecodeParams {
   int pinned_exp;
   int emit_partials;  // write (O, m, l) per query head instead of O / l
   int external_merge;  // splits only store partials; qx_split_merge_kernel merges them
+  // One-wave tensor-core decode with 2..64 splits: the splits of each (unit,
+  // kv head) store their partials tagged and merge them among themselves
+  // (slice_merge) instead of in qx_split_merge_kernel.
+  int slice_merge;
+  unsigned merge_tag;  // this call's tag for those partials (never 0)
+  uint2* tpartials;    // scratch [items][G][D+2] {value bits, tag}
   int early_trigger;   // one-wave grid: let the next grid launch early (griddepcontrol)
   // Single-sequence calls (seq_table == nullptr) on a contiguous arena:
   // cache rows [0, pre_rows) of the sequence were written by grids that have
@@ -841,6 +847,127 @@ __global__ void __launch_bounds__(DecodeCfg<GraniteVerify4, KT, VT>::NT, 2)
 // the decode kernel used.
 constexpr int kMergeLoads = 16;
 
+// One pass of a quad's log-sum-exp merge: (mv, lv, ov)[k] are split
+// q + 4k's (m, l, O[d]) of this pass (m = -inf, l = O = 0 past the last
+// split); the quad's running (M, L, o) absorb them. The split merge kernel
+// and the decode kernels' slice merge (tc_slice_merge) both run this, so
+// they produce the same bits.
+__device__ __forceinline__ void merge_quad_pass(const float* mv, const float* lv, const float* ov, bool pinned,
+                                                float& M, float& L, float& o) {
+  float mx = mv[0];
+#pragma unroll
+  for (int k = 1; k < kMergeLoads; ++k) mx = fmaxf(mx, mv[k]);
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  const float Mn = fmaxf(M, mx);
+  const float a = M == -INFINITY ? 0.0f : softmax_exp(M - Mn, pinned);
+  float Ls = 0.0f, os = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kMergeLoads; ++k) {
+    const float w = mv[k] == -INFINITY ? 0.0f : softmax_exp(mv[k] - Mn, pinned);
+    Ls = fmaf(w, lv[k], Ls);
+    os = fmaf(w, ov[k], os);
+  }
+  Ls += __shfl_xor_sync(0xffffffffu, Ls, 1);
+  os += __shfl_xor_sync(0xffffffffu, os, 1);
+  Ls += __shfl_xor_sync(0xffffffffu, Ls, 2);
+  os += __shfl_xor_sync(0xffffffffu, os, 2);
+  L = fmaf(L, a, Ls);
+  o = fmaf(o, a, os);
+  M = Mn;
+}
+
+// The splits of one (unit cu, kv head h) merge their partials among
+// themselves, with no second grid: every split stores its (O, m, l) as tagged
+// values (st_tagged), then split s takes the 32-dim output slices s,
+// s + nsplit, ... of the group's G x D outputs and merges each as
+// qx_split_merge_kernel does (four lanes per dim, one merge_quad_pass over
+// at most 4 x kMergeLoads splits), polling the tagged values it reads; the
+// outputs equal that kernel's bit for bit. A split waits for the others, so
+// every CTA of the grid must be resident at once: the host takes this path
+// only for a grid of one wave. Each wait is bounded (kMaxWaitNs); a timeout
+// sets QX_ERR_BIT_TIMEOUT and leaves the slice unwritten. Run by 128
+// threads, thread t holding dim t of every head (O[k], and Mg[k], Lg[k] of
+// head k).
+template <int G, int D, int HQ>
+__device__ __forceinline__ void slice_merge(const DecodeParams& p, const float* O, const float* Mg, const float* Lg,
+                                            int nsplit, int s, long long cu, int h, int tid, bool pinned) {
+  static_assert(D == 128, "thread t holds dim t of every head");
+  const unsigned tag = p.merge_tag;
+  const long long stride = (long long)G * (D + 2);
+  uint2* mine = p.tpartials + (long long)blockIdx.x * stride;
+#pragma unroll
+  for (int k = 0; k < G; ++k) st_tagged(mine + k * (D + 2) + tid, O[k], tag);
+  if (tid < G) {
+    float m = Mg[0], l = Lg[0];
+#pragma unroll
+    for (int k = 1; k < G; ++k)
+      if (k == tid) {
+        m = Mg[k];
+        l = Lg[k];
+      }
+    st_tagged(mine + tid * (D + 2) + D, m, tag);
+    st_tagged(mine + tid * (D + 2) + D + 1, l, tag);
+  }
+  const uint2* first = p.tpartials + (long long)(blockIdx.x - s) * stride;
+  const int q = tid & 3, dl = tid >> 2;
+  constexpr int SLICES = G * (D / 32);
+  bool failed = false;
+  for (int j = s; j < SLICES; j += nsplit) {
+    const int g = j / (D / 32), d = (j % (D / 32)) * 32 + dl;
+    const uint2* base = first + (long long)g * (D + 2);
+    uint2 mt[kMergeLoads], lt[kMergeLoads], ot[kMergeLoads];
+#pragma unroll
+    for (int k = 0; k < kMergeLoads; ++k) {
+      const int i = q + 4 * k;
+      if (i < nsplit && !failed) {
+        mt[k] = ld_tagged(base + i * stride + D);
+        lt[k] = ld_tagged(base + i * stride + D + 1);
+        ot[k] = ld_tagged(base + i * stride + d);
+      } else {
+        mt[k] = make_uint2(__float_as_uint(-INFINITY), tag);
+        lt[k] = ot[k] = make_uint2(0u, tag);
+      }
+    }
+    // every value still missing is loaded again, all in flight together
+    unsigned long long t0 = 0;
+    for (unsigned spins = 0;; ++spins) {
+      bool all = true;
+#pragma unroll
+      for (int k = 0; k < kMergeLoads; ++k) all &= mt[k].y == tag && lt[k].y == tag && ot[k].y == tag;
+      if (all || failed) break;
+#pragma unroll
+      for (int k = 0; k < kMergeLoads; ++k) {
+        const int i = q + 4 * k;  // (values past the last split carry the tag already)
+        if (mt[k].y != tag) mt[k] = ld_tagged(base + i * stride + D);
+        if (lt[k].y != tag) lt[k] = ld_tagged(base + i * stride + D + 1);
+        if (ot[k].y != tag) ot[k] = ld_tagged(base + i * stride + d);
+      }
+      if ((spins & 15u) == 0u) {
+        const unsigned long long now = global_ns();
+        if (t0 == 0) t0 = now;
+        else if (now - t0 > kMaxWaitNs) failed = true;
+      }
+    }
+    float mv[kMergeLoads], lv[kMergeLoads], ov[kMergeLoads];
+#pragma unroll
+    for (int k = 0; k < kMergeLoads; ++k) {
+      mv[k] = __uint_as_float(mt[k].x);
+      lv[k] = __uint_as_float(lt[k].x);
+      ov[k] = __uint_as_float(ot[k].x);
+    }
+    float M = -INFINITY, L = 0.0f, o = 0.0f;
+    merge_quad_pass(mv, lv, ov, pinned, M, L, o);
+    if (failed) {
+      flag_error(p.err, QX_ERR_BIT_TIMEOUT);
+    } else if (q == 0) {
+      const float v = o / L;
+      if (!isfinite(v)) flag_error(p.err, QX_ERR_BIT_NONFINITE);
+      store_any(p.out, out_elem<G, D, HQ, 1, G>(p, cu, h, g, d), p.out_dtype, v);
+    }
+  }
+}
+
 template <int G, int D, int HKV, int HQ, int NTOK = 1, int G0 = G>
 __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_constant__ DecodeParams p) {
   const int tid = threadIdx.x, q = tid & 3;
@@ -873,27 +1000,7 @@ __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_consta
       lv[k] = i < n ? __ldcg(pi + D + 1) : 0.0f;
       ov[k] = i < n ? __ldcg(pi + d) : 0.0f;
     }
-    float mx = mv[0];
-#pragma unroll
-    for (int k = 1; k < kMergeLoads; ++k) mx = fmaxf(mx, mv[k]);
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float Mn = fmaxf(M, mx);
-    const float a = M == -INFINITY ? 0.0f : softmax_exp(M - Mn, pinned);
-    float Ls = 0.0f, os = 0.0f;
-#pragma unroll
-    for (int k = 0; k < kMergeLoads; ++k) {
-      const float w = mv[k] == -INFINITY ? 0.0f : softmax_exp(mv[k] - Mn, pinned);
-      Ls = fmaf(w, lv[k], Ls);
-      os = fmaf(w, ov[k], os);
-    }
-    Ls += __shfl_xor_sync(0xffffffffu, Ls, 1);
-    os += __shfl_xor_sync(0xffffffffu, os, 1);
-    Ls += __shfl_xor_sync(0xffffffffu, Ls, 2);
-    os += __shfl_xor_sync(0xffffffffu, os, 2);
-    L = fmaf(L, a, Ls);
-    o = fmaf(o, a, os);
-    M = Mn;
+    merge_quad_pass(mv, lv, ov, pinned, M, L, o);
   }
   if (p.xworld) {
     // KV-length split across GPUs: this CTA's slice of this rank's partial

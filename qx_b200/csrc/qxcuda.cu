@@ -47,6 +47,11 @@ struct qxc_ctx {
   size_t partials_cap = 0;  // floats
   int* tickets = nullptr;
   size_t tickets_cap = 0;  // ints
+  // tagged partials of the slice merge (zeroed when allocated: tag 0 is no
+  // call's) and the last call's tag
+  uint2* tpartials = nullptr;
+  size_t tpartials_cap = 0;  // uint2
+  unsigned merge_gen = 0;
   // per-call sequence tables: device ring + pinned host ring
   static constexpr int kRing = 8;
   SeqInfo* seq_dev[kRing] = {};
@@ -627,6 +632,38 @@ qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer
   return QXC_OK;
 }
 
+// A Qwen decode whose grid is one wave, with 2 to 64 splits of some (unit,
+// kv head), merges its splits inside the decode grid (slice_merge in
+// decode.cuh) instead of a second grid: the splits wait for one another,
+// which a one-wave grid allows, and the merge kernel's launch and its wait
+// for the decode grid's end drop out of the call.
+qxc_status use_slice_merge(qxc_ctx* ctx, const qxc_kv* kv, const CallPlan& plan, DecodeParams* p) {
+  if (kv->desc.model != QXC_MODEL_QWEN3) return QXC_OK;
+  int max_split = 1;
+  for (const SeqInfo& si : plan.tab) max_split = std::max(max_split, (si.attend + plan.chunk - 1) / plan.chunk);
+  if (max_split < 2 || max_split > 4 * kMergeLoads) return QXC_OK;
+  if (plan.items > decode_blocks_per_sm(kv) * ctx->sm_count) return QXC_OK;
+  const size_t need = (size_t)plan.items * kv->hq / plan.units * (kv->d + 2);
+  if (need > ctx->tpartials_cap) {
+    if (ctx->tpartials) {
+      QXC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+      cudaFree(ctx->tpartials);
+      ctx->tpartials = nullptr;
+      ctx->tpartials_cap = 0;
+    }
+    QXC_CUDA(ctx, cudaMalloc(&ctx->tpartials, need * sizeof(uint2)));
+    QXC_CUDA(ctx, cudaMemsetAsync(ctx->tpartials, 0, need * sizeof(uint2), ctx->stream));
+    ctx->tpartials_cap = need;
+  }
+  ctx->merge_gen += 1u;
+  if (ctx->merge_gen == 0u) ctx->merge_gen = 1u;
+  p->slice_merge = 1;
+  p->external_merge = 0;
+  p->merge_tag = ctx->merge_gen;
+  p->tpartials = ctx->tpartials;
+  return QXC_OK;
+}
+
 bool default_pinned(const qxc_kv* kv, int flags) {
   if (flags & QXC_DECODE_NATIVE_EXP) return false;
   if (flags & QXC_DECODE_PINNED_EXP) return true;
@@ -1005,6 +1042,7 @@ void qxc_destroy(qxc_ctx* ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   cudaFree(ctx->partials);
+  cudaFree(ctx->tpartials);
   cudaFree(ctx->tickets);
   for (int i = 0; i < qxc_ctx::kRing; ++i) {
     cudaFree(ctx->seq_dev[i]);
@@ -1427,6 +1465,8 @@ qxc_status qxc_decode(qxc_ctx* ctx, qxc_kv* kv, const qxc_decode_args* a) {
   p.out_dtype = a->out_dtype;
   p.pinned_exp = default_pinned(kv, a->flags) ? 1 : 0;
   p.emit_partials = 0;
+  st = use_slice_merge(ctx, kv, plan, &p);
+  if (st != QXC_OK) return st;
   st = launch_decode(ctx, kv, p, plan.items);
   if (st != QXC_OK) return st;
   if (!(a->flags & QXC_DECODE_NO_ADVANCE))
