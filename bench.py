@@ -664,7 +664,8 @@ def run_config3(args, world, rank, local):
                      clk, launches)
     line["config"]["split"] = ctx.last_split
     line["roofline"] = hbm_roofline(B if world == 1 else per_rank_bytes, per,
-                                    "qx_decode_tc_kernel<bf16,TcQwen> + qx_split_merge_kernel (timed together)",
+                                    "qx_decode_tc_kernel<bf16,TcQwen> (splits merged inside the grid)" if world == 1
+                                    else "qx_decode_tc_kernel<bf16,TcQwen> + qx_split_merge_kernel (timed together)",
                                     "config3" if world == 1 else None)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))

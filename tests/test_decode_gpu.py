@@ -358,6 +358,46 @@ def test_qwen_config3_full_length(gpu_ctx, oracle):
     assert np.array_equal(gk.reshape(-1), kr)
 
 
+@pytest.mark.parametrize("split", [128, 0])
+def test_qwen_ragged_sequences_one_call(gpu_ctx, oracle, split):
+    """Three Qwen sequences of different lengths in one call. At split 128
+    they take 3, 9 and 23 splits (140 CTAs, one wave), so each (sequence, kv
+    head) merges its own number of splits inside the decode grid; two calls
+    in a row reuse the tagged partials under a new tag."""
+    import torch
+    prefixes, cap = [300, 1100, 2900], 3000
+    arena = KvArena(gpu_ctx, MODEL_QWEN3, 1, 3, cap, BF16, BF16)
+    caches = []
+    for sq, pre in enumerate(prefixes):
+        _, _, _, kc, vc = qwen_case(0x7400 + sq, pre, cap)
+        arena.write(sq, 0, 0, kc[:pre], vc[:pre])
+        arena.set_len(sq, pre)
+        caches.append((kc, vc))
+    ones = np.ones(128, np.float32)
+    dev = lambda a: torch.from_numpy(a.view(np.int16).reshape(len(prefixes), -1)).cuda()
+    pos = list(prefixes)
+    for step in range(2):
+        qs, ks, vs, refs = [], [], [], []
+        for sq in range(3):
+            q, k, v, _, _ = qwen_case(0x7500 + 8 * step + sq, 0, 1)
+            kc, vc = caches[sq]
+            _, _, ref, _ = oracle.qwen_decode(q, k, v, ones, ones, kc, vc, pos[sq], BF16, threads=8)
+            qs.append(q), ks.append(k), vs.append(v), refs.append(ref)
+        out = torch.zeros(3, 4096, device="cuda")
+        arena.decode(dev(np.stack(qs)), dev(np.stack(ks)), dev(np.stack(vs)), out, pos, seq_ids=[0, 1, 2],
+                     split=split)
+        gpu_ctx.sync()
+        got = out.cpu().numpy()
+        for sq in range(3):
+            assert normwise(got[sq], refs[sq]) <= 2e-3, (step, sq)
+            assert np.abs(got[sq] - refs[sq]).max() <= 0.01
+        pos = [p + 1 for p in pos]
+    for sq in range(3):
+        gk, gv = arena.read(sq, 0, 0, pos[sq])
+        assert np.array_equal(gk.reshape(pos[sq], -1), caches[sq][0][:pos[sq]].reshape(pos[sq], -1))
+        assert np.array_equal(gv.reshape(pos[sq], -1), caches[sq][1][:pos[sq]].reshape(pos[sq], -1))
+
+
 @pytest.mark.parametrize("alternate", [False, True])
 def test_qwen_back_to_back_steps(gpu_ctx, oracle, alternate):
     """Decode steps queued back to back with no host sync. Each step's grid
