@@ -28,7 +28,9 @@
 //      finish, which merges the head's splits into 128 values of the
 //      attention vector.
 //   C  CTAs with o-projection rows: the attention vector, their rows of the
-//      o-projection and the residual: their part of hidden(i + 1).
+//      o-projection and the residual: their part of hidden(i + 1). The
+//      residual's input rows come from the CTA's own copy of hidden(i) in
+//      shared memory (taken in A), not from a second global load.
 //
 // The next layer's cache rows (16.8 MB of fp32 KV at 4096 positions) are
 // prefetched from HBM into L2 as soon as a layer's attention is done and
@@ -118,7 +120,8 @@ struct StackCfg {
   static constexpr int OFF_MW = OFF_WML + 64 * 4;       // float [2][16] merge weights, [2] L
   static constexpr int OFF_RED = OFF_MW + 64 * 4;       // float [8] warp sums, [1] scale
   static constexpr int OFF_ROPE = OFF_RED + 64;         // float [32][2] (sin, cos) at the position, int ok, KV counts
-  static constexpr int OFF_BAR = OFF_ROPE + 288;        // 3 mbarriers: KV, weights 0, weights 1
+  static constexpr int OFF_H = OFF_ROPE + 288;          // float [1024] this layer's input hidden (the residual)
+  static constexpr int OFF_BAR = OFF_H + 1024 * 4;      // 3 mbarriers: KV, weights 0, weights 1
   static constexpr int SMEM = OFF_BAR + 32 + 1024;      // + slack to align the base to 1024
 };
 static_assert(StackCfg::SMEM <= 227 * 1024, "the stack kernel's shared memory must fit one SM");
@@ -259,6 +262,7 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
   unsigned char* ks = sm + C::OFF_K;
   unsigned char* vs = sm + C::OFF_V;
   float* xs = reinterpret_cast<float*>(sm + C::OFF_X);
+  float* hs = reinterpret_cast<float*>(sm + C::OFF_H);
   float* qs = reinterpret_cast<float*>(sm + C::OFF_Q);  // [2][64]
   float* newk = qs + 128;
   float* newv = qs + 192;
@@ -431,6 +435,8 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
         break;
       }
       if (tid == kKvIssuer && i > 0) issue_kv(i, 2);  // the rest of this layer's rows
+#pragma unroll
+      for (int k = 0; k < 4; ++k) hs[tid + 256 * k] = hv[k];  // the residual's input, for C
       trace.mark();
       // cpu_rms_norm_simd: thread t sums x[t], x[t + 256], ... by fma; the
       // warps, then the 8 warp sums, reduce as reduce_simd32
@@ -713,8 +719,11 @@ __global__ void __launch_bounds__(kStackThreads, 1) qx_attention_stack_kernel(co
       trace.mark();
       if (ro0 + warp < ro1) {
         const int r = ro0 + warp;
-        // the residual: this layer's input row r
-        const float hr = lane != 0 ? 0.0f : (i == 0 ? __ldg(p.hidden_in + r) : stack_take(p, hin_x + r, tag - 1u, poll));
+        // the residual: this layer's input row r (kept from A's hidden-state
+        // poll on a CTA with q/k/v rows)
+        const float hr = lane != 0 ? 0.0f
+                         : has_q  ? hs[r]
+                         : (i == 0 ? __ldg(p.hidden_in + r) : stack_take(p, hin_x + r, tag - 1u, poll));
         const float y = q4_row_dot_smem(wo_codes + warp * 512, wo_scales + warp * 32, xs, lane);
         if (lane == 0 && !poll.failed) {
           const float v = __fmaf_rn(kResidualMultiplier, y, hr);
