@@ -877,21 +877,106 @@ __device__ __forceinline__ void merge_quad_pass(const float* mv, const float* lv
   M = Mn;
 }
 
+// KV-length split across GPUs: slice `slice` (32 dims) of query head qh of
+// this rank's merged partial (quad lane 0 of quad dl holds o of dim
+// slice * 32 + dl; every lane holds M and L) goes tagged into every rank's
+// inbox; then the slices of all ranks are merged in rank order
+// (qx_lse_merge's arithmetic) straight into p.xout. The peers' matching
+// slices are being merged by grids that are one wave, so they are running
+// too. Run by 128 threads whose barrier is `sync`; xs is 17 floats of
+// shared memory. A CTA whose own merge gave up (local_ok false on any
+// thread) pushes nothing and fails the peer group, as a timed-out exchange
+// does (mark_peer_group_failed).
+template <int D, int HQ, class Sync>
+__device__ __forceinline__ void exchange_slice(const DecodeParams& p, long long cu, long long qh, int slice, float o,
+                                               float M, float L, bool local_ok, int tid, bool pinned, float* xs,
+                                               Sync sync) {
+  constexpr int S = D / 32, ROW = 34;
+  const int q = tid & 3, dl = tid >> 2;
+  float* xml = xs;  // m_r, l_r of up to 8 ranks
+  volatile int* xok = reinterpret_cast<volatile int*>(xs + 16);
+  // an earlier exchange on this group timed out: push nothing (one thread
+  // reads the word, so the whole CTA takes one branch)
+  if (tid == 0) *xok = peer_group_failed(p.xfailed) ? 0 : 1;
+  sync();
+  if (!local_ok) *xok = 0;
+  sync();
+  if (!*xok) {
+    if (tid == 0) {
+      flag_error(p.err, QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER);
+      mark_peer_group_failed(p.xfailed, p.xfailed_host);
+    }
+    return;
+  }
+  const int W = p.xworld;
+  unsigned* stp = p.xstep + qh * S + slice;
+  const unsigned st = *stp, tag = st + 1u, half = st & 1u;
+  const long long rows = (long long)HQ * S;
+  const long long mine = ((long long)half * W + p.xrank) * rows + qh * S + slice;
+  if (q == 0)
+    for (int r = 0; r < W; ++r) st_tagged(p.xinbox[r] + mine * ROW + dl, o, tag);
+  if (tid == 0)
+    for (int r = 0; r < W; ++r) {
+      st_tagged(p.xinbox[r] + mine * ROW + 32, M, tag);
+      st_tagged(p.xinbox[r] + mine * ROW + 33, L, tag);
+    }
+  const uint2* in = p.xinbox[p.xrank] + ((long long)half * W * rows + qh * S + slice) * ROW;
+  bool ok = true;
+  float ov[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) ov[r] = 0.0f;
+  if (tid < 32) {
+    // dim tid of every rank's slice, and lanes 0 .. 2W-1 also (m, l) of
+    // rank tid / 2, all polled together
+    float v = 0.0f;
+    const uint2* ml = tid < 2 * W ? in + (tid >> 1) * rows * ROW + 32 + (tid & 1) : nullptr;
+    ok = wait_tagged_n<8>(in + tid, rows * ROW, W, ml, tag, ov, &v);
+    if (tid < 2 * W) xml[tid] = v;
+  }
+  if (!ok) {
+    flag_error(p.err, QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER);
+    mark_peer_group_failed(p.xfailed, p.xfailed_host);
+    *xok = 0;
+  }
+  sync();
+  if (!*xok) return;
+  if (tid < 32) {
+    float mx = -INFINITY;
+    for (int r = 0; r < W; ++r) mx = fmaxf(mx, xml[2 * r]);
+    float Lt = 0.0f, Ot = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (r >= W) break;
+      const float m = xml[2 * r];
+      if (m == -INFINITY) continue;  // empty shard
+      const float w = softmax_exp(m - mx, pinned);
+      Lt = fmaf(w, xml[2 * r + 1], Lt);
+      Ot = fmaf(w, ov[r], Ot);
+    }
+    const float v = Ot / Lt;
+    if (!isfinite(v)) flag_error(p.err, QX_ERR_BIT_NONFINITE);
+    store_any(p.xout, (cu * HQ + qh) * D + slice * 32 + tid, p.xout_dtype, v);
+  }
+  if (tid == 0) *stp = st + 1u;
+}
+
 // The splits of one (unit cu, kv head h) merge their partials among
 // themselves, with no second grid: every split stores its (O, m, l) as tagged
 // values (st_tagged), then split s takes the 32-dim output slices s,
 // s + nsplit, ... of the group's G x D outputs and merges each as
 // qx_split_merge_kernel does (four lanes per dim, one merge_quad_pass over
 // at most 4 x kMergeLoads splits), polling the tagged values it reads; the
-// outputs equal that kernel's bit for bit. A split waits for the others, so
-// every CTA of the grid must be resident at once: the host takes this path
-// only for a grid of one wave. Each wait is bounded (kMaxWaitNs); a timeout
-// sets QX_ERR_BIT_TIMEOUT and leaves the slice unwritten. Run by 128
-// threads, thread t holding dim t of every head (O[k], and Mg[k], Lg[k] of
-// head k).
+// outputs equal that kernel's bit for bit. On a KV length split across GPUs
+// (p.xworld) each merged slice then goes through exchange_slice, as in that
+// kernel, with xs (17 floats of shared memory) as its scratch. A split
+// waits for the others, so every CTA of the grid must be resident at once:
+// the host takes this path only for a grid of one wave. Each wait is
+// bounded (kMaxWaitNs); a timeout sets QX_ERR_BIT_TIMEOUT and leaves the
+// slice unwritten. Run by 128 threads (barrier 1), thread t holding dim t
+// of every head (O[k], and Mg[k], Lg[k] of head k).
 template <int G, int D, int HQ>
 __device__ __forceinline__ void slice_merge(const DecodeParams& p, const float* O, const float* Mg, const float* Lg,
-                                            int nsplit, int s, long long cu, int h, int tid, bool pinned) {
+                                            int nsplit, int s, long long cu, int h, int tid, bool pinned, float* xs) {
   static_assert(D == 128, "thread t holds dim t of every head");
   const unsigned tag = p.merge_tag;
   const long long stride = (long long)G * (D + 2);
@@ -958,7 +1043,13 @@ __device__ __forceinline__ void slice_merge(const DecodeParams& p, const float* 
     }
     float M = -INFINITY, L = 0.0f, o = 0.0f;
     merge_quad_pass(mv, lv, ov, pinned, M, L, o);
-    if (failed) {
+    if (p.xworld) {
+      // KV-length split across GPUs: this slice of this rank's merge goes
+      // to every rank and the ranks' slices are merged into p.xout
+      exchange_slice<D, HQ>(p, cu, (long long)h * G + g, j % (D / 32), o, M, L, !failed, tid, pinned, xs,
+                            [] { consumers_sync(128); });
+      consumers_sync(128);  // xs is free for the next slice
+    } else if (failed) {
       flag_error(p.err, QX_ERR_BIT_TIMEOUT);
     } else if (q == 0) {
       const float v = o / L;
@@ -1003,74 +1094,9 @@ __global__ void __launch_bounds__(128) qx_split_merge_kernel(const __grid_consta
     merge_quad_pass(mv, lv, ov, pinned, M, L, o);
   }
   if (p.xworld) {
-    // KV-length split across GPUs: this CTA's slice of this rank's partial
-    // (32 dims of O, and m, l) goes tagged into every rank's inbox; then
-    // the slices of all ranks are merged in rank order (qx_lse_merge's
-    // arithmetic) straight into the output. The grid is one wave, so the
-    // peers' matching CTAs are running too.
-    constexpr int S = D / 32, ROW = 34;
-    const int slice = blk % S, dl = tid >> 2;
-    __shared__ float xml[16];  // m_r, l_r of up to 8 ranks
-    __shared__ int xok;
-    // an earlier exchange on this group timed out: push nothing (one thread
-    // reads the word, so the whole CTA takes one branch)
-    if (tid == 0) xok = peer_group_failed(p.xfailed) ? 0 : 1;
-    __syncthreads();
-    if (!xok) {
-      if (tid == 0) flag_error(p.err, QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER);
-      return;
-    }
-    const long long qh = (long long)h * G + g;
-    const int W = p.xworld;
-    unsigned* stp = p.xstep + qh * S + slice;
-    const unsigned st = *stp, tag = st + 1u, half = st & 1u;
-    const long long rows = (long long)HQ * S;
-    const long long mine = ((long long)half * W + p.xrank) * rows + qh * S + slice;
-    if (q == 0)
-      for (int r = 0; r < W; ++r) st_tagged(p.xinbox[r] + mine * ROW + dl, o, tag);
-    if (tid == 0)
-      for (int r = 0; r < W; ++r) {
-        st_tagged(p.xinbox[r] + mine * ROW + 32, M, tag);
-        st_tagged(p.xinbox[r] + mine * ROW + 33, L, tag);
-      }
-    const uint2* in = p.xinbox[p.xrank] + ((long long)half * W * rows + qh * S + slice) * ROW;
-    bool ok = true;
-    float ov[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r) ov[r] = 0.0f;
-    if (tid < 32) {
-      // dim tid of every rank's slice, and lanes 0 .. 2W-1 also (m, l) of
-      // rank tid / 2, all polled together
-      float v = 0.0f;
-      const uint2* ml = tid < 2 * W ? in + (tid >> 1) * rows * ROW + 32 + (tid & 1) : nullptr;
-      ok = wait_tagged_n<8>(in + tid, rows * ROW, W, ml, tag, ov, &v);
-      if (tid < 2 * W) xml[tid] = v;
-    }
-    if (!ok) {
-      flag_error(p.err, QX_ERR_BIT_TIMEOUT | QX_ERR_BIT_PEER);
-      mark_peer_group_failed(p.xfailed, p.xfailed_host);
-      xok = 0;
-    }
-    __syncthreads();
-    if (!xok) return;
-    if (tid < 32) {
-      float mx = -INFINITY;
-      for (int r = 0; r < W; ++r) mx = fmaxf(mx, xml[2 * r]);
-      float Lt = 0.0f, Ot = 0.0f;
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        if (r >= W) break;
-        const float m = xml[2 * r];
-        if (m == -INFINITY) continue;  // empty shard
-        const float w = softmax_exp(m - mx, pinned);
-        Lt = fmaf(w, xml[2 * r + 1], Lt);
-        Ot = fmaf(w, ov[r], Ot);
-      }
-      const float v = Ot / Lt;
-      if (!isfinite(v)) flag_error(p.err, QX_ERR_BIT_NONFINITE);
-      store_any(p.xout, (cu * HQ + qh) * D + slice * 32 + tid, p.xout_dtype, v);
-    }
-    if (tid == 0) *stp = st + 1u;
+    __shared__ float xml[17];  // m_r, l_r of up to 8 ranks; [16]: the CTA's go-ahead
+    exchange_slice<D, HQ>(p, cu, (long long)h * G + g, blk % (D / 32), o, M, L, true, tid, pinned, xml,
+                          [] { __syncthreads(); });
     return;
   }
   if (q == 0) {

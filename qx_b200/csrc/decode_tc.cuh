@@ -568,7 +568,7 @@ __global__ void __launch_bounds__(192, 1) qx_decode_tc_kernel(const __grid_const
       finish_outputs<G, TM::HEAD_D, HKV, HQ, 2>(p, O2, M2, L2, nsplit, s, cu, h, tid, warp, lane, pinned,
                                                 reinterpret_cast<float*>(sm + C::OFF_K), stat, s_flag);
     } else if (p.slice_merge && nsplit > 1) {
-      slice_merge<G, D, HQ>(p, O, Mg, Lg, nsplit, s, cu, h, tid, pinned);
+      slice_merge<G, D, HQ>(p, O, Mg, Lg, nsplit, s, cu, h, tid, pinned, reinterpret_cast<float*>(sm + C::OFF_K));
     } else {
       finish_outputs<G, D, HKV, HQ, G>(p, O, Mg, Lg, nsplit, s, cu, h, tid, warp, lane, pinned,
                                        reinterpret_cast<float*>(sm + C::OFF_K), stat, s_flag);

@@ -636,7 +636,9 @@ qxc_status fill_params(qxc_ctx* ctx, qxc_kv* kv, const CallPlan& plan, int layer
 // kv head), merges its splits inside the decode grid (slice_merge in
 // decode.cuh) instead of a second grid: the splits wait for one another,
 // which a one-wave grid allows, and the merge kernel's launch and its wait
-// for the decode grid's end drop out of the call.
+// for the decode grid's end drop out of the call. On a KV length split
+// across GPUs (qxc_decode_exchange) the merged slices then go through the
+// same exchange as in the merge kernel.
 qxc_status use_slice_merge(qxc_ctx* ctx, const qxc_kv* kv, const CallPlan& plan, DecodeParams* p) {
   if (kv->desc.model != QXC_MODEL_QWEN3) return QXC_OK;
   int max_split = 1;
@@ -2030,6 +2032,10 @@ static qxc_status decode_partials_impl(qxc_ctx* ctx, qxc_kv* kv, const qxc_parti
     p.xworld = g->world;
     p.xout = xout;
     p.xout_dtype = xout_dtype;
+    // a one-wave Qwen grid merges its splits and exchanges the result with
+    // the peers itself (exchange_slice), with no merge grid
+    st = use_slice_merge(ctx, kv, plan, &p);
+    if (st != QXC_OK) return st;
   }
   st = launch_decode(ctx, kv, p, plan.items);
   if (st != QXC_OK) return st;
