@@ -17,7 +17,10 @@ runs under torchrun: one independent sequence (replica) per GPU, no
 collective on the data path ("weak" scaling), device time max-reduced over
 ranks. The config-1 line also carries `sharded`: config 4 (256 sequences)
 sharded over the N ranks by LPT on KV bytes, with the one-GPU value of the
-same run and the efficiency against N times it. `--impl reference` times the CPU
+same run and the efficiency against N times it; at N>1 also `kv_split`:
+config 3's single 32768-position context with its KV length split over the
+ranks, the (m, l, O) partials crossing NVLink inside the decode grid, with
+the one-GPU value of the same run. `--impl reference` times the CPU
 restatement of qx's GQA path (oracle/, the reference being Rust and not
 buildable here) with all host threads on the same workload.
 """
@@ -653,9 +656,9 @@ def run_config3(args, world, rank, local):
                      {"workload": "config3: Qwen3 layer decode, 32 q / 4 kv heads, d=128, bf16 KV, length 32768",
                       "l2": f"calls rotate over {NSET} cache copies ({NSET * per_rank_bytes / 2**20:.0f} MB > 126 MB L2)",
                       "parallelism": "single GPU" if world == 1 else
-                      {"peer": f"KV length split x{world}; the split merge kernel pushes each rank's (m,l,O) "
-                               "partials to every rank with tagged NVLink peer stores and merges them "
-                               "(qxc_decode_exchange)",
+                      {"peer": f"KV length split x{world}; the decode grid merges its splits and pushes each "
+                               "rank's (m,l,O) slices to every rank with tagged NVLink peer stores, then merges "
+                               "the ranks' slices (qxc_decode_exchange)",
                        "kernel": f"KV length split x{world}; (m,l,O) partials exchanged with NVLink peer stores "
                                  "and merged by a separate kernel (qxc_exchange_merge)",
                        "nccl": f"KV length split x{world}, NCCL all-gather of (m,l,O) partials + LSE merge"}
@@ -663,9 +666,12 @@ def run_config3(args, world, rank, local):
                       "timing": f"{R} steps per CUDA graph replay"},
                      clk, launches)
     line["config"]["split"] = ctx.last_split
-    line["roofline"] = hbm_roofline(B if world == 1 else per_rank_bytes, per,
-                                    "qx_decode_tc_kernel<bf16,TcQwen> (splits merged inside the grid)" if world == 1
-                                    else "qx_decode_tc_kernel<bf16,TcQwen> + qx_split_merge_kernel (timed together)",
+    kernel = ("qx_decode_tc_kernel<bf16,TcQwen> (splits merged inside the grid)" if world == 1 else
+              {"peer": "qx_decode_tc_kernel<bf16,TcQwen> (splits merged and exchanged over NVLink inside the grid)",
+               "kernel": "qx_decode_tc_kernel<bf16,TcQwen> + qx_exchange_merge_kernel (timed together)",
+               "nccl": "qx_decode_tc_kernel<bf16,TcQwen> + NCCL all-gather + qx_lse_merge_kernel (timed together)"}
+              [args.exchange])
+    line["roofline"] = hbm_roofline(B if world == 1 else per_rank_bytes, per, kernel,
                                     "config3" if world == 1 else None)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -1111,6 +1117,37 @@ def sharded_config4(args, world, rank, local):
             "gpu_launches": r["launches"]}
 
 
+def kv_split_config3(args, world, rank, local):
+    """The path with a collective (config 3), measured beside the config-1
+    headline at N > 1: one Qwen3 context of 32768 positions with its KV
+    length split over the N ranks, each step's (m, l, O) partials crossing
+    NVLink inside the decode grid (qxc_decode_exchange). Rank 0 first times
+    the whole context alone on its GPU (the other ranks wait), so the object
+    carries the one-GPU value of the same run and the speed-up."""
+    import copy
+    a = copy.copy(args)
+    a.no_cpu_baseline = True
+    a.split = 0
+    a.exchange = "peer"
+    # a step is ~15 us: time at least 1000 (20 graph replays), whatever the
+    # headline's step count
+    a.steps = max(args.steps, 1000)
+    a.warmup = max(args.warmup, 100)
+    one = None
+    barrier(world)
+    if rank == 0:
+        one = run_config3(a, 1, 0, local)["value"]
+    barrier(world)
+    line = run_config3(a, world, rank, local)
+    return {"workload": f"config3: Qwen3 layer decode, 32 q / 4 kv heads, d=128, bf16 KV, length "
+                        f"{args.qwen_context}, KV length split x{world}",
+            "metric": line["metric"], "value": line["value"], "unit": line["unit"], "n_gpus": world,
+            "steps": line["steps"], "ms_per_step": line["ms_per_step"], "scaling": "strong",
+            "one_gpu_value": one, "speedup": line["value"] / one if one else None,
+            "parallelism": line["config"]["parallelism"], "split": line["config"]["split"],
+            "rank0_hbm_frac": line["roofline"]["frac"], "gpu_launches": line.get("gpu_launches")}
+
+
 # ---------------------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------------------
@@ -1188,6 +1225,8 @@ def main():
                     help="layer workload: qxc_attention_layer per layer (graph-captured) instead of qxc_attention_stack")
     ap.add_argument("--no-sharded", action="store_true",
                     help="config1: leave out the `sharded` object (config 4 sharded over the ranks)")
+    ap.add_argument("--no-kv-split", action="store_true",
+                    help="config1 at N>1: leave out the `kv_split` object (config 3's KV length split over the ranks)")
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--split", type=int, default=0)
     ap.add_argument("--paged", type=int, default=0, help="config4: paged KV arena with this many rows per page")
@@ -1243,6 +1282,11 @@ def main():
         line = run(args, world, rank, local)
         if args.workload == "config1" and not args.no_sharded:
             line["sharded"] = sharded_config4(args, world, rank, local)
+        if args.workload == "config1" and world > 1 and not args.no_kv_split:
+            try:
+                line["kv_split"] = kv_split_config3(args, world, rank, local)
+            except Exception as exc:  # the headline and `sharded` still print
+                line["kv_split"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

@@ -2006,7 +2006,22 @@ static qxc_status decode_partials_impl(qxc_ctx* ctx, qxc_kv* kv, const qxc_parti
   const int seq = a->seq, rope = a->position;
   st = ensure_pages(ctx, kv, 1, &seq, &attend);
   if (st != QXC_OK) return st;
-  st = plan_call(ctx, kv, 1, &seq, &attend, &new_slot, &rope, 1, a->split, &plan);
+  // With a peer group a one-wave Qwen grid merges and exchanges inside the
+  // decode grid, one NVLink round trip per 32-dim output slice a split
+  // takes (exchange_slice). The automatic split then gives every kv head at
+  // least one split per slice (32: 8 query heads x 4 slices) while the grid
+  // stays one wave: with fewer, some splits take two slices one after the
+  // other and the step pays the round trip twice (config 3 at N = 4: 22
+  // splits of 384 rows, 21.4 us per step).
+  int split = a->split;
+  if (g && split == 0 && kv->desc.model == QXC_MODEL_QWEN3) {
+    const int unit = split_unit(kv), slices = kv->hq / kv->hkv * (kv->d / 32);
+    const int chunk = std::max(unit, attend / slices / unit * unit);
+    const int nsplit = (attend + chunk - 1) / chunk;
+    if (nsplit >= slices && nsplit <= 4 * kMergeLoads && nsplit * kv->hkv <= decode_blocks_per_sm(kv) * ctx->sm_count)
+      split = chunk;
+  }
+  st = plan_call(ctx, kv, 1, &seq, &attend, &new_slot, &rope, 1, split, &plan);
   if (st != QXC_OK) return st;
   DecodeParams p;
   st = fill_params(ctx, kv, plan, a->layer, 1, &p);
